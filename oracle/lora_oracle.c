@@ -1,0 +1,424 @@
+/*
+ * lora_oracle.c — CPU restatement of smollm2.c's LoRA-on-lm_head training
+ * step, used ONLY as test infrastructure (the parity checker for the CUDA
+ * path, and the timed CPU baseline in bench.py).  Nothing in the product
+ * library links or calls this file.
+ *
+ * Every function follows one reference function, op for op, so that with
+ * one thread the results are bit-identical to the reference built from its
+ * own sources (checked by tests/test_oracle.py against oracle/_ref and the
+ * committed fixtures in tests/golden/):
+ *
+ *   oracle_base_logits   src/forward.c:396-403   (x86 matmul_f32: fp64 acc.)
+ *   f16 -> f32           src/forward.c:256-286   (f16_to_f32, exact)
+ *   per-token step       src/train.c:124-173     (matmul_hA, matmul_midB,
+ *                                                 lora_accum)
+ *   softmax-CE           src/train.c:107-121     (ce_loss_and_grad)
+ *   mean over n_pred     src/train.c:230-237
+ *   Adam                 src/train.c:175-196     (adam_update)
+ *   target indexing      src/train.c:198-229     (targets = tokens[pos+1])
+ *   Kaiming A init       src/train.c:83-93       (glibc rand, Box-Muller)
+ *   softmax-CE gradcheck src/backward.c:450-503  (grad_check_softmax_ce)
+ *   merge                src/train.c:393-460     (lora_patched_weight)
+ *
+ * Extensions that the reference does not have (weight decay, grad-clip) are
+ * applied after the mean exactly where an AdamW implementation applies
+ * them; with wd = 0 and clip = 0 they are no-ops, so the reference path is
+ * unchanged.  Their "on" settings are parity-unpinned by the reference.
+ *
+ * Build: gcc -std=c99 -O2 -ffp-contract=off (no -march=native, no fast-math:
+ * the reference's own -std=c99 build does not contract a*b+c either).
+ * With nthreads > 1 the per-token gradient sums are accumulated per
+ * contiguous token block and the blocks are added in block order: the
+ * result is deterministic but no longer bit-identical to the reference's
+ * single running sum (it differs by fp32 re-association only).
+ */
+#define _GNU_SOURCE
+#include <math.h>
+#include <pthread.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define ORACLE_B1 0.9f
+#define ORACLE_B2 0.999f
+#define ORACLE_EPS 1e-8f
+#define ORACLE_MAX_RANK 256
+
+/* f16 bits -> f32, exact (src/forward.c:256-286). */
+float oracle_f16_to_f32(uint16_t h) {
+    uint32_t sign = ((uint32_t)(h & 0x8000u)) << 16;
+    int exp = (h >> 10) & 0x1f;
+    int mant = h & 0x3ff;
+    float f;
+    uint32_t u;
+    if (exp == 0) {
+        if (mant == 0) { u = sign; memcpy(&f, &u, 4); return f; }
+        f = ldexpf((float)mant, -24);
+        return sign ? -f : f;
+    }
+    if (exp == 0x1f) {
+        u = sign | 0x7f800000u | ((uint32_t)mant << 13);
+        memcpy(&f, &u, 4);
+        return f;
+    }
+    u = sign | ((uint32_t)(exp + 127 - 15) << 23) | ((uint32_t)mant << 13);
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+/* Base logits of one position: fp64 accumulation over the hidden dim, then
+ * rounded to f32 (src/forward.c:396-403, the x86 branch of matmul_f32 that
+ * the reference uses for the tied lm_head).  Wf is W converted to f32
+ * (exact).  Eight rows are interleaved so the eight running sums pipeline;
+ * each row is still summed in index order, so every logit is bit-identical
+ * to the reference's one-row loop (the f16 x f32 products are exact in
+ * fp64). */
+static void base_logits_f32w(const float* Wf, const float* h, int d, int V,
+                             float* out) {
+    int o = 0;
+    for (; o + 8 <= V; o += 8) {
+        const float* w = Wf + (size_t)o * d;
+        double a0 = 0, a1 = 0, a2 = 0, a3 = 0, a4 = 0, a5 = 0, a6 = 0, a7 = 0;
+        for (int i = 0; i < d; i++) {
+            double x = (double)h[i];
+            a0 += (double)w[i] * x;
+            a1 += (double)w[(size_t)d + i] * x;
+            a2 += (double)w[(size_t)2 * d + i] * x;
+            a3 += (double)w[(size_t)3 * d + i] * x;
+            a4 += (double)w[(size_t)4 * d + i] * x;
+            a5 += (double)w[(size_t)5 * d + i] * x;
+            a6 += (double)w[(size_t)6 * d + i] * x;
+            a7 += (double)w[(size_t)7 * d + i] * x;
+        }
+        out[o] = (float)a0; out[o + 1] = (float)a1; out[o + 2] = (float)a2;
+        out[o + 3] = (float)a3; out[o + 4] = (float)a4; out[o + 5] = (float)a5;
+        out[o + 6] = (float)a6; out[o + 7] = (float)a7;
+    }
+    for (; o < V; o++) {
+        const float* w = Wf + (size_t)o * d;
+        double acc = 0.0;
+        for (int i = 0; i < d; i++) acc += (double)w[i] * (double)h[i];
+        out[o] = (float)acc;
+    }
+}
+
+static float* convert_weight(const uint16_t* W, int d, int V) {
+    float* Wf = (float*)malloc((size_t)V * d * sizeof(float));
+    if (!Wf) return NULL;
+    for (size_t i = 0; i < (size_t)V * d; i++) Wf[i] = oracle_f16_to_f32(W[i]);
+    return Wf;
+}
+
+void oracle_base_logits(const uint16_t* W, const float* h, int d, int V,
+                        float* out) {
+    float* Wf = convert_weight(W, d, V);
+    if (!Wf) return;
+    base_logits_f32w(Wf, h, d, V, out);
+    free(Wf);
+}
+
+/* Softmax-CE on one row, in place: logits -> p - onehot; returns the loss
+ * (src/train.c:107-121). */
+static float ce_row(float* logits, int V, int target, float* dl) {
+    float mx = logits[0];
+    for (int i = 1; i < V; i++) if (logits[i] > mx) mx = logits[i];
+    float sum = 0.0f;
+    for (int i = 0; i < V; i++) {
+        dl[i] = expf(logits[i] - mx);
+        sum += dl[i];
+    }
+    float inv = 1.0f / sum;
+    for (int i = 0; i < V; i++) dl[i] *= inv;
+    float loss = -logf(dl[target] + 1e-12f);
+    dl[target] -= 1.0f;
+    return loss;
+}
+
+typedef struct {
+    int d, V, r;
+    float scale;
+    const float* Wf;    /* [V][d] f32 copy of the f16 weight */
+    const float* A;     /* [d][r] */
+    const float* B;     /* [r][V] */
+    const float* H;     /* [T][d] */
+    const int32_t* tgt; /* [T]    */
+    int t0, t1;         /* token block [t0, t1) */
+    float* gA;          /* [d][r] partial (zeroed by caller) */
+    float* gB;          /* [r][V] partial (zeroed by caller) */
+    float* loss;        /* per-token loss [T] */
+    int status;
+} block_job;
+
+/* lora_accum (src/train.c:144-173) for the tokens of one block, with the
+ * base logits of each position computed as in oracle_base_logits. */
+static void* run_block(void* arg) {
+    block_job* j = (block_job*)arg;
+    const int d = j->d, V = j->V, R = j->r;
+    float* logits = (float*)malloc((size_t)V * sizeof(float));
+    float* delta = (float*)malloc((size_t)V * sizeof(float));
+    float mid[ORACLE_MAX_RANK], d_mid[ORACLE_MAX_RANK];
+    if (!logits || !delta) { j->status = -1; free(logits); free(delta); return NULL; }
+    for (int t = j->t0; t < j->t1; t++) {
+        const float* h = j->H + (size_t)t * d;
+        base_logits_f32w(j->Wf, h, d, V, logits);
+        /* matmul_hA */
+        for (int r = 0; r < R; r++) {
+            float s = 0;
+            for (int i = 0; i < d; i++) s += h[i] * j->A[i * R + r];
+            mid[r] = s;
+        }
+        /* matmul_midB */
+        for (int v = 0; v < V; v++) {
+            float s = 0;
+            for (int r = 0; r < R; r++) s += mid[r] * j->B[r * V + v];
+            delta[v] = s;
+        }
+        for (int v = 0; v < V; v++) logits[v] += j->scale * delta[v];
+        float* dl = delta; /* reuse, as the reference does */
+        j->loss[t] = ce_row(logits, V, j->tgt[t], dl);
+        for (int r = 0; r < R; r++) {
+            float s = 0;
+            for (int v = 0; v < V; v++) {
+                j->gB[r * V + v] += j->scale * mid[r] * dl[v];
+                s += j->B[r * V + v] * dl[v];
+            }
+            d_mid[r] = j->scale * s;
+        }
+        for (int i = 0; i < d; i++)
+            for (int r = 0; r < R; r++)
+                j->gA[i * R + r] += h[i] * d_mid[r];
+    }
+    free(logits);
+    free(delta);
+    j->status = 0;
+    return NULL;
+}
+
+/*
+ * Gradient of one step: accumulated gA/gB over T positions (not yet
+ * divided by n_pred) and the per-position loss.  targets[t] is the id the
+ * position predicts.  Returns 0, or -1 on bad arguments (rank above the
+ * reference's LORA_MAX_RANK, target out of range).
+ */
+int oracle_accumulate(int d, int V, int r, float scale, const uint16_t* W,
+                      const float* A, const float* B, const float* H,
+                      const int32_t* targets, int T, int nthreads,
+                      float* gA_sum, float* gB_sum, float* loss_tok) {
+    if (r < 1 || r > ORACLE_MAX_RANK || T < 1 || d < 1 || V < 1) return -1;
+    for (int t = 0; t < T; t++)
+        if (targets[t] < 0 || targets[t] >= V) return -1;
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > T) nthreads = T;
+    size_t a_sz = (size_t)d * r, b_sz = (size_t)r * V;
+    memset(gA_sum, 0, a_sz * sizeof(float));
+    memset(gB_sum, 0, b_sz * sizeof(float));
+    block_job* jobs = (block_job*)calloc((size_t)nthreads, sizeof(block_job));
+    pthread_t* th = (pthread_t*)calloc((size_t)nthreads, sizeof(pthread_t));
+    if (!jobs || !th) { free(jobs); free(th); return -1; }
+    float* Wf = convert_weight(W, d, V);
+    int rc = Wf ? 0 : -1;
+    for (int k = 0; k < nthreads; k++) {
+        block_job* j = &jobs[k];
+        j->d = d; j->V = V; j->r = r; j->scale = scale;
+        j->Wf = Wf; j->A = A; j->B = B; j->H = H; j->tgt = targets;
+        j->t0 = (int)((long long)T * k / nthreads);
+        j->t1 = (int)((long long)T * (k + 1) / nthreads);
+        j->loss = loss_tok;
+        if (k == 0) { j->gA = gA_sum; j->gB = gB_sum; }
+        else {
+            j->gA = (float*)calloc(a_sz, sizeof(float));
+            j->gB = (float*)calloc(b_sz, sizeof(float));
+            if (!j->gA || !j->gB) rc = -1;
+        }
+    }
+    if (rc == 0) {
+        if (nthreads == 1) run_block(&jobs[0]);
+        else {
+            for (int k = 0; k < nthreads; k++) pthread_create(&th[k], NULL, run_block, &jobs[k]);
+            for (int k = 0; k < nthreads; k++) pthread_join(th[k], NULL);
+        }
+        for (int k = 0; k < nthreads; k++) if (jobs[k].status != 0) rc = -1;
+        for (int k = 1; k < nthreads && rc == 0; k++) {
+            for (size_t i = 0; i < a_sz; i++) gA_sum[i] += jobs[k].gA[i];
+            for (size_t i = 0; i < b_sz; i++) gB_sum[i] += jobs[k].gB[i];
+        }
+    }
+    for (int k = 1; k < nthreads; k++) { free(jobs[k].gA); free(jobs[k].gB); }
+    free(Wf);
+    free(jobs);
+    free(th);
+    return rc;
+}
+
+/*
+ * Optimizer part of train_step: g *= 1/n_pred (src/train.c:233-237), then
+ * the extensions (global-norm clip, decoupled weight decay; no-ops at 0),
+ * then adam_update (src/train.c:175-196).  *step is the Adam step counter
+ * (incremented here, as the reference does).  gA/gB are overwritten with
+ * the mean gradient actually applied.
+ */
+void oracle_adam(int d, int V, int r, float lr, float wd, float clip,
+                 int n_pred, int* step, float* A, float* B, float* gA,
+                 float* gB, float* mA, float* vA, float* mB, float* vB) {
+    size_t a_sz = (size_t)d * r, b_sz = (size_t)r * V;
+    float inv = 1.0f / (float)n_pred;
+    for (size_t i = 0; i < a_sz; i++) gA[i] *= inv;
+    for (size_t i = 0; i < b_sz; i++) gB[i] *= inv;
+    if (clip > 0.0f) {
+        double ss = 0.0;
+        for (size_t i = 0; i < a_sz; i++) ss += (double)gA[i] * gA[i];
+        for (size_t i = 0; i < b_sz; i++) ss += (double)gB[i] * gB[i];
+        float norm = (float)sqrt(ss);
+        float c = clip / (norm + 1e-6f);
+        if (c < 1.0f) {
+            for (size_t i = 0; i < a_sz; i++) gA[i] *= c;
+            for (size_t i = 0; i < b_sz; i++) gB[i] *= c;
+        }
+    }
+    (*step)++;
+    float b1t = 1.0f - powf(ORACLE_B1, (float)*step);
+    float b2t = 1.0f - powf(ORACLE_B2, (float)*step);
+    for (size_t i = 0; i < a_sz; i++) {
+        if (wd > 0.0f) A[i] -= lr * wd * A[i];
+        mA[i] = ORACLE_B1 * mA[i] + (1 - ORACLE_B1) * gA[i];
+        vA[i] = ORACLE_B2 * vA[i] + (1 - ORACLE_B2) * gA[i] * gA[i];
+        float mhat = mA[i] / b1t;
+        float vhat = vA[i] / b2t;
+        A[i] -= lr * mhat / (sqrtf(vhat) + ORACLE_EPS);
+    }
+    for (size_t i = 0; i < b_sz; i++) {
+        if (wd > 0.0f) B[i] -= lr * wd * B[i];
+        mB[i] = ORACLE_B1 * mB[i] + (1 - ORACLE_B1) * gB[i];
+        vB[i] = ORACLE_B2 * vB[i] + (1 - ORACLE_B2) * gB[i] * gB[i];
+        float mhat = mB[i] / b1t;
+        float vhat = vB[i] / b2t;
+        B[i] -= lr * mhat / (sqrtf(vhat) + ORACLE_EPS);
+    }
+}
+
+/*
+ * Full step over one packed sample, as train_step does it
+ * (src/train.c:198-242): use_n = min(n_tokens, seq_max); positions
+ * 0..use_n-2 predict tokens[pos+1]; H holds the hidden state of each
+ * position (row pos).  Returns the mean loss, or -1.0f on error.
+ * gA/gB receive the mean gradient that was applied.
+ */
+float oracle_train_step(int d, int V, int r, float scale, float lr, float wd,
+                        float clip, int seq_max, const uint16_t* W,
+                        const float* H, const int32_t* tokens, int n_tokens,
+                        int nthreads, int* step, float* A, float* B,
+                        float* gA, float* gB, float* mA, float* vA,
+                        float* mB, float* vB) {
+    if (!tokens || n_tokens < 2) return -1.0f;
+    int use_n = n_tokens;
+    if (use_n > seq_max) use_n = seq_max;
+    if (use_n < 2) return -1.0f;
+    int n_pred = use_n - 1;
+    float* loss = (float*)malloc((size_t)n_pred * sizeof(float));
+    if (!loss) return -1.0f;
+    if (oracle_accumulate(d, V, r, scale, W, A, B, H, tokens + 1, n_pred,
+                          nthreads, gA, gB, loss) != 0) {
+        free(loss);
+        return -1.0f;
+    }
+    float total = 0.0f;
+    for (int t = 0; t < n_pred; t++) total += loss[t];
+    free(loss);
+    oracle_adam(d, V, r, lr, wd, clip, n_pred, step, A, B, gA, gB, mA, vA, mB, vB);
+    float inv = 1.0f / (float)n_pred;
+    return total * inv;
+}
+
+/* Kaiming init of A via Box-Muller on glibc rand() (src/train.c:83-93);
+ * B starts at zero. */
+void oracle_kaiming_init(int seed, int d, int r, float* A) {
+    srand((unsigned)(seed ? seed : 42));
+    float std_a = sqrtf(2.0f / (float)d);
+    size_t a_sz = (size_t)d * r;
+    for (size_t i = 0; i < a_sz; i++) {
+        float u1 = ((float)rand() + 1.0f) / ((float)RAND_MAX + 1.0f);
+        float u2 = ((float)rand() + 1.0f) / ((float)RAND_MAX + 1.0f);
+        float z = sqrtf(-2.0f * logf(u1)) * cosf(6.28318530718f * u2);
+        A[i] = z * std_a;
+    }
+}
+
+/* Softmax-CE finite-difference check (src/backward.c:450-503): vocab-sized
+ * logits from srand(42) / randf()*0.5, target vocab/2; returns the max abs
+ * difference between p - onehot and the centred fp64 difference. */
+static float gc_randf(void) { return ((float)rand() / 2147483647.0f) - 0.5f; }
+
+static double ce_fwd_d(const float* logits, int vocab, int target) {
+    double mx = logits[0];
+    for (int i = 1; i < vocab; i++) if (logits[i] > mx) mx = logits[i];
+    double sum = 0;
+    for (int i = 0; i < vocab; i++) sum += exp((double)logits[i] - mx);
+    double pt = exp((double)logits[target] - mx) / sum;
+    return -log(pt + 1e-20);
+}
+
+float oracle_grad_check_softmax_ce(int vocab, float eps) {
+    srand(42u);
+    float* logits = (float*)malloc((size_t)vocab * sizeof(float));
+    float* probs = (float*)malloc((size_t)vocab * sizeof(float));
+    float* g_num = (float*)malloc((size_t)vocab * sizeof(float));
+    if (!logits || !probs || !g_num) { free(logits); free(probs); free(g_num); return -1.0f; }
+    for (int i = 0; i < vocab; i++) logits[i] = gc_randf() * 0.5f;
+    int target = vocab / 2;
+    float mx = logits[0];
+    for (int i = 1; i < vocab; i++) if (logits[i] > mx) mx = logits[i];
+    float sum = 0;
+    for (int i = 0; i < vocab; i++) { probs[i] = expf(logits[i] - mx); sum += probs[i]; }
+    float inv = 1.0f / sum;
+    for (int i = 0; i < vocab; i++) probs[i] *= inv;
+    probs[target] -= 1.0f; /* analytic p - onehot */
+    for (int i = 0; i < vocab; i++) {
+        float o = logits[i];
+        logits[i] = o + eps; double lp = ce_fwd_d(logits, vocab, target);
+        logits[i] = o - eps; double lm = ce_fwd_d(logits, vocab, target);
+        logits[i] = o;
+        g_num[i] = (float)((lp - lm) / (2.0 * eps));
+    }
+    float err = 0.0f;
+    for (int i = 0; i < vocab; i++) {
+        float e = fabsf(probs[i] - g_num[i]);
+        if (e > err) err = e;
+    }
+    free(logits); free(probs); free(g_num);
+    return err;
+}
+
+/* Truncating f32 -> f16 of the merge path (src/train.c:393-409). */
+uint16_t oracle_merge_f32_to_f16(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    uint32_t sign = (x & 0x80000000u) >> 16;
+    uint32_t em = x & 0x7fffffffu;
+    if (em >= 0x47800000u) {
+        if (em > 0x7f800000u) return (uint16_t)(sign | 0x7e00);
+        return (uint16_t)(sign | 0x7c00);
+    }
+    if (em < 0x38800000u) {
+        if (em < 0x33000000u) return (uint16_t)sign;
+        uint32_t sh = 113 - (em >> 23);
+        uint32_t mant = (em & 0x7fffff) | 0x800000;
+        return (uint16_t)(sign | (mant >> sh));
+    }
+    return (uint16_t)(sign | ((em + 0xc800000) >> 13));
+}
+
+/* W' = f16trunc(f32(W) + scale * (A.B)^T), row v, col i (src/train.c:415-460). */
+void oracle_merge(const uint16_t* W, const float* A, const float* B, int d,
+                  int r, int V, float scale, uint16_t* out) {
+    for (int v = 0; v < V; v++) {
+        for (int i = 0; i < d; i++) {
+            const float* arow = A + (size_t)i * r;
+            float s = 0.0f;
+            for (int k = 0; k < r; k++) s += arow[k] * B[(size_t)k * V + v];
+            float delta = scale * s;
+            float base = oracle_f16_to_f32(W[(size_t)v * d + i]);
+            out[(size_t)v * d + i] = oracle_merge_f32_to_f16(base + delta);
+        }
+    }
+}

@@ -1,0 +1,63 @@
+"""Seeded synthetic inputs with the shapes and value distributions of the
+LoRA-on-lm_head workloads (the real SmolLM2 GGUF and datasets are not
+available, so every run draws its inputs from a seed).
+
+Distributions (N(mean, std) throughout):
+  W  [V][d]  f16   N(0, 0.02)              tied token_embd / lm_head
+  h  [T][d]  bf16  N(0, 1)                 post-final-RMSNorm hidden states
+  A  [d][r]  fp32  N(0, 1/sqrt(d))         i.e. variance 1/d (unit-variance h.A)
+  B  [r][V]  fp32  N(0, 1e-3)
+  targets    int32 bounded Zipf(s=1.1) over ids 0..V-1 (p(k) ~ k^-1.1,
+                   id = k-1), inverse-CDF sampling.
+A and B are returned in the reference layouts (A[d*r + j], B[j*V + v],
+src/train.c:35-36).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even fp32 -> bf16 bit patterns (uint16)."""
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32)
+    rounding = ((u >> 16) & 1) + 0x7FFF
+    return ((u + rounding) >> 16).astype(np.uint16)
+
+
+def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return (np.ascontiguousarray(b, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f16_exact(h_f32: np.ndarray) -> np.ndarray:
+    """The f32 values the tensor cores see after an RN conversion to f16."""
+    return np.asarray(h_f32, np.float32).astype(np.float16).astype(np.float32)
+
+
+def zipf_targets(rng: np.random.Generator, n: int, V: int, s: float = 1.1) -> np.ndarray:
+    k = np.arange(1, V + 1, dtype=np.float64)
+    cdf = np.cumsum(k ** (-s))
+    cdf /= cdf[-1]
+    u = rng.random(n)
+    return np.minimum(np.searchsorted(cdf, u, side="right"), V - 1).astype(np.int32)
+
+
+def make_weight(seed: int, V: int, d: int) -> np.ndarray:
+    """W [V][d] as f16 bit patterns (uint16)."""
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal((V, d), dtype=np.float32) * np.float32(0.02)).astype(np.float16)
+    return w.view(np.uint16)
+
+
+def make_step_inputs(seed: int, T: int, V: int, d: int, r: int):
+    """h (bf16 bits), targets, A [d][r], B [r][V] for one step."""
+    rng = np.random.default_rng(seed + 1)
+    h = f32_to_bf16_bits(rng.standard_normal((T, d), dtype=np.float32))
+    A = (rng.standard_normal((r, d), dtype=np.float32) * np.float32(1.0 / np.sqrt(d))).T.copy()
+    B = (rng.standard_normal((V, r), dtype=np.float32) * np.float32(1e-3)).T.copy()
+    tgt = zipf_targets(rng, T, V)
+    return h, tgt, A, B
+
+
+def oracle_hidden(h_bf16: np.ndarray) -> np.ndarray:
+    """Hidden rows as the kernels consume them (bf16 -> f16 RN), in f32."""
+    return f16_exact(bf16_bits_to_f32(h_bf16))
