@@ -1,0 +1,388 @@
+"""Benchmark of the fused LoRA-on-lm_head CE fwd+bwd+AdamW step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload per GPU (weak scaling): the isolated fused op, h [8192 x 576] bf16,
+W [49152 x 576] f16, LoRA rank 4 (alpha 8), Zipf(1.1) targets, one
+fwd + bwd + AdamW (lr 1e-3, wd 0.01) step per iteration; for N > 1 every
+rank takes its own 8192 positions and the dA/dB gradients are summed by one
+NCCL all-reduce inside the step.  Inputs are seeded synthetic data.  The
+working set (W 56.6 MB + h 9.4 MB) fits in L2, so L2 is flushed (a 256 MB
+write) before every timed step; each step is timed alone with CUDA events
+on the library's stream.
+
+Prints one JSON line (rank 0).  `value` is the device-resident step
+throughput (tokens/s over all ranks); `e2e` is the same step through the
+public C ABI call with pinned host buffers (h and targets copied in, loss
+read back, all inside the timed region).  `roofline` describes the
+dominant kernel, `cpu_baseline` the reference CPU path timed on this
+host's cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import multiprocessing as mp
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "smollm2.c_b200"))
+sys.path.insert(0, os.path.join(REPO, "oracle"))
+
+V, D, R, ALPHA = 49152, 576, 4, 8
+T_PER_GPU = 8192
+LR, WD = 1e-3, 0.01
+METRIC = "LoRA lm_head CE fwd+bwd tokens/s"
+UNIT = "tokens/s"
+# FLOPs per predicted token of the whole step (two GEMM passes with the
+# rank-r terms, dA): 4*V*d + 8*V*r + 4*d*r.
+F_TOK = 4 * V * D + 8 * V * R + 4 * D * R
+# FLOPs per token of one GEMM pass kernel: 2*V*d (tensor) + 4*V*r (rank terms).
+F_PASS = 2 * V * D + 4 * V * R
+
+
+def env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["bf16_tflops"]), float(j["hbm_gbs"]), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed
+    region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out = ""
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rows.append((float(f[1]), float(f[2]), float(f[3]), f[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[3]) if v.lower() == "active"})
+        loaded = [r[0] for r in rows if r[2] > 200.0] or [r[0] for r in rows]
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ----------------------------------------------------------------- CPU leg
+def _ref_worker_init(lib_path):
+    global _REF
+    import oracle as orc
+    _REF = orc.RefHarness()
+
+
+def _ref_worker(args):
+    """The reference's train_step (oracle/_ref) on one shard of positions;
+    returns its own wall time."""
+    import numpy as np
+    import workload as wl
+    seed, T = args
+    W = wl.make_weight(1, V, D)
+    h, tgt, A, B = wl.make_step_inputs(seed, T, V, D, R)
+    H = wl.oracle_hidden(h)
+    tokens = np.concatenate([[1], tgt]).astype(np.int32)
+    t0 = time.perf_counter()
+    _REF.train_steps(W, H, tokens, R, ALPHA, LR, 1 << 30, n_steps=1, A_dr=A, B_rv=B)
+    return time.perf_counter() - t0
+
+
+def _oracle_worker(args):
+    import numpy as np
+    import oracle as orc
+    import workload as wl
+    seed, T, threads = args
+    W = wl.make_weight(1, V, D)
+    h, tgt, A, B = wl.make_step_inputs(seed, T, V, D, R)
+    H = wl.oracle_hidden(h)
+    o = orc.Oracle()
+    t0 = time.perf_counter()
+    o.step(W, A, B, H, tgt, ALPHA / R, LR, wd=WD, nthreads=threads)
+    return time.perf_counter() - t0
+
+
+class CpuReference:
+    """Tokens/s of the reference CPU path on this host: the reference's own
+    train.c (oracle/_ref, single-threaded by design) run as one process per
+    core, each on its own shard of positions (the data-parallel split the
+    GPU path uses); the oracle port on all cores when oracle/_ref is absent.
+    The pool is spawned (never forked) and started before any GPU work."""
+
+    def __init__(self):
+        import oracle as orc
+        self.cores = os.cpu_count() or 1
+        self.kind = "reference" if orc.ref_available() else "port"
+        self.procs = min(self.cores, 128) if self.kind == "reference" else 1
+        ctx = mp.get_context("spawn")
+        if self.kind == "reference":
+            self.pool = ctx.Pool(self.procs, initializer=_ref_worker_init, initargs=(None,))
+            t_cal = max(self.pool.map(_ref_worker, [(100 + i, 2) for i in range(self.procs)]))
+            self.per_tok = max(t_cal / 2, 1e-3)
+        else:
+            self.pool = ctx.Pool(1)
+            self.per_tok = 0.05 / self.cores
+
+    def sample(self, target_seconds: float):
+        if self.kind == "reference":
+            n_tok = max(2, int(target_seconds / self.per_tok))
+            # the slowest worker's own train_step time (input generation excluded)
+            wall = max(self.pool.map(_ref_worker, [(200 + i, n_tok) for i in range(self.procs)]))
+            total, used = n_tok * self.procs, self.procs
+            sample = (f"{self.procs} processes x {n_tok} positions of the isolated-op shape "
+                      f"(V {V}, d {D}, r {R}); the reference train_step in each")
+        else:
+            n_tok = max(self.cores, int(target_seconds / self.per_tok))
+            wall = max(self.pool.map(_oracle_worker, [(300, n_tok, self.cores)]))
+            total, used = n_tok, self.cores
+            sample = f"{n_tok} positions on {self.cores} threads (oracle port)"
+        return {"value": total / wall, "unit": UNIT, "cores": used, "kind": self.kind,
+                "sample": sample}
+
+    def close(self):
+        self.pool.close()
+        self.pool.join()
+
+
+def run_reference_arm(args):
+    rank = env_int("RANK", 0)
+    world = env_int("WORLD_SIZE", 1)
+    if rank != 0:
+        return
+    ref = CpuReference()
+    per_step = max(2.0, min(8.0, 150.0 / max(1, args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        ref.sample(per_step / 2)
+    steps = [ref.sample(per_step) for _ in range(args.steps)]
+    ref.close()
+    value = statistics.mean(s["value"] for s in steps)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * T_PER_GPU * world / value,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; bf16 h, f16 W, Zipf(1.1) targets)",
+        "config": {"workload": "isolated fused LoRA lm_head CE fwd+bwd+Adam: h [8192x576] per "
+                               "GPU, W [49152x576] f16, r 4, alpha 8; each step a sample of "
+                               "positions", "T_per_gpu": T_PER_GPU, "parallelism": f"dp{world}"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": steps[0]["cores"],
+                         "kind": steps[0]["kind"], "sample": steps[0]["sample"]},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------- GPU leg
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference_arm(args)
+        return
+    args.warmup = max(args.warmup, 3)
+
+    import numpy as np
+    import torch
+    import lora_ce
+    import workload as wl
+
+    rank = env_int("RANK", 0)
+    world = env_int("WORLD_SIZE", 1)
+    local = env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group(backend="cpu:gloo,cuda:nccl",
+                                timeout=datetime.timedelta(seconds=300))
+
+    # CPU baseline first (spawned pool, before any GPU work in this process)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        ref = CpuReference()
+        cpu = ref.sample(15.0)
+        ref.close()
+
+    T = T_PER_GPU
+    W = wl.make_weight(1, V, D)
+    h, tgt, A, B = wl.make_step_inputs(1000 + rank, T, V, D, R)
+    _, _, A, B = wl.make_step_inputs(1000, T, V, D, R)  # same adapter on every rank
+    cfg = lora_ce.default_config(D, V, R, T, scale=ALPHA / R, lr=LR, weight_decay=WD,
+                                 device=local)
+    m = lora_ce.LoraCE(cfg)
+    m.set_weight(W)
+    m.set_adapter(A, B, 0)
+    if world > 1:
+        uid = [lora_ce.LoraCE.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        m.comm_init(world, rank, uid[0])
+
+    dev = torch.device("cuda", local)
+    st = torch.cuda.ExternalStream(m.stream, device=dev)
+    dH = torch.from_numpy(h.view(np.int16)).to(dev)
+    dT = torch.from_numpy(tgt).to(dev)
+    dLoss = torch.zeros(2, dtype=torch.float32, device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def flush_l2():
+        with torch.cuda.stream(st):
+            flush.fill_(1.0)
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        if dist is not None:
+            dist.barrier()
+
+    def timed(fn, n):
+        """n calls of fn, each bracketed by CUDA events on the library's
+        stream with an L2 flush in between; returns per-call ms."""
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(n)]
+        for s, e in evs:
+            flush_l2()
+            s.record(st)
+            fn()
+            e.record(st)
+        torch.cuda.synchronize(dev)
+        return [s.elapsed_time(e) for s, e in evs]
+
+    def dev_step():
+        m.step_device(dH.data_ptr(), lora_ce.BF16, T, dT.data_ptr(), dLoss.data_ptr())
+
+    # device-resident throughput
+    for _ in range(args.warmup):
+        flush_l2()
+        dev_step()
+    m.sync()
+    barrier()
+    with ClockSampler(local) as clk:
+        ms = timed(dev_step, args.steps)
+    m.sync()
+    launches_per_step = m.last_launches
+    barrier()
+    step_ms = sum(ms) / len(ms)
+    t_max = torch.tensor([sum(ms)], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    total_ms = float(t_max.item())
+    value = world * T * args.steps / (total_ms / 1e3)
+
+    # per-kernel durations (same stream), for the roofline of the dominant kernel
+    m.set_profiling(True)
+    phase = {}
+    for _ in range(max(3, args.steps // 2)):
+        flush_l2()
+        dev_step()
+        for k, v in m.phase_times().items():
+            phase.setdefault(k, []).append(v)
+    m.set_profiling(False)
+    phase_ms = {k: sum(v) / len(v) for k, v in phase.items()}
+    dom = max(("pass1_lse", "pass2_grad"), key=lambda k: phase_ms[k])
+    peak_tf, hbm, peak_kind = peaks()
+    achieved = F_PASS * T / (phase_ms[dom] * 1e-3) / 1e12
+    traffic = None
+    tp = os.path.join(REPO, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        with open(tp) as f:
+            traffic = json.load(f).get(dom)
+
+    # end to end through the public API with pinned host buffers
+    hH = torch.from_numpy(h.view(np.int16)).pin_memory()
+    hT = torch.from_numpy(tgt).pin_memory()
+    hHn, hTn = hH.numpy().view(np.uint16), hT.numpy()
+    for _ in range(2):
+        m.step(hHn, hTn)
+    barrier()
+    e2e_ms = timed(lambda: m.step(hHn, hTn), args.steps)
+    e2e_t = torch.tensor([sum(e2e_ms)], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e_value = world * T * args.steps / (float(e2e_t.item()) / 1e3)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded; h bf16 N(0,1), W f16 N(0,0.02), Zipf(1.1) targets)",
+            "config": {"workload": "isolated fused LoRA lm_head CE fwd+bwd+AdamW step: "
+                                   "h [8192x576] bf16 per GPU, W [49152x576] f16, r 4, alpha 8",
+                       "T_per_gpu": T, "vocab": V, "dim": D, "rank": R, "lr": LR,
+                       "weight_decay": WD, "parallelism": f"dp{world}",
+                       "l2": "flushed (256 MB write) before every timed step"},
+            "tflops_step": F_TOK * T * world / (total_ms / args.steps * 1e-3) / 1e12 / world,
+            "frac_step_of_peak": F_TOK * T / (step_ms * 1e-3) / 1e12 / peak_tf,
+            "phase_ms": {k: round(v, 4) for k, v in phase_ms.items()},
+            "roofline": {"kernel": dom, "bound": "tensor", "achieved": achieved,
+                         "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf,
+                         "peak_kind": f"{peak_kind} bf16 dense burst",
+                         "flops_per_launch": F_PASS * T, "traffic": traffic},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": UNIT,
+                    "h2d_bytes_per_step": int(hH.numel() * 2 + hT.numel() * 4),
+                    "d2h_bytes_per_step": 8},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    m.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

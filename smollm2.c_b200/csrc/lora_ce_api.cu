@@ -1,0 +1,628 @@
+// lora_ce_api.cu — host side of the C ABI declared in include/lora_ce.h:
+// handle lifetime, uploads, the per-step launch sequence and the optional
+// NCCL all-reduce.  No CPU compute path exists: every step runs on the GPU
+// or fails with an error code.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "lora_ce.h"
+#include "lora_ce_kernels.cuh"
+
+using namespace lce;
+
+namespace {
+
+// Phases of one step, in launch order (lora_ce_phase_name).
+enum Phase { kPhPrep, kPhPass1, kPhCombine, kPhPass2, kPhDA, kPhFinalize, kPhAllReduce,
+             kPhNorm, kPhAdam, kNumPhases };
+const char* const kPhaseNames[kNumPhases] = {"prep", "pass1_lse", "combine", "pass2_grad",
+                                             "dA_partial", "finalize", "allreduce",
+                                             "sqnorm", "adam"};
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+#define LCE_CUDA(call)                                                                  \
+  do {                                                                                  \
+    cudaError_t e_ = (call);                                                            \
+    if (e_ != cudaSuccess)                                                              \
+      return fail(LORA_CE_ECUDA, std::string(#call) + ": " + cudaGetErrorString(e_));  \
+  } while (0)
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// [rows][d] f16 row-major, read in boxes of 64 x box_rows with 128 B swizzle.
+bool make_map(CUtensorMap* m, const void* base, long long rows, int d, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)d, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)d * 2};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+long long round_up(long long x, long long m) { return (x + m - 1) / m * m; }
+
+// Largest number of CTA segments any resident tile's run of n_b tiles is
+// split into, for n_a x n_b tiles over G CTAs.
+int max_segments(int n_a, int n_b, int G) {
+  const long long total = (long long)n_a * n_b;
+  int best = 1;
+  for (int a = 0; a < n_a; ++a) {
+    const int s0 = tile_owner((long long)a * n_b, total, G);
+    const int s1 = tile_owner((long long)a * n_b + n_b - 1, total, G);
+    if (s1 - s0 + 1 > best) best = s1 - s0 + 1;
+  }
+  return best;
+}
+
+}  // namespace
+
+struct lora_ce_handle {
+  lora_ce_config cfg{};
+  int R = 0, d = 0, V = 0;
+  long long Vpad = 0, Tcap = 0;
+  int num_sms = 0;
+  cudaStream_t stream = nullptr;
+  bool poisoned = false;
+  bool have_weight = false;
+  int32_t step = 0;
+  int32_t launches = 0;
+  int last_T = 0;
+  // device buffers
+  __half* W = nullptr;
+  __half* h16 = nullptr;
+  float* tok = nullptr;
+  float* params = nullptr;  // [A (d*R) | Bt (Vpad*R)]
+  float* mom1 = nullptr;
+  float* mom2 = nullptr;
+  float* Gbuf = nullptr;    // [dA | dB | loss | n_pred]
+  float* gmean = nullptr;
+  float* p_max = nullptr;
+  float* p_sum = nullptr;
+  float* p_q = nullptr;
+  long long p1_cap = 0;     // floats per p_max / p_sum
+  float* z_tgt = nullptr;
+  float* loss_tok = nullptr;
+  float* dU = nullptr;
+  float* gAp = nullptr;
+  float* gBp = nullptr;
+  int gbp_segs = 0;
+  double* norm_parts = nullptr;
+  int* err = nullptr;       // device error flag
+  float* d_loss = nullptr;  // [loss, err-as-int] result pair
+  void* in_H = nullptr;     // staging for host inputs
+  int32_t* in_tgt = nullptr;
+  CUtensorMap mapW_res{}, mapW_str{};
+  ncclComm_t comm = nullptr;
+  int nranks = 1, rank = 0;
+  // optional per-phase timing (events on the handle's stream)
+  bool prof = false;
+  cudaEvent_t ev[kNumPhases + 1] = {};
+};
+
+namespace {
+
+template <class T>
+int dalloc(T** p, size_t count) {
+  if (cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T) + 16) != cudaSuccess)
+    return fail(LORA_CE_ENOMEM, "cudaMalloc failed");
+  if (cudaMemset(*p, 0, count * sizeof(T) + 16) != cudaSuccess)
+    return fail(LORA_CE_ECUDA, "cudaMemset failed");
+  return 0;
+}
+
+void free_all(lora_ce_handle* h) {
+  void* ptrs[] = {h->W,     h->h16,   h->tok,      h->params, h->mom1,  h->mom2,
+                  h->Gbuf,  h->gmean, h->p_max,    h->p_sum,  h->p_q,   h->z_tgt,
+                  h->loss_tok, h->dU, h->gAp,      h->gBp,    h->norm_parts, h->err,
+                  h->d_loss, h->in_H, h->in_tgt};
+  for (void* p : ptrs)
+    if (p) cudaFree(p);
+}
+
+int check_cfg(const lora_ce_config* c) {
+  if (!c) return fail(LORA_CE_EINVAL, "null config");
+  if (c->dim < 64 || c->dim % 64 != 0 || c->dim > 64 * kMaxKBlocks)
+    return fail(LORA_CE_EINVAL, "dim must be a multiple of 64 in [64, 640]");
+  if (c->vocab < 1) return fail(LORA_CE_EINVAL, "vocab must be positive");
+  if (c->rank != 4 && c->rank != 8 && c->rank != 16)
+    return fail(LORA_CE_EINVAL, "rank must be 4, 8 or 16");
+  if (c->max_tokens < 1) return fail(LORA_CE_EINVAL, "max_tokens must be positive");
+  if (!(c->lr >= 0.f) || !(c->eps > 0.f) || !(c->beta1 >= 0.f && c->beta1 < 1.f) ||
+      !(c->beta2 >= 0.f && c->beta2 < 1.f) || !(c->weight_decay >= 0.f) ||
+      !(c->clip_norm >= 0.f) || !std::isfinite(c->scale))
+    return fail(LORA_CE_EINVAL, "bad optimizer hyper-parameters");
+  return 0;
+}
+
+inline void mark(lora_ce_handle* h, int phase) {
+  if (h->prof) cudaEventRecord(h->ev[phase], h->stream);
+}
+
+template <int R>
+int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t* dtg,
+             float* d_loss_out) {
+  cudaStream_t st = h->stream;
+  const int d = h->d, V = h->V;
+  const int kblocks = d / kBK;
+  const long long Tpad = round_up(T, kBN);
+  int launches = 0;
+
+  CUtensorMap mapH_res, mapH_str;
+  if (!make_map(&mapH_res, h->h16, T, d, kBM) || !make_map(&mapH_str, h->h16, T, d, kBN))
+    return fail(LORA_CE_ECUDA, "cuTensorMapEncodeTiled failed for h");
+
+  // 1. convert h, U = h.A, per-position records
+  mark(h, kPhPrep);
+  {
+    const int threads = 256;
+    const long long warps = Tpad;
+    const int blocks = (int)((warps * 32 + threads - 1) / threads);
+    lce_prep<R><<<blocks, threads, 0, st>>>(dH, dtype, T, (int)Tpad, d, h->params, h->cfg.scale,
+                                            dtg, V, h->h16, h->tok, h->err);
+    ++launches;
+  }
+  const size_t smem = SmemLayout::bytes(kblocks);
+  mark(h, kPhPass1);
+  // 2. pass 1: per-position max / sum / q over the vocabulary
+  const int n_a1 = (T + kBM - 1) / kBM, n_b1 = (int)(h->Vpad / kBN);
+  const long long total1 = (long long)n_a1 * n_b1;
+  const int G1 = (int)std::min<long long>(h->num_sms, total1);
+  const int seg1 = max_segments(n_a1, n_b1, G1);
+  const long long stride1 = (long long)n_a1 * kBM;
+  if ((long long)seg1 * stride1 > h->p1_cap)
+    return fail(LORA_CE_ESTATE, "pass-1 partial buffer too small");
+  GemmArgs g{};
+  g.kblocks = kblocks;
+  g.T = T;
+  g.V = V;
+  g.R = R;
+  g.Vpad = h->Vpad;
+  g.err = h->err;
+  g.tok = h->tok;
+  g.Bt = h->params + (long long)d * R;
+  g.p_max = h->p_max;
+  g.p_sum = h->p_sum;
+  g.p_q = h->p_q;
+  g.z_tgt = h->z_tgt;
+  g.gBp = h->gBp;
+  {
+    g.n_a = n_a1;
+    g.n_b = n_b1;
+    g.Tcap = stride1;
+    auto kern = lce_gemm_kernel<EpiLse<R>>;
+    LCE_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kern<<<G1, kThreads, smem, st>>>(mapH_res, h->mapW_str, g);
+    ++launches;
+  }
+  // 3. merge partials -> M, 1/S, loss_t, dU
+  mark(h, kPhCombine);
+  lce_combine<R><<<(T + 255) / 256, 256, 0, st>>>(T, n_b1, G1, stride1, h->p_max, h->p_sum,
+                                                  h->p_q, h->z_tgt, g.Bt, h->cfg.scale, h->tok,
+                                                  h->dU, h->loss_tok);
+  ++launches;
+  // 4. pass 2: dB per vocab row
+  const int n_a2 = (V + kBM - 1) / kBM, n_b2 = (int)(Tpad / kBN);
+  const long long total2 = (long long)n_a2 * n_b2;
+  const int G2 = (int)std::min<long long>(h->num_sms, total2);
+  if (max_segments(n_a2, n_b2, G2) > h->gbp_segs)
+    return fail(LORA_CE_ESTATE, "pass-2 partial buffer too small");
+  mark(h, kPhPass2);
+  {
+    g.n_a = n_a2;
+    g.n_b = n_b2;
+    g.Tcap = stride1;
+    auto kern = lce_gemm_kernel<EpiGrad<R>>;
+    LCE_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kern<<<G2, kThreads, smem, st>>>(h->mapW_res, mapH_str, g);
+    ++launches;
+  }
+  // 5. dA partials, 6. pack gradient sums
+  const int n_chunks = (T + 255) / 256;
+  mark(h, kPhDA);
+  lce_dA_partial<R><<<n_chunks, 256, 0, st>>>(T, d, h->h16, h->dU, h->gAp);
+  ++launches;
+  const long long nparam = (long long)d * R + (long long)V * R;
+  mark(h, kPhFinalize);
+  {
+    const int blocks = (int)std::min<long long>((nparam + 255) / 256, 8LL * h->num_sms);
+    lce_finalize<R><<<blocks, 256, 0, st>>>(T, d, V, h->Vpad, n_chunks, h->gAp, n_b2, G2, h->gBp,
+                                            h->loss_tok, h->Gbuf);
+    ++launches;
+  }
+  // 7. data-parallel sum over ranks
+  mark(h, kPhAllReduce);
+  if (h->comm) {
+    if (ncclAllReduce(h->Gbuf, h->Gbuf, (size_t)(nparam + 2), ncclFloat, ncclSum, h->comm, st) !=
+        ncclSuccess)
+      return fail(LORA_CE_ENCCL, "ncclAllReduce failed");
+  }
+  // 8. clip norm (optional), 9. Adam
+  AdamArgs aa{};
+  aa.n = nparam;
+  aa.lr = h->cfg.lr;
+  aa.b1 = h->cfg.beta1;
+  aa.b2 = h->cfg.beta2;
+  aa.c1 = 1.0f - h->cfg.beta1;
+  aa.c2 = 1.0f - h->cfg.beta2;
+  aa.eps = h->cfg.eps;
+  aa.wd = h->cfg.weight_decay;
+  aa.clip = h->cfg.clip_norm;
+  const int32_t next_step = h->step + 1;
+  aa.b1t = 1.0f - powf(h->cfg.beta1, (float)next_step);
+  aa.b2t = 1.0f - powf(h->cfg.beta2, (float)next_step);
+  aa.n_norm_parts = 0;
+  mark(h, kPhNorm);
+  if (aa.clip > 0.f) {
+    aa.n_norm_parts = 256;
+    lce_sqnorm<<<256, 256, 0, st>>>(nparam, h->Gbuf, h->norm_parts);
+    ++launches;
+  }
+  mark(h, kPhAdam);
+  {
+    const int blocks = (int)std::min<long long>((nparam + 255) / 256, 8LL * h->num_sms);
+    lce_adam<<<blocks, 256, 0, st>>>(aa, h->params, h->mom1, h->mom2, h->Gbuf, h->gmean,
+                                     h->norm_parts, d_loss_out);
+    ++launches;
+  }
+  mark(h, kNumPhases);
+  LCE_CUDA(cudaGetLastError());
+  h->step = next_step;
+  h->launches = launches;
+  h->last_T = T;
+  return 0;
+}
+
+int dispatch_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t* dtg,
+                  float* d_loss) {
+  switch (h->R) {
+    case 4: return run_step<4>(h, dH, dtype, T, dtg, d_loss);
+    case 8: return run_step<8>(h, dH, dtype, T, dtg, d_loss);
+    case 16: return run_step<16>(h, dH, dtype, T, dtg, d_loss);
+  }
+  return fail(LORA_CE_EINVAL, "unsupported rank");
+}
+
+int check_step_args(lora_ce_handle* h, const void* H, int dtype, int T, const int32_t* tg) {
+  if (!h) return fail(LORA_CE_EINVAL, "null handle");
+  if (h->poisoned) return fail(LORA_CE_ESTATE, "handle poisoned by an earlier error");
+  if (!h->have_weight) return fail(LORA_CE_ESTATE, "lora_ce_set_weight_f16 not called");
+  if (!H || !tg) return fail(LORA_CE_EINVAL, "null input");
+  if (dtype < 0 || dtype > 2) return fail(LORA_CE_EINVAL, "bad hidden-state dtype");
+  if (T < 1 || T > h->cfg.max_tokens) return fail(LORA_CE_EINVAL, "T out of range");
+  return 0;
+}
+
+int elt_size(int dtype) { return dtype == LORA_CE_F32 ? 4 : 2; }
+
+int check_device_error(lora_ce_handle* h) {
+  int e = 0;
+  LCE_CUDA(cudaMemcpyAsync(&e, h->err, sizeof(int), cudaMemcpyDeviceToHost, h->stream));
+  LCE_CUDA(cudaStreamSynchronize(h->stream));
+  if (e != 0) {
+    h->poisoned = true;
+    char buf[96];
+    snprintf(buf, sizeof buf, "device error %d (%s)", e,
+             e == kErrTarget ? "target id out of range" : "bounded wait expired");
+    return fail(LORA_CE_EDEVICE, buf);
+  }
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+void lora_ce_default_config(lora_ce_config* c, int32_t dim, int32_t vocab, int32_t rank,
+                            int32_t max_tokens) {
+  if (!c) return;
+  memset(c, 0, sizeof(*c));
+  c->dim = dim;
+  c->vocab = vocab;
+  c->rank = rank;
+  c->scale = rank > 0 ? 16.0f / (float)rank : 0.f;
+  c->lr = 1e-4f;
+  c->beta1 = 0.9f;
+  c->beta2 = 0.999f;
+  c->eps = 1e-8f;
+  c->weight_decay = 0.f;
+  c->clip_norm = 0.f;
+  c->max_tokens = max_tokens;
+  c->device = 0;
+}
+
+const char* lora_ce_last_error(void) { return g_last_error.c_str(); }
+
+int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
+  if (!out) return fail(LORA_CE_EINVAL, "null output pointer");
+  *out = nullptr;
+  int rc = check_cfg(cfg);
+  if (rc) return rc;
+  LCE_CUDA(cudaSetDevice(cfg->device));
+  cudaDeviceProp prop;
+  LCE_CUDA(cudaGetDeviceProperties(&prop, cfg->device));
+  if (prop.major != 10) return fail(LORA_CE_ECUDA, "this library runs on sm_100 (B200) only");
+  if (!encode_fn()) return fail(LORA_CE_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  lora_ce_handle* h = new (std::nothrow) lora_ce_handle();
+  if (!h) return fail(LORA_CE_ENOMEM, "host allocation failed");
+  h->cfg = *cfg;
+  h->R = cfg->rank;
+  h->d = cfg->dim;
+  h->V = cfg->vocab;
+  h->Vpad = round_up(cfg->vocab, kBN);
+  h->Tcap = round_up(cfg->max_tokens, kBN);
+  h->num_sms = prop.multiProcessorCount;
+  const int R = h->R, d = h->d;
+  const long long V = h->V, Vpad = h->Vpad, Tcap = h->Tcap;
+  // worst-case partial-buffer sizes over every T <= max_tokens
+  long long p1 = 0;
+  int s2 = 1;
+  const int n_b1 = (int)(Vpad / kBN), n_a2 = (int)((V + kBM - 1) / kBM);
+  for (int n_a1 = 1; (long long)n_a1 * kBM < Tcap + kBM; ++n_a1) {
+    const long long total = (long long)n_a1 * n_b1;
+    const int G = (int)std::min<long long>(h->num_sms, total);
+    p1 = std::max<long long>(p1, (long long)max_segments(n_a1, n_b1, G) * n_a1 * kBM);
+  }
+  for (int n_b2 = 1; (long long)n_b2 * kBN <= Tcap; ++n_b2) {
+    const long long total = (long long)n_a2 * n_b2;
+    const int G = (int)std::min<long long>(h->num_sms, total);
+    s2 = std::max(s2, max_segments(n_a2, n_b2, G));
+  }
+  h->p1_cap = p1;
+  h->gbp_segs = s2;
+  const long long nparam_pad = (long long)d * R + Vpad * R;
+  const long long nparam = (long long)d * R + V * R;
+  rc = 0;
+  if (!rc) rc = dalloc(&h->W, (size_t)V * d);
+  if (!rc) rc = dalloc(&h->h16, (size_t)Tcap * d);
+  if (!rc) rc = dalloc(&h->tok, (size_t)Tcap * tok_stride(R));
+  if (!rc) rc = dalloc(&h->params, (size_t)nparam_pad);
+  if (!rc) rc = dalloc(&h->mom1, (size_t)nparam_pad);
+  if (!rc) rc = dalloc(&h->mom2, (size_t)nparam_pad);
+  if (!rc) rc = dalloc(&h->Gbuf, (size_t)nparam + 2);
+  if (!rc) rc = dalloc(&h->gmean, (size_t)nparam);
+  if (!rc) rc = dalloc(&h->p_max, (size_t)p1);
+  if (!rc) rc = dalloc(&h->p_sum, (size_t)p1);
+  if (!rc) rc = dalloc(&h->p_q, (size_t)p1 * R);
+  if (!rc) rc = dalloc(&h->z_tgt, (size_t)Tcap);
+  if (!rc) rc = dalloc(&h->loss_tok, (size_t)Tcap);
+  if (!rc) rc = dalloc(&h->dU, (size_t)Tcap * R);
+  if (!rc) rc = dalloc(&h->gAp, (size_t)(Tcap / 256) * d * R);
+  if (!rc) rc = dalloc(&h->gBp, (size_t)s2 * Vpad * R);
+  if (!rc) rc = dalloc(&h->norm_parts, 256);
+  if (!rc) rc = dalloc(&h->err, 1);
+  if (!rc) rc = dalloc(&h->d_loss, 2);
+  if (!rc) rc = dalloc(reinterpret_cast<char**>(&h->in_H), (size_t)Tcap * d * 4);
+  if (!rc) rc = dalloc(&h->in_tgt, (size_t)Tcap);
+  if (!rc && cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess)
+    rc = fail(LORA_CE_ECUDA, "cudaStreamCreate failed");
+  if (!rc && !(make_map(&h->mapW_res, h->W, V, d, kBM) && make_map(&h->mapW_str, h->W, V, d, kBN)))
+    rc = fail(LORA_CE_ECUDA, "cuTensorMapEncodeTiled failed for W");
+  if (rc) {
+    free_all(h);
+    if (h->stream) cudaStreamDestroy(h->stream);
+    delete h;
+    return rc;
+  }
+  *out = h;
+  return 0;
+}
+
+int lora_ce_destroy(lora_ce_handle* h) {
+  if (!h) return 0;
+  cudaSetDevice(h->cfg.device);
+  if (h->stream) cudaStreamSynchronize(h->stream);
+  if (h->comm) ncclCommDestroy(h->comm);
+  for (cudaEvent_t e : h->ev)
+    if (e) cudaEventDestroy(e);
+  free_all(h);
+  if (h->stream) cudaStreamDestroy(h->stream);
+  delete h;
+  return 0;
+}
+
+int lora_ce_set_weight_f16(lora_ce_handle* h, const uint16_t* W) {
+  if (!h || !W) return fail(LORA_CE_EINVAL, "null argument");
+  LCE_CUDA(cudaSetDevice(h->cfg.device));
+  LCE_CUDA(cudaMemcpyAsync(h->W, W, (size_t)h->V * h->d * 2, cudaMemcpyHostToDevice, h->stream));
+  LCE_CUDA(cudaStreamSynchronize(h->stream));
+  h->have_weight = true;
+  return 0;
+}
+
+int lora_ce_set_adapter(lora_ce_handle* h, const float* A, const float* B, int32_t step) {
+  if (!h || !A || !B || step < 0) return fail(LORA_CE_EINVAL, "bad argument");
+  LCE_CUDA(cudaSetDevice(h->cfg.device));
+  const int R = h->R, d = h->d, V = h->V;
+  std::vector<float> Bt((size_t)h->Vpad * R, 0.f);
+  for (int j = 0; j < R; ++j)
+    for (int v = 0; v < V; ++v) Bt[(size_t)v * R + j] = B[(size_t)j * V + v];
+  const size_t nA = (size_t)d * R;
+  LCE_CUDA(cudaMemcpyAsync(h->params, A, nA * 4, cudaMemcpyHostToDevice, h->stream));
+  LCE_CUDA(cudaMemcpyAsync(h->params + nA, Bt.data(), Bt.size() * 4, cudaMemcpyHostToDevice,
+                           h->stream));
+  const size_t np = nA + Bt.size();
+  LCE_CUDA(cudaMemsetAsync(h->mom1, 0, np * 4, h->stream));
+  LCE_CUDA(cudaMemsetAsync(h->mom2, 0, np * 4, h->stream));
+  LCE_CUDA(cudaStreamSynchronize(h->stream));
+  h->step = step;
+  return 0;
+}
+
+int lora_ce_get_adapter(lora_ce_handle* h, float* A, float* B, int32_t* step) {
+  if (!h) return fail(LORA_CE_EINVAL, "null handle");
+  LCE_CUDA(cudaSetDevice(h->cfg.device));
+  int rc = check_device_error(h);
+  if (rc) return rc;
+  const int R = h->R, d = h->d, V = h->V;
+  if (A) LCE_CUDA(cudaMemcpy(A, h->params, (size_t)d * R * 4, cudaMemcpyDeviceToHost));
+  if (B) {
+    std::vector<float> Bt((size_t)V * R);
+    LCE_CUDA(cudaMemcpy(Bt.data(), h->params + (size_t)d * R, Bt.size() * 4,
+                        cudaMemcpyDeviceToHost));
+    for (int j = 0; j < R; ++j)
+      for (int v = 0; v < V; ++v) B[(size_t)j * V + v] = Bt[(size_t)v * R + j];
+  }
+  if (step) *step = h->step;
+  return 0;
+}
+
+int lora_ce_get_grads(lora_ce_handle* h, float* gA, float* gB, float* loss_sum, float* n_pred) {
+  if (!h) return fail(LORA_CE_EINVAL, "null handle");
+  LCE_CUDA(cudaSetDevice(h->cfg.device));
+  int rc = check_device_error(h);
+  if (rc) return rc;
+  const int R = h->R, d = h->d, V = h->V;
+  if (gA) LCE_CUDA(cudaMemcpy(gA, h->gmean, (size_t)d * R * 4, cudaMemcpyDeviceToHost));
+  if (gB) {
+    std::vector<float> t((size_t)V * R);
+    LCE_CUDA(cudaMemcpy(t.data(), h->gmean + (size_t)d * R, t.size() * 4, cudaMemcpyDeviceToHost));
+    for (int j = 0; j < R; ++j)
+      for (int v = 0; v < V; ++v) gB[(size_t)j * V + v] = t[(size_t)v * R + j];
+  }
+  const long long nparam = (long long)d * R + (long long)V * R;
+  float tail[2];
+  LCE_CUDA(cudaMemcpy(tail, h->Gbuf + nparam, 8, cudaMemcpyDeviceToHost));
+  if (loss_sum) *loss_sum = tail[0];
+  if (n_pred) *n_pred = tail[1];
+  return 0;
+}
+
+int lora_ce_get_token_loss(lora_ce_handle* h, float* loss_t, int32_t T) {
+  if (!h || !loss_t || T < 0 || T > h->last_T) return fail(LORA_CE_EINVAL, "bad argument");
+  LCE_CUDA(cudaSetDevice(h->cfg.device));
+  int rc = check_device_error(h);
+  if (rc) return rc;
+  LCE_CUDA(cudaMemcpy(loss_t, h->loss_tok, (size_t)T * 4, cudaMemcpyDeviceToHost));
+  return 0;
+}
+
+int lora_ce_step_device(lora_ce_handle* h, const void* dH, int32_t dtype, int32_t T,
+                        const int32_t* dtg, float* d_loss) {
+  int rc = check_step_args(h, dH, dtype, T, dtg);
+  if (rc) return rc;
+  LCE_CUDA(cudaSetDevice(h->cfg.device));
+  rc = dispatch_step(h, dH, dtype, T, dtg, d_loss ? d_loss : h->d_loss);
+  if (rc) h->poisoned = true;
+  return rc;
+}
+
+int lora_ce_step(lora_ce_handle* h, const void* H, int32_t dtype, int32_t T,
+                 const int32_t* targets, float* loss_out) {
+  int rc = check_step_args(h, H, dtype, T, targets);
+  if (rc) return rc;
+  LCE_CUDA(cudaSetDevice(h->cfg.device));
+  LCE_CUDA(cudaMemcpyAsync(h->in_H, H, (size_t)T * h->d * elt_size(dtype), cudaMemcpyHostToDevice,
+                           h->stream));
+  LCE_CUDA(cudaMemcpyAsync(h->in_tgt, targets, (size_t)T * 4, cudaMemcpyHostToDevice, h->stream));
+  rc = dispatch_step(h, h->in_H, dtype, T, h->in_tgt, h->d_loss);
+  if (rc) {
+    h->poisoned = true;
+    return rc;
+  }
+  LCE_CUDA(cudaMemcpyAsync(h->d_loss + 1, h->err, 4, cudaMemcpyDeviceToDevice, h->stream));
+  float res[2];
+  LCE_CUDA(cudaMemcpyAsync(res, h->d_loss, 8, cudaMemcpyDeviceToHost, h->stream));
+  LCE_CUDA(cudaStreamSynchronize(h->stream));
+  int e;
+  memcpy(&e, &res[1], 4);
+  if (e != 0) {
+    h->poisoned = true;
+    return fail(LORA_CE_EDEVICE, e == kErrTarget ? "target id out of range"
+                                                 : "device pipeline error (bounded wait expired)");
+  }
+  if (loss_out) *loss_out = res[0];
+  return 0;
+}
+
+int lora_ce_sync(lora_ce_handle* h) {
+  if (!h) return fail(LORA_CE_EINVAL, "null handle");
+  LCE_CUDA(cudaSetDevice(h->cfg.device));
+  return check_device_error(h);
+}
+
+int lora_ce_nccl_unique_id(void* id128) {
+  if (!id128) return fail(LORA_CE_EINVAL, "null id buffer");
+  static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId size");
+  ncclUniqueId id;
+  if (ncclGetUniqueId(&id) != ncclSuccess) return fail(LORA_CE_ENCCL, "ncclGetUniqueId failed");
+  memcpy(id128, &id, 128);
+  return 0;
+}
+
+int lora_ce_comm_init(lora_ce_handle* h, int32_t nranks, int32_t rank, const void* id128) {
+  if (!h || !id128 || nranks < 1 || rank < 0 || rank >= nranks)
+    return fail(LORA_CE_EINVAL, "bad communicator arguments");
+  if (h->comm) return fail(LORA_CE_ESTATE, "communicator already initialised");
+  LCE_CUDA(cudaSetDevice(h->cfg.device));
+  ncclUniqueId id;
+  memcpy(&id, id128, 128);
+  if (ncclCommInitRank(&h->comm, nranks, id, rank) != ncclSuccess)
+    return fail(LORA_CE_ENCCL, "ncclCommInitRank failed");
+  h->nranks = nranks;
+  h->rank = rank;
+  return 0;
+}
+
+int lora_ce_set_profiling(lora_ce_handle* h, int32_t enable) {
+  if (!h) return fail(LORA_CE_EINVAL, "null handle");
+  LCE_CUDA(cudaSetDevice(h->cfg.device));
+  if (enable && !h->ev[0])
+    for (cudaEvent_t& e : h->ev) LCE_CUDA(cudaEventCreate(&e));
+  h->prof = enable != 0;
+  return 0;
+}
+
+int32_t lora_ce_phase_times(lora_ce_handle* h, float* ms, int32_t cap) {
+  if (!h || !ms || !h->prof) return fail(LORA_CE_EINVAL, "profiling not enabled");
+  if (cudaSetDevice(h->cfg.device) != cudaSuccess ||
+      cudaEventSynchronize(h->ev[kNumPhases]) != cudaSuccess)
+    return fail(LORA_CE_ECUDA, "cudaEventSynchronize failed");
+  const int n = cap < kNumPhases ? cap : kNumPhases;
+  for (int i = 0; i < n; ++i)
+    if (cudaEventElapsedTime(&ms[i], h->ev[i], h->ev[i + 1]) != cudaSuccess)
+      return fail(LORA_CE_ECUDA, "cudaEventElapsedTime failed");
+  return n;
+}
+
+const char* lora_ce_phase_name(int32_t i) {
+  return (i >= 0 && i < kNumPhases) ? kPhaseNames[i] : "";
+}
+
+void* lora_ce_stream(lora_ce_handle* h) { return h ? (void*)h->stream : nullptr; }
+
+int32_t lora_ce_last_launches(lora_ce_handle* h) { return h ? h->launches : 0; }
+
+}  // extern "C"

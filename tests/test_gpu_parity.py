@@ -1,0 +1,221 @@
+"""Parity of the CUDA path (through the C ABI) with the oracle on seeded
+inputs.  Tolerances: loss within 1e-4 relative; dA, dB and the updated A, B
+within 1e-3 relative L2; target indexing exact."""
+import os
+
+import numpy as np
+import pytest
+
+import lora_ce
+import workload as wl
+
+pytestmark = pytest.mark.gpu
+
+NTHREADS = os.cpu_count() or 8
+LOSS_RTOL = 1e-4
+L2_RTOL = 1e-3
+
+
+def rel(a, b):
+    return float(np.linalg.norm(np.asarray(a, np.float64) - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def make(V, d, r, T, seed, dtype="bf16"):
+    W = wl.make_weight(seed, V, d)
+    h, tgt, A, B = wl.make_step_inputs(seed, T, V, d, r)
+    Hor = wl.oracle_hidden(h)
+    if dtype == "bf16":
+        H = h
+    elif dtype == "f16":
+        H = Hor.astype(np.float16)
+    else:
+        H = Hor.copy()  # f32 values already f16-representable
+    return W, H, Hor, tgt, A, B
+
+
+def run_case(oracle, V, d, r, T, seed, dtype="bf16", steps=1, scale=2.0, lr=1e-3, wd=0.0,
+             clip=0.0):
+    W, H, Hor, tgt, A, B = make(V, d, r, T, seed, dtype)
+    cfg = lora_ce.default_config(d, V, r, T, scale=scale, lr=lr, weight_decay=wd,
+                                 clip_norm=clip)
+    m = lora_ce.LoraCE(cfg)
+    m.set_weight(W)
+    m.set_adapter(A, B, 0)
+    state, Ao, Bo = None, A, B
+    for k in range(steps):
+        loss = m.step(H, tgt)
+        ref = oracle.step(W, Ao, Bo, Hor, tgt, scale, lr, wd=wd, clip=clip, nthreads=NTHREADS,
+                          state=state)
+        state, Ao, Bo = ref["state"], ref["A"], ref["B"]
+        gA, gB, loss_sum, n_pred = m.get_grads()
+        A1, B1, step = m.get_adapter()
+        assert step == k + 1 and n_pred == T
+        assert abs(loss - ref["loss"]) <= LOSS_RTOL * abs(ref["loss"]), (k, loss, ref["loss"])
+        tl = m.token_loss(T)
+        assert rel(tl, ref["loss_tok"]) <= LOSS_RTOL
+        for name, a, b in (("dA", gA, ref["gA"]), ("dB", gB, ref["gB"]), ("A", A1, Ao),
+                           ("B", B1, Bo)):
+            e = rel(a, b)
+            assert e <= L2_RTOL, f"step {k}: {name} rel L2 {e:.3e}"
+        # continue both from the GPU state so later steps test one update each
+        Ao, Bo = A1, B1
+        m.set_adapter(A1, B1, step)
+        state["mA"], state["vA"], state["mB"], state["vB"] = (np.zeros_like(state["mA"]),
+                                                              np.zeros_like(state["vA"]),
+                                                              np.zeros_like(state["mB"]),
+                                                              np.zeros_like(state["vB"]))
+    m.close()
+
+
+@pytest.mark.parametrize(
+    "V,d,r,T,dtype",
+    [
+        (49152, 576, 4, 256, "bf16"),   # the isolated-op shape at reduced T
+        (49152, 576, 4, 1, "bf16"),     # a single position
+        (4099, 128, 4, 129, "f16"),     # V and T off the tile grid
+        (1000, 64, 8, 300, "f32"),      # small d, rank 8, f32 input
+        (2048, 576, 16, 513, "bf16"),   # rank 16
+        (49152, 576, 8, 127, "bf16"),
+    ],
+)
+def test_step_matches_oracle(oracle, V, d, r, T, dtype):
+    run_case(oracle, V, d, r, T, seed=V + T + r, dtype=dtype, steps=2)
+
+
+def test_adamw_and_clip_extensions(oracle):
+    run_case(oracle, 49152, 576, 4, 300, seed=77, wd=0.01, clip=1.0, steps=2)
+    run_case(oracle, 3000, 128, 4, 50, seed=78, wd=0.01, clip=1e-4, steps=1)  # clip active
+
+
+def test_adam_state_carries_over_steps(oracle):
+    """Three consecutive steps with the Adam moments kept on both sides."""
+    V, d, r, T = 8192, 576, 4, 200
+    W, H, Hor, tgt, A, B = make(V, d, r, T, 5)
+    m = lora_ce.LoraCE(lora_ce.default_config(d, V, r, T, scale=2.0, lr=1e-3))
+    m.set_weight(W)
+    m.set_adapter(A, B, 0)
+    state = None
+    Ao, Bo = A, B
+    for k in range(3):
+        loss = m.step(H, tgt)
+        ref = oracle.step(W, Ao, Bo, Hor, tgt, 2.0, 1e-3, nthreads=NTHREADS, state=state)
+        state, Ao, Bo = ref["state"], ref["A"], ref["B"]
+        assert abs(loss - ref["loss"]) <= LOSS_RTOL * ref["loss"]
+    A1, B1, step = m.get_adapter()
+    assert step == 3
+    assert rel(A1, Ao) <= L2_RTOL and rel(B1, Bo) <= L2_RTOL
+    m.close()
+
+
+def test_target_indexing_matches_train_step(oracle):
+    """tokens -> targets: positions 0..use_n-2 predict tokens[pos+1] with
+    use_n = min(n, seq_max) (src/train.c:198-229)."""
+    V, d, r = 4096, 128, 4
+    W, H, Hor, tgt, A, B = make(V, d, r, 64, 9)
+    tokens = np.concatenate([[3], tgt]).astype(np.int32)
+    for seq_max in (65, 30, 2):
+        m = lora_ce.LoraCE(lora_ce.default_config(d, V, r, 64, scale=2.0, lr=1e-3))
+        m.set_weight(W)
+        m.set_adapter(A, B, 0)
+        loss = m.train_step_tokens(H, tokens, seq_max)
+        ref = oracle.train_step_tokens(W, A, B, Hor, tokens, seq_max, 2.0, 1e-3)
+        _, _, _, n_pred = m.get_grads()
+        assert n_pred == min(len(tokens), seq_max) - 1
+        assert abs(loss - ref["loss"]) <= LOSS_RTOL * ref["loss"]
+        m.close()
+    m = lora_ce.LoraCE(lora_ce.default_config(d, V, r, 64))
+    m.set_weight(W)
+    assert m.train_step_tokens(H, tokens[:1], 10) == -1.0
+    m.close()
+
+
+def test_deterministic():
+    V, d, r, T = 49152, 576, 4, 1000
+    W, H, _, tgt, A, B = make(V, d, r, T, 21)
+    outs = []
+    for _ in range(2):
+        m = lora_ce.LoraCE(lora_ce.default_config(d, V, r, T, scale=2.0, lr=1e-3))
+        m.set_weight(W)
+        m.set_adapter(A, B, 0)
+        loss = m.step(H, tgt)
+        outs.append((loss,) + m.get_grads()[:2] + m.get_adapter()[:2])
+        m.close()
+    for a, b in zip(outs[0], outs[1]):
+        np.testing.assert_array_equal(a, b)
+
+
+def test_adapter_roundtrip_and_lora0001(tmp_path):
+    V, d, r = 2048, 128, 8
+    W, _, _, _, A, B = make(V, d, r, 4, 3)
+    m = lora_ce.LoraCE(lora_ce.default_config(d, V, r, 16))
+    m.set_weight(W)
+    m.set_adapter(A, B, 17)
+    A1, B1, s = m.get_adapter()
+    np.testing.assert_array_equal(A1, A)
+    np.testing.assert_array_equal(B1, B)
+    assert s == 17
+    p = str(tmp_path / "lora.bin")
+    m.save(p)
+    assert os.path.getsize(p) == 28 + 4 * d * r + 4 * r * V
+    m2 = lora_ce.LoraCE(lora_ce.default_config(d, V, r, 16))
+    m2.load(p)
+    A2, B2, s2 = m2.get_adapter()
+    np.testing.assert_array_equal(A2, A)
+    np.testing.assert_array_equal(B2, B)
+    assert s2 == 17
+    m.close()
+    m2.close()
+
+
+def test_errors_are_reported_not_raised_on_device():
+    V, d, r, T = 1024, 64, 4, 32
+    W, H, _, tgt, A, B = make(V, d, r, T, 4)
+    m = lora_ce.LoraCE(lora_ce.default_config(d, V, r, T))
+    with pytest.raises(lora_ce.LoraCEError, match="ESTATE"):
+        m.step(H, tgt)  # no weight yet
+    m.set_weight(W)
+    with pytest.raises(lora_ce.LoraCEError, match="EINVAL"):
+        m.step(np.zeros((T + 1, d), np.uint16), np.zeros(T + 1, np.int32))  # T > max_tokens
+    bad = tgt.copy()
+    bad[5] = V  # caught by the kernel's range check, clamped, reported
+    with pytest.raises(lora_ce.LoraCEError, match="EDEVICE"):
+        m.step(H, bad)
+    with pytest.raises(lora_ce.LoraCEError, match="ESTATE"):
+        m.step(H, tgt)  # poisoned
+    m.close()
+    # the context is still usable
+    m = lora_ce.LoraCE(lora_ce.default_config(d, V, r, T))
+    m.set_weight(W)
+    m.set_adapter(A, B, 0)
+    assert np.isfinite(m.step(H, tgt))
+    m.close()
+
+
+def test_full_size_isolated_op(oracle):
+    """h [8192x576], W [49152x576], r = 4: one step against the oracle
+    (all host cores), plus the additivity of the gradient sums over two
+    halves of the positions."""
+    V, d, r, T = 49152, 576, 4, 8192
+    W, H, Hor, tgt, A, B = make(V, d, r, T, 2024)
+    m = lora_ce.LoraCE(lora_ce.default_config(d, V, r, T, scale=2.0, lr=1e-3))
+    m.set_weight(W)
+    m.set_adapter(A, B, 0)
+    loss = m.step(H, tgt)
+    gA, gB, lsum, n = m.get_grads()
+    A1, B1, _ = m.get_adapter()
+    ref = oracle.step(W, A, B, Hor, tgt, 2.0, 1e-3, nthreads=NTHREADS)
+    assert abs(loss - ref["loss"]) <= LOSS_RTOL * ref["loss"]
+    for name, a, b in (("dA", gA, ref["gA"]), ("dB", gB, ref["gB"]), ("A", A1, ref["A"]),
+                       ("B", B1, ref["B"])):
+        assert rel(a, b) <= L2_RTOL, (name, rel(a, b))
+    # sums over the halves add up to the sum over all positions
+    sums = []
+    for sl in (slice(0, T // 2), slice(T // 2, T)):
+        m.set_adapter(A, B, 0)
+        m.step(np.ascontiguousarray(H[sl]), np.ascontiguousarray(tgt[sl]))
+        ga, gb, ls, nn = m.get_grads()
+        sums.append((ga * nn, gb * nn, ls))
+    assert rel(sums[0][0] + sums[1][0], gA * n) <= 1e-5
+    assert rel(sums[0][1] + sums[1][1], gB * n) <= 1e-5
+    assert abs(sums[0][2] + sums[1][2] - lsum) <= 1e-5 * lsum
+    m.close()
