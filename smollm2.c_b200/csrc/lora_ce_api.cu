@@ -194,13 +194,15 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
                                             dtg, V, h->h16, h->tok, h->err);
     ++launches;
   }
-  const size_t smem = SmemLayout::bytes(kblocks);
+  const int smem1 = SmemLayout::bytes(kblocks, EpiLse<R>::kRec);
+  const int smem2 = SmemLayout::bytes(kblocks, EpiGrad<R>::kRec);
+  const bool stage1 = smem1 <= kMaxDynSmem, stage2 = smem2 <= kMaxDynSmem;
   mark(h, kPhPass1);
   // 2. pass 1: per-position max / sum / q over the vocabulary
   const int n_a1 = (T + kBM - 1) / kBM, n_b1 = (int)(h->Vpad / kBN);
   const long long total1 = (long long)n_a1 * n_b1;
   const int G1 = (int)std::min<long long>(h->num_sms, total1);
-  const int seg1 = max_segments(n_a1, n_b1, G1);
+  const int seg1 = 2 * max_segments(n_a1, n_b1, G1);
   const long long stride1 = (long long)n_a1 * kBM;
   if ((long long)seg1 * stride1 > h->p1_cap)
     return fail(LORA_CE_ESTATE, "pass-1 partial buffer too small");
@@ -222,8 +224,9 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
     g.n_a = n_a1;
     g.n_b = n_b1;
     g.Tcap = stride1;
-    auto kern = lce_gemm_kernel<EpiLse<R>>;
-    LCE_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    auto kern = stage1 ? lce_gemm_kernel<EpiLse<R>, true> : lce_gemm_kernel<EpiLse<R>, false>;
+    const int smem = stage1 ? smem1 : SmemLayout::bytes(kblocks, 0);
+    LCE_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     kern<<<G1, kThreads, smem, st>>>(mapH_res, h->mapW_str, g);
     ++launches;
   }
@@ -237,22 +240,23 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
   const int n_a2 = (V + kBM - 1) / kBM, n_b2 = (int)(Tpad / kBN);
   const long long total2 = (long long)n_a2 * n_b2;
   const int G2 = (int)std::min<long long>(h->num_sms, total2);
-  if (max_segments(n_a2, n_b2, G2) > h->gbp_segs)
+  if (2 * max_segments(n_a2, n_b2, G2) > h->gbp_segs)
     return fail(LORA_CE_ESTATE, "pass-2 partial buffer too small");
   mark(h, kPhPass2);
   {
     g.n_a = n_a2;
     g.n_b = n_b2;
     g.Tcap = stride1;
-    auto kern = lce_gemm_kernel<EpiGrad<R>>;
-    LCE_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    auto kern = stage2 ? lce_gemm_kernel<EpiGrad<R>, true> : lce_gemm_kernel<EpiGrad<R>, false>;
+    const int smem = stage2 ? smem2 : SmemLayout::bytes(kblocks, 0);
+    LCE_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     kern<<<G2, kThreads, smem, st>>>(h->mapW_res, mapH_str, g);
     ++launches;
   }
   // 5. dA partials, 6. pack gradient sums
-  const int n_chunks = (T + 255) / 256;
+  const int n_chunks = (T + kDAChunk - 1) / kDAChunk;
   mark(h, kPhDA);
-  lce_dA_partial<R><<<n_chunks, 256, 0, st>>>(T, d, h->h16, h->dU, h->gAp);
+  lce_dA_partial<R><<<n_chunks, 192, 0, st>>>(T, d, h->h16, h->dU, h->gAp);
   ++launches;
   const long long nparam = (long long)d * R + (long long)V * R;
   mark(h, kPhFinalize);
@@ -393,12 +397,12 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
   for (int n_a1 = 1; (long long)n_a1 * kBM < Tcap + kBM; ++n_a1) {
     const long long total = (long long)n_a1 * n_b1;
     const int G = (int)std::min<long long>(h->num_sms, total);
-    p1 = std::max<long long>(p1, (long long)max_segments(n_a1, n_b1, G) * n_a1 * kBM);
+    p1 = std::max<long long>(p1, 2LL * max_segments(n_a1, n_b1, G) * n_a1 * kBM);
   }
   for (int n_b2 = 1; (long long)n_b2 * kBN <= Tcap; ++n_b2) {
     const long long total = (long long)n_a2 * n_b2;
     const int G = (int)std::min<long long>(h->num_sms, total);
-    s2 = std::max(s2, max_segments(n_a2, n_b2, G));
+    s2 = std::max(s2, 2 * max_segments(n_a2, n_b2, G));
   }
   h->p1_cap = p1;
   h->gbp_segs = s2;
@@ -419,7 +423,7 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
   if (!rc) rc = dalloc(&h->z_tgt, (size_t)Tcap);
   if (!rc) rc = dalloc(&h->loss_tok, (size_t)Tcap);
   if (!rc) rc = dalloc(&h->dU, (size_t)Tcap * R);
-  if (!rc) rc = dalloc(&h->gAp, (size_t)(Tcap / 256) * d * R);
+  if (!rc) rc = dalloc(&h->gAp, (size_t)((Tcap + kDAChunk - 1) / kDAChunk) * d * R);
   if (!rc) rc = dalloc(&h->gBp, (size_t)s2 * Vpad * R);
   if (!rc) rc = dalloc(&h->norm_parts, 256);
   if (!rc) rc = dalloc(&h->err, 1);

@@ -39,8 +39,10 @@ constexpr int kBK = 64;                // K elements per 128-byte swizzle row
 constexpr int kStages = 2;             // streamed-operand ring depth
 constexpr int kAKBytes = kBM * kBK * 2;   // 16 KB per resident K-block
 constexpr int kBStageBytes = kBN * kBK * 2;  // 32 KB per streamed stage
-constexpr int kThreads = 192;          // warp0 TMA, warp1 MMA, warps2-5 epilogue
-constexpr int kEpiThreads = 128;
+constexpr int kEpiWarps = 8;           // two per TMEM lane quarter
+constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kThreads = 64 + kEpiThreads;  // warp0 TMA, warp1 MMA, warps 2.. epilogue
+constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kTmemCols = 512;    // two 256-column fp32 accumulators
 constexpr int kMaxKBlocks = 10;        // d <= 640
 
@@ -74,17 +76,47 @@ struct GemmArgs {
   float* gBp;         // [seg][Vpad][R]
 };
 
+// Dynamic shared memory: [resident K-blocks | streamed ring | staged
+// column records (2 x kBN x rec floats, optional) | barriers].
 struct SmemLayout {
-  // offsets from the 1024-aligned base
   static __host__ __device__ constexpr int a_off() { return 0; }
   static __host__ __device__ constexpr int b_off(int kblocks) { return kblocks * kAKBytes; }
-  static __host__ __device__ constexpr int bar_off(int kblocks) {
+  static __host__ __device__ constexpr int rec_off(int kblocks) {
     return b_off(kblocks) + kStages * kBStageBytes;
   }
-  static __host__ __device__ constexpr int bytes(int kblocks) {
-    return 1024 /*align slack*/ + bar_off(kblocks) + 256;
+  static __host__ __device__ constexpr int rec_bytes(int rec_floats) {
+    return 2 * kBN * rec_floats * 4;
+  }
+  static __host__ __device__ constexpr int bar_off(int kblocks, int rec_floats) {
+    return rec_off(kblocks) + rec_bytes(rec_floats);
+  }
+  static __host__ __device__ constexpr int bytes(int kblocks, int rec_floats) {
+    return 1024 /*align slack*/ + bar_off(kblocks, rec_floats) + 256;
   }
 };
+constexpr int kMaxDynSmem = 232448;  // 227 KB opt-in per CTA on sm_100
+
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// N floats (N % 4 == 0) through 16-byte loads from global or shared memory.
+template <int N>
+__device__ __forceinline__ void ld_vec(const float* p, float (&v)[N]) {
+#pragma unroll
+  for (int j = 0; j < N; j += 4) {
+    const float4 x = *reinterpret_cast<const float4*>(p + j);
+    v[j] = x.x; v[j + 1] = x.y; v[j + 2] = x.z; v[j + 3] = x.w;
+  }
+}
+template <int N>
+__device__ __forceinline__ void st_vec(float* p, const float (&v)[N]) {
+#pragma unroll
+  for (int j = 0; j < N; j += 4)
+    *reinterpret_cast<float4*>(p + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+}
 
 // Barrier indices inside the barrier block.
 enum : int {
@@ -110,67 +142,55 @@ __device__ __forceinline__ void mbar_drain_wait(uint64_t* bar, uint32_t parity, 
   }
 }
 
-template <int R>
-__device__ __forceinline__ void load_row(const float* p, float (&v)[R]) {
-  if constexpr (R % 4 == 0) {
-#pragma unroll
-    for (int j = 0; j < R; j += 4) {
-      float4 x = __ldg(reinterpret_cast<const float4*>(p + j));
-      v[j] = x.x; v[j + 1] = x.y; v[j + 2] = x.z; v[j + 3] = x.w;
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < R; ++j) v[j] = __ldg(p + j);
-  }
-}
-
-// Same as load_row, but issued as a volatile load so the compiler does not
-// merge it with an earlier load of the same row (which would keep 32 rows
-// live in registers across two loops).
-template <int R>
-__device__ __forceinline__ void load_row_again(const float* p, float (&v)[R]) {
-  static_assert(R % 4 == 0, "rank must be a multiple of 4");
-#pragma unroll
-  for (int j = 0; j < R; j += 4)
-    asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];"
-                 : "=f"(v[j]), "=f"(v[j + 1]), "=f"(v[j + 2]), "=f"(v[j + 3])
-                 : "l"(p + j));
-}
-
 // ------------------------------------------------------------- epilogues
-// Pass 1: thread owns position t of resident tile a; columns are vocab ids.
+// Each epilogue struct owns one TMEM lane (a resident row) and consumes the
+// columns of the streamed tile in chunks of kCW.  Per column it needs a
+// small record (kRec floats): the mainloop stages the records of a whole
+// tile in shared memory (or points at them in global memory, where the
+// layout is the same).
+
+// Pass 1: the thread owns position t; columns are vocab ids; the record of
+// column v is B[:, v] (R floats).
 template <int R>
 struct EpiLse {
+  static constexpr int kRec = R;
+  static constexpr int kCW = 16;
+  static constexpr float kLazy = 8.0f;   // move the reference max only past this
+  static constexpr float kRedo = 80.0f;  // re-sum a chunk that jumped this far
   int t;
   bool valid;
   int tgt;
   float sU[R];
-  float m, s;
-  float q[R];
+  float m, mL, s;  // reference max, m*log2(e), sum of e^(z-m)
+  float q[R];      // sum of e^(z-m) * B[:, v]
+
+  __device__ static const float* global_recs(const GemmArgs& g, int b) {
+    return g.Bt + (long long)b * kBN * R;
+  }
+  __device__ static void load_rec(const GemmArgs& g, int b, int c, float (&r)[kRec]) {
+    ld_vec<R>(g.Bt + ((long long)b * kBN + c) * R, r);
+  }
 
   __device__ void begin(const GemmArgs& g, int a, int row) {
     t = a * kBM + row;
     valid = t < g.T;
     const float* tk = g.tok + (long long)(valid ? t : 0) * tok_stride(R);
-    load_row<R>(tk, sU);
+    ld_vec<R>(tk, sU);
     tgt = valid ? __float_as_int(tk[R + 2]) : -1;
     m = -INFINITY;
+    mL = -INFINITY;
     s = 0.f;
 #pragma unroll
     for (int j = 0; j < R; ++j) q[j] = 0.f;
   }
 
-  // kCW accumulator columns starting at vocab id v0.  One pass per column:
-  // z = acc + sU.B[:,v], e = exp(z - m), s += e, q += e*B[:,v], with m a
-  // reference point that is only moved (and s, q rescaled) when the
-  // chunk's max exceeds it by more than kLazy; values up to e^kLazy are
-  // summed without loss of precision.  A chunk whose max is more than
-  // kRedo above m (the first chunk, or a jump that could have overflowed)
-  // is summed again against its own max.
-  static constexpr int kCW = R >= 16 ? 8 : 16;
-  static constexpr float kLazy = 8.0f;
-  static constexpr float kRedo = 80.0f;
-  __device__ __forceinline__ void chunk(const GemmArgs& g, int v0, float (&acc)[kCW]) {
+  // One pass per column: z = acc + sU.B[:,v], e = e^(z - m), s += e,
+  // q += e*B[:,v], where m only moves (and s, q are rescaled) when the
+  // chunk max exceeds it by more than kLazy, so terms up to e^kLazy are
+  // summed at full precision; a chunk more than kRedo above m (the first
+  // chunk, or a jump that could have overflowed) is summed again.
+  __device__ __forceinline__ void chunk(const GemmArgs& g, int v0, float (&acc)[kCW],
+                                        const float* recs) {
     if (v0 >= g.V) return;
     const float s_old = s;
     float q_old[R];
@@ -181,40 +201,41 @@ struct EpiLse {
 #pragma unroll
     for (int i = 0; i < kCW; ++i) {
       float bv[R];
-      load_row<R>(g.Bt + (long long)(v0 + i) * R, bv);
+      ld_vec<R>(recs + i * R, bv);
       float z = acc[i];
 #pragma unroll
       for (int j = 0; j < R; ++j) z = fmaf(sU[j], bv[j], z);
       if (tail && v0 + i >= g.V) z = -INFINITY;
       acc[i] = z;
       cm = fmaxf(cm, z);
-      const float e = expf(z - m);
+      const float e = ex2f(fmaf(z, kLog2e, -mL));
       s += e;
 #pragma unroll
       for (int j = 0; j < R; ++j) q[j] = fmaf(e, bv[j], q[j]);
     }
     if (cm > m + kLazy) {
       if (cm - m <= kRedo) {
-        const float f = expf(m - cm);
+        const float f = ex2f((m - cm) * kLog2e);
         s *= f;
 #pragma unroll
         for (int j = 0; j < R; ++j) q[j] *= f;
       } else {
-        const float f = expf(m - cm);  // 0 when m = -inf
+        const float f = ex2f((m - cm) * kLog2e);  // 0 when m = -inf
+        const float cmL = cm * kLog2e;
         s = s_old * f;
 #pragma unroll
         for (int j = 0; j < R; ++j) q[j] = q_old[j] * f;
+        const volatile float* vr = recs;  // fresh loads: keeps the first loop's rows dead
 #pragma unroll
         for (int i = 0; i < kCW; ++i) {
-          float bv[R];
-          load_row_again<R>(g.Bt + (long long)(v0 + i) * R, bv);
-          const float e = expf(acc[i] - cm);
+          const float e = ex2f(fmaf(acc[i], kLog2e, -cmL));
           s += e;
 #pragma unroll
-          for (int j = 0; j < R; ++j) q[j] = fmaf(e, bv[j], q[j]);
+          for (int j = 0; j < R; ++j) q[j] = fmaf(e, vr[i * R + j], q[j]);
         }
       }
       m = cm;
+      mL = cm * kLog2e;
     }
     if (valid && (unsigned)(tgt - v0) < (unsigned)kCW) {
       // Opaque selects keep acc[] in registers (a plain acc[tgt - v0] would
@@ -230,9 +251,9 @@ struct EpiLse {
     }
   }
 
-  __device__ void flush(const GemmArgs& g, int seg) {
+  __device__ void flush(const GemmArgs& g, int slot) {
     if (!valid) return;
-    const long long o = (long long)seg * g.Tcap + t;
+    const long long o = (long long)slot * g.Tcap + t;
     g.p_max[o] = m;
     g.p_sum[o] = s;
 #pragma unroll
@@ -240,60 +261,75 @@ struct EpiLse {
   }
 };
 
-// Pass 2: thread owns vocab row v of resident tile a; columns are positions.
+// Pass 2: the thread owns vocab row v; columns are positions; the record
+// of position t is {sU[0..R), M*log2(e), 1/S, target, 0}.
 template <int R>
 struct EpiGrad {
+  static constexpr int kRec = R + 4;
+  static constexpr int kCW = 16;
   int v;
   bool valid;
   float bv[R];
   float gacc[R];
 
+  __device__ static const float* global_recs(const GemmArgs& g, int b) {
+    return g.tok + (long long)b * kBN * kRec;
+  }
+  __device__ static void load_rec(const GemmArgs& g, int b, int c, float (&r)[kRec]) {
+    ld_vec<kRec>(g.tok + ((long long)b * kBN + c) * kRec, r);
+  }
+
   __device__ void begin(const GemmArgs& g, int a, int row) {
     v = a * kBM + row;
     valid = v < g.V;
-    load_row<R>(g.Bt + (long long)(valid ? v : 0) * R, bv);
+    ld_vec<R>(g.Bt + (long long)(valid ? v : 0) * R, bv);
 #pragma unroll
     for (int j = 0; j < R; ++j) gacc[j] = 0.f;
   }
 
-  static constexpr int kCW = R >= 16 ? 8 : 16;
-  __device__ __forceinline__ void chunk(const GemmArgs& g, int t0, float (&acc)[kCW]) {
+  // p = e^(z - M) / S = 2^(z*log2(e) - M*log2(e)) * (1/S); dl = p - onehot;
+  // dB[v][:] += sU[t][:] * dl.
+  __device__ __forceinline__ void chunk(const GemmArgs& g, int t0, float (&acc)[kCW],
+                                        const float* recs) {
     if (t0 >= g.T) return;  // padded positions contribute nothing
 #pragma unroll
     for (int i = 0; i < kCW; ++i) {
-      const float* tk = g.tok + (long long)(t0 + i) * tok_stride(R);
       float su[R];
-      load_row<R>(tk, su);
-      const float4 mi = __ldg(reinterpret_cast<const float4*>(tk + R));  // M, 1/S, tgt, 0
+      ld_vec<R>(recs + i * kRec, su);
+      const float4 mi = *reinterpret_cast<const float4*>(recs + i * kRec + R);
       float z = acc[i];
 #pragma unroll
       for (int j = 0; j < R; ++j) z = fmaf(bv[j], su[j], z);
-      float p = expf(z - mi.x) * mi.y;
+      float p = ex2f(fmaf(z, kLog2e, -mi.x)) * mi.y;
       if (__float_as_int(mi.z) == v) p -= 1.0f;
 #pragma unroll
       for (int j = 0; j < R; ++j) gacc[j] = fmaf(su[j], p, gacc[j]);
     }
   }
 
-  __device__ void flush(const GemmArgs& g, int seg) {
+  __device__ void flush(const GemmArgs& g, int slot) {
     if (!valid) return;
-    float* o = g.gBp + ((long long)seg * g.Vpad + v) * R;
+    float* o = g.gBp + ((long long)slot * g.Vpad + v) * R;
 #pragma unroll
     for (int j = 0; j < R; ++j) o[j] = gacc[j];
   }
 };
 
 // ------------------------------------------------------------- mainloop
-template <class Epi>
+// kStage: stage the column records of each tile in shared memory (double
+// buffered, prefetched one tile ahead); otherwise read them from global.
+template <class Epi, bool kStage>
 __global__ void __launch_bounds__(kThreads, 1)
     lce_gemm_kernel(const __grid_constant__ CUtensorMap map_res,
                     const __grid_constant__ CUtensorMap map_str, const GemmArgs g) {
+  constexpr int kRecF = kStage ? Epi::kRec : 0;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem + SmemLayout::a_off();
   uint8_t* sB = smem + SmemLayout::b_off(g.kblocks);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SmemLayout::bar_off(g.kblocks));
+  float* srec = reinterpret_cast<float*>(smem + SmemLayout::rec_off(g.kblocks));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SmemLayout::bar_off(g.kblocks, kRecF));
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
 
   const int warp = threadIdx.x >> 5;
@@ -422,44 +458,70 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_drain_wait(&bars[kBarDrain], 0, g.err);
     }
   } else {
-    // ------------------------------------------------ epilogue (warps 2..5)
-    const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+    // ------------------------------------------------ epilogue (warps 2..9)
+    // Warp w reads TMEM lanes 32*(w%4)..+31; warps 2-5 take columns
+    // 0..127 of each tile, warps 6-9 columns 128..255, so every resident
+    // row has two partial states, flushed to slots 2*segment + half.
+    const int e = warp - 2;
+    const int quarter = warp & 3;
+    const int half = e >> 2;
     const int row = quarter * 32 + lane;
+    const int ct = e * 32 + lane;  // the column this thread stages
     const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
+    constexpr int CW = Epi::kCW;
+    constexpr int NCH = (kBN / 2) / CW;
     Epi epi;
     int cur_a = -1;
     long long li = 0;
+    bool failed = false;
+    float rec[Epi::kRec];
+    if (kStage && x_begin < x_end) Epi::load_rec(g, (int)(x_begin % g.n_b), ct, rec);
     for (long long x = x_begin; x < x_end; ++x, ++li) {
       const int a = (int)(x / g.n_b);
       const int b = (int)(x % g.n_b);
       if (a != cur_a) {
-        if (cur_a >= 0) epi.flush(g, blockIdx.x - tile_owner((long long)cur_a * g.n_b, total, G));
+        if (cur_a >= 0 && !failed)
+          epi.flush(g, 2 * (blockIdx.x - tile_owner((long long)cur_a * g.n_b, total, G)) + half);
         epi.begin(g, a, row);
         cur_a = a;
       }
+      const float* recs;
+      if constexpr (kStage) {
+        // Every epilogue thread reaches this barrier once per tile, also
+        // after a failed wait, so the barrier count always matches.
+        float* buf = srec + (li & 1) * (kBN * Epi::kRec);
+        st_vec<Epi::kRec>(buf + ct * Epi::kRec, rec);
+        named_bar_sync(1, kEpiThreads);
+        if (x + 1 < x_end) Epi::load_rec(g, (int)((x + 1) % g.n_b), ct, rec);
+        recs = buf;
+      } else {
+        recs = Epi::global_recs(g, b);
+      }
+      if (failed) continue;
       const int buf = (int)(li & 1);
       const uint32_t use = (uint32_t)(li >> 1);
       if (!mbar_wait(&bars[kBarAccFull + buf], use & 1, g.err, kErrWaitEpilogue)) {
-        cur_a = -1;
-        break;
+        failed = true;
+        continue;
       }
       tc_fence_after();
       {
         // Two register buffers: the TMEM load of chunk c+1 is in flight
         // while chunk c is processed.
-        constexpr int CW = Epi::kCW;
-        constexpr int NCH = kBN / CW;
-        const uint32_t base = lane_addr + (uint32_t)(buf * kBN);
+        const int col0 = half * (kBN / 2);
+        const uint32_t base = lane_addr + (uint32_t)(buf * kBN + col0);
+        const float* rb = recs + col0 * Epi::kRec;
+        const int gcol = b * kBN + col0;
         float ca[CW], cb[CW];
         tmem_ld<CW>(base, ca);
         tmem_ld_wait<CW>(ca);
 #pragma unroll 1
         for (int c = 0; c < NCH; c += 2) {
           tmem_ld<CW>(base + (uint32_t)((c + 1) * CW), cb);
-          epi.chunk(g, b * kBN + c * CW, ca);
+          epi.chunk(g, gcol + c * CW, ca, rb + c * CW * Epi::kRec);
           tmem_ld_wait<CW>(cb);
           if (c + 2 < NCH) tmem_ld<CW>(base + (uint32_t)((c + 2) * CW), ca);
-          epi.chunk(g, b * kBN + (c + 1) * CW, cb);
+          epi.chunk(g, gcol + (c + 1) * CW, cb, rb + (c + 1) * CW * Epi::kRec);
           if (c + 2 < NCH) tmem_ld_wait<CW>(ca);
         }
       }
@@ -467,7 +529,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars[kBarAccEmpty + buf]);
     }
-    if (cur_a >= 0) epi.flush(g, blockIdx.x - tile_owner((long long)cur_a * g.n_b, total, G));
+    if (cur_a >= 0 && !failed)
+      epi.flush(g, 2 * (blockIdx.x - tile_owner((long long)cur_a * g.n_b, total, G)) + half);
   }
 
   tc_fence_before();
@@ -532,9 +595,11 @@ __global__ void lce_prep(const void* __restrict__ H, int dtype, int T, int Tpad,
   }
 }
 
-// Merge the pass-1 partials of each position: M = max, S = sum e^(z-M),
-// Q = sum e^(z-M) B[:,v]; then p_t, loss_t = -log(p_t + 1e-12) and
-// dU_t = s * (Q/S - B[:,target]) (the reference's d_mid, src/train.c:161-168).
+// Merge the pass-1 partials of each position (two slots per CTA segment,
+// one per column half): M = max, S = sum e^(z-M), Q = sum e^(z-M) B[:,v];
+// then p_t, loss_t = -log(p_t + 1e-12) and dU_t = s * (Q/S - B[:,target])
+// (the reference's d_mid, src/train.c:161-168).  The record of t gets
+// M*log2(e) and 1/S for pass 2.
 template <int R>
 __global__ void lce_combine(int T, int n_b1, int G1, long long Tcap, const float* __restrict__ p_max,
                             const float* __restrict__ p_sum, const float* __restrict__ p_q,
@@ -547,15 +612,17 @@ __global__ void lce_combine(int T, int n_b1, int G1, long long Tcap, const float
   const long long total = (long long)((T + kBM - 1) / kBM) * n_b1;
   const int s0 = tile_owner((long long)a * n_b1, total, G1);
   const int s1 = tile_owner((long long)a * n_b1 + n_b1 - 1, total, G1);
-  const int nseg = s1 - s0 + 1;
+  const int nslot = 2 * (s1 - s0 + 1);
   float M = -INFINITY;
-  for (int k = 0; k < nseg; ++k) M = fmaxf(M, p_max[(long long)k * Tcap + t]);
+  for (int k = 0; k < nslot; ++k) M = fmaxf(M, p_max[(long long)k * Tcap + t]);
   float S = 0.f, Q[R];
 #pragma unroll
   for (int j = 0; j < R; ++j) Q[j] = 0.f;
-  for (int k = 0; k < nseg; ++k) {
+  for (int k = 0; k < nslot; ++k) {
     const long long o = (long long)k * Tcap + t;
-    const float f = expf(p_max[o] - M);
+    const float pm = p_max[o];
+    if (pm == -INFINITY) continue;  // a half that saw no valid column
+    const float f = expf(pm - M);
     S = fmaf(p_sum[o], f, S);
 #pragma unroll
     for (int j = 0; j < R; ++j) Q[j] = fmaf(p_q[o * R + j], f, Q[j]);
@@ -565,21 +632,22 @@ __global__ void lce_combine(int T, int n_b1, int G1, long long Tcap, const float
   const int tg = __float_as_int(rec[R + 2]);
   const float pt = expf(z_tgt[t] - M) * inv;
   loss_tok[t] = -logf(pt + 1e-12f);
-  rec[R] = M;
+  rec[R] = M * kLog2e;
   rec[R + 1] = inv;
 #pragma unroll
   for (int j = 0; j < R; ++j) dU[(long long)t * R + j] = scale * (Q[j] * inv - Bt[(long long)tg * R + j]);
 }
 
-// dA partials: gAp[c][i][j] = sum over the 256 positions of chunk c of
-// h16[t][i] * dU[t][j].
+// dA partials: gAp[c][i][j] = sum over the kDAChunk positions of chunk c
+// of h16[t][i] * dU[t][j].
+constexpr int kDAChunk = 64;
 template <int R>
 __global__ void lce_dA_partial(int T, int d, const __half* __restrict__ h16,
                                const float* __restrict__ dU, float* __restrict__ gAp) {
-  __shared__ float sdU[256 * R];
+  __shared__ float sdU[kDAChunk * R];
   const int c = blockIdx.x;
-  const int t0 = c * 256;
-  const int nt = min(256, T - t0);
+  const int t0 = c * kDAChunk;
+  const int nt = min(kDAChunk, T - t0);
   for (int k = threadIdx.x; k < nt * R; k += blockDim.x) sdU[k] = dU[(long long)t0 * R + k];
   __syncthreads();
   for (int i = threadIdx.x; i < d; i += blockDim.x) {
@@ -619,7 +687,7 @@ __global__ void lce_finalize(int T, int d, int V, long long Vpad, int n_chunks,
       const int a = v / kBM;
       const int s0 = tile_owner((long long)a * n_b2, total2, G2);
       const int s1 = tile_owner((long long)a * n_b2 + n_b2 - 1, total2, G2);
-      for (int q = 0; q <= s1 - s0; ++q) s += gBp[(long long)q * Vpad * R + e];
+      for (int q = 0; q < 2 * (s1 - s0 + 1); ++q) s += gBp[(long long)q * Vpad * R + e];
     }
     Gbuf[k] = s;
   }
