@@ -7,6 +7,7 @@
 #include <nccl.h>
 
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -94,6 +95,8 @@ struct lora_ce_handle {
   int R = 0, d = 0, V = 0;
   long long Vpad = 0, Tcap = 0;
   int num_sms = 0;
+  int pair = 2;             // 2: CTA-pair (cta_group::2) GEMM tiles; 1: single-CTA tiles
+  int units1 = 0, units2 = 0;  // co-resident tile-range owners of pass 1 / pass 2
   cudaStream_t stream = nullptr;
   bool poisoned = false;
   bool have_weight = false;
@@ -104,10 +107,10 @@ struct lora_ce_handle {
   __half* W = nullptr;
   __half* h16 = nullptr;
   float* tok = nullptr;
-  float* params = nullptr;  // [A (d*R) | Bt (Vpad*R)]
+  float* params = nullptr;  // [A (d*R) | B (Vpad*R, pair-interleaved: bidx)]
   float* mom1 = nullptr;
   float* mom2 = nullptr;
-  float* Gbuf = nullptr;    // [dA | dB | loss | n_pred]
+  float* Gbuf = nullptr;    // [dA | dB (bidx layout) | loss | n_pred]
   float* gmean = nullptr;
   float* p_max = nullptr;
   float* p_sum = nullptr;
@@ -118,6 +121,7 @@ struct lora_ce_handle {
   float* dU = nullptr;
   float* gAp = nullptr;
   float* gBp = nullptr;
+  unsigned long long* corr_fx = nullptr;  // onehot part of dB, fixed point [Vpad*R]
   int gbp_segs = 0;
   double* norm_parts = nullptr;
   int* err = nullptr;       // device error flag
@@ -146,7 +150,7 @@ int dalloc(T** p, size_t count) {
 void free_all(lora_ce_handle* h) {
   void* ptrs[] = {h->W,     h->h16,   h->tok,      h->params, h->mom1,  h->mom2,
                   h->Gbuf,  h->gmean, h->p_max,    h->p_sum,  h->p_q,   h->z_tgt,
-                  h->loss_tok, h->dU, h->gAp,      h->gBp,    h->norm_parts, h->err,
+                  h->loss_tok, h->dU, h->gAp,      h->gBp,    h->norm_parts, h->err, h->corr_fx,
                   h->d_loss, h->in_H, h->in_tgt};
   for (void* p : ptrs)
     if (p) cudaFree(p);
@@ -164,6 +168,64 @@ int check_cfg(const lora_ce_config* c) {
       !(c->beta2 >= 0.f && c->beta2 < 1.f) || !(c->weight_decay >= 0.f) ||
       !(c->clip_norm >= 0.f) || !std::isfinite(c->scale))
     return fail(LORA_CE_EINVAL, "bad optimizer hyper-parameters");
+  return 0;
+}
+
+template <class Epi>
+void (*gemm_kernel(int pair, int kblocks, int* smem_out))(const CUtensorMap, const CUtensorMap,
+                                                          const GemmArgs) {
+  const int smem_staged = SmemLayout::bytes(kblocks, Epi::kRec);
+  const bool staged = smem_staged <= kMaxDynSmem;
+  *smem_out = staged ? smem_staged : SmemLayout::bytes(kblocks, 0);
+  if (pair == 2) return staged ? lce_gemm_kernel<Epi, true, 2> : lce_gemm_kernel<Epi, false, 2>;
+  return staged ? lce_gemm_kernel<Epi, true, 1> : lce_gemm_kernel<Epi, false, 1>;
+}
+
+// How many tile-range owners (CTAs, or 2-CTA clusters) of this GEMM pass
+// can be resident at once: the persistent split assumes all of them are.
+template <class Epi>
+int resident_units(int pair, int kblocks, int num_sms) {
+  int smem = 0;
+  auto kern = gemm_kernel<Epi>(pair, kblocks, &smem);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return 0;
+  if (pair == 1) return num_sms;
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3((unsigned)num_sms);
+  lc.blockDim = dim3(kThreads);
+  lc.dynamicSmemBytes = (size_t)smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &lc) != cudaSuccess) return 0;
+  return n;
+}
+
+// Launch one GEMM pass: `units` tile-range owners (CTAs, or 2-CTA clusters).
+template <class Epi>
+int launch_gemm(const CUtensorMap& map_res, const CUtensorMap& map_str, const GemmArgs& g,
+                int units, int pair, int kblocks, cudaStream_t st) {
+  int smem = 0;
+  auto kern = gemm_kernel<Epi>(pair, kblocks, &smem);
+  LCE_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3((unsigned)(units * pair));
+  lc.blockDim = dim3(kThreads);
+  lc.dynamicSmemBytes = (size_t)smem;
+  lc.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)pair;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  lc.attrs = attr;
+  lc.numAttrs = pair == 2 ? 1 : 0;
+  LCE_CUDA(cudaLaunchKernelEx(&lc, kern, map_res, map_str, g));
   return 0;
 }
 
@@ -194,16 +256,15 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
                                             dtg, V, h->h16, h->tok, h->err);
     ++launches;
   }
-  const int smem1 = SmemLayout::bytes(kblocks, EpiLse<R>::kRec);
-  const int smem2 = SmemLayout::bytes(kblocks, EpiGrad<R>::kRec);
-  const bool stage1 = smem1 <= kMaxDynSmem, stage2 = smem2 <= kMaxDynSmem;
+  const int pair = h->pair;
+  const int res_rows = kBM * pair;
   mark(h, kPhPass1);
   // 2. pass 1: per-position max / sum / q over the vocabulary
-  const int n_a1 = (T + kBM - 1) / kBM, n_b1 = (int)(h->Vpad / kBN);
+  const int n_a1 = (T + res_rows - 1) / res_rows, n_b1 = (int)(h->Vpad / kBN);
   const long long total1 = (long long)n_a1 * n_b1;
-  const int G1 = (int)std::min<long long>(h->num_sms, total1);
+  const int G1 = (int)std::min<long long>(h->units1, total1);
   const int seg1 = 2 * max_segments(n_a1, n_b1, G1);
-  const long long stride1 = (long long)n_a1 * kBM;
+  const long long stride1 = (long long)n_a1 * res_rows;
   if ((long long)seg1 * stride1 > h->p1_cap)
     return fail(LORA_CE_ESTATE, "pass-1 partial buffer too small");
   GemmArgs g{};
@@ -220,37 +281,38 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
   g.p_q = h->p_q;
   g.z_tgt = h->z_tgt;
   g.gBp = h->gBp;
+  g.n_a = n_a1;
+  g.n_b = n_b1;
+  g.Tcap = stride1;
   {
-    g.n_a = n_a1;
-    g.n_b = n_b1;
-    g.Tcap = stride1;
-    auto kern = stage1 ? lce_gemm_kernel<EpiLse<R>, true> : lce_gemm_kernel<EpiLse<R>, false>;
-    const int smem = stage1 ? smem1 : SmemLayout::bytes(kblocks, 0);
-    LCE_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    kern<<<G1, kThreads, smem, st>>>(mapH_res, h->mapW_str, g);
+    int rc = launch_gemm<EpiLse<R>>(mapH_res, pair == 2 ? h->mapW_res : h->mapW_str, g, G1, pair,
+                                    kblocks, st);
+    if (rc) return rc;
     ++launches;
   }
   // 3. merge partials -> M, 1/S, loss_t, dU
   mark(h, kPhCombine);
-  lce_combine<R><<<(T + 255) / 256, 256, 0, st>>>(T, n_b1, G1, stride1, h->p_max, h->p_sum,
+  lce_combine<R><<<(T + 255) / 256, 256, 0, st>>>(T, res_rows, n_b1, G1, stride1, h->p_max,
+                                                  h->p_sum,
                                                   h->p_q, h->z_tgt, g.Bt, h->cfg.scale, h->tok,
                                                   h->dU, h->loss_tok);
   ++launches;
+  // onehot part of dB (order-independent fixed-point sums)
+  lce_onehot<R><<<(T + 255) / 256, 256, 0, st>>>(T, h->tok, h->corr_fx, h->err);
+  ++launches;
   // 4. pass 2: dB per vocab row
-  const int n_a2 = (V + kBM - 1) / kBM, n_b2 = (int)(Tpad / kBN);
+  const int n_a2 = (V + res_rows - 1) / res_rows, n_b2 = (int)(Tpad / kBN);
   const long long total2 = (long long)n_a2 * n_b2;
-  const int G2 = (int)std::min<long long>(h->num_sms, total2);
+  const int G2 = (int)std::min<long long>(h->units2, total2);
   if (2 * max_segments(n_a2, n_b2, G2) > h->gbp_segs)
     return fail(LORA_CE_ESTATE, "pass-2 partial buffer too small");
   mark(h, kPhPass2);
   {
     g.n_a = n_a2;
     g.n_b = n_b2;
-    g.Tcap = stride1;
-    auto kern = stage2 ? lce_gemm_kernel<EpiGrad<R>, true> : lce_gemm_kernel<EpiGrad<R>, false>;
-    const int smem = stage2 ? smem2 : SmemLayout::bytes(kblocks, 0);
-    LCE_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    kern<<<G2, kThreads, smem, st>>>(h->mapW_res, mapH_str, g);
+    int rc = launch_gemm<EpiGrad<R>>(h->mapW_res, pair == 2 ? mapH_res : mapH_str, g, G2, pair,
+                                     kblocks, st);
+    if (rc) return rc;
     ++launches;
   }
   // 5. dA partials, 6. pack gradient sums
@@ -258,12 +320,12 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
   mark(h, kPhDA);
   lce_dA_partial<R><<<n_chunks, 192, 0, st>>>(T, d, h->h16, h->dU, h->gAp);
   ++launches;
-  const long long nparam = (long long)d * R + (long long)V * R;
+  const long long nparam = (long long)d * R + h->Vpad * R;
   mark(h, kPhFinalize);
   {
     const int blocks = (int)std::min<long long>((nparam + 255) / 256, 8LL * h->num_sms);
-    lce_finalize<R><<<blocks, 256, 0, st>>>(T, d, V, h->Vpad, n_chunks, h->gAp, n_b2, G2, h->gBp,
-                                            h->loss_tok, h->Gbuf);
+    lce_finalize<R><<<blocks, 256, 0, st>>>(T, d, V, h->Vpad, n_chunks, h->gAp, res_rows, n_b2, G2,
+                                            h->gBp, h->corr_fx, h->loss_tok, h->Gbuf);
     ++launches;
   }
   // 7. data-parallel sum over ranks
@@ -339,7 +401,9 @@ int check_device_error(lora_ce_handle* h) {
     h->poisoned = true;
     char buf[96];
     snprintf(buf, sizeof buf, "device error %d (%s)", e,
-             e == kErrTarget ? "target id out of range" : "bounded wait expired");
+             e == kErrTarget  ? "target id out of range"
+             : e == kErrRange ? "s*U out of the supported range"
+                              : "bounded wait expired");
     return fail(LORA_CE_EDEVICE, buf);
   }
   return 0;
@@ -388,26 +452,49 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
   h->Vpad = round_up(cfg->vocab, kBN);
   h->Tcap = round_up(cfg->max_tokens, kBN);
   h->num_sms = prop.multiProcessorCount;
+  {
+    const char* e = getenv("LORA_CE_CTA_PAIR");  // "1": single-CTA tiles (comparison runs)
+    h->pair = (e && e[0] == '1') ? 1 : 2;
+  }
   const int R = h->R, d = h->d;
+  const int res_rows = kBM * h->pair;
+  {
+    const int kb = d / kBK;
+    int u1 = 0, u2 = 0;
+    switch (R) {
+      case 4: u1 = resident_units<EpiLse<4>>(h->pair, kb, h->num_sms);
+              u2 = resident_units<EpiGrad<4>>(h->pair, kb, h->num_sms); break;
+      case 8: u1 = resident_units<EpiLse<8>>(h->pair, kb, h->num_sms);
+              u2 = resident_units<EpiGrad<8>>(h->pair, kb, h->num_sms); break;
+      default: u1 = resident_units<EpiLse<16>>(h->pair, kb, h->num_sms);
+               u2 = resident_units<EpiGrad<16>>(h->pair, kb, h->num_sms); break;
+    }
+    if (u1 < 1 || u2 < 1) {
+      delete h;
+      return fail(LORA_CE_ECUDA, "GEMM kernels cannot be made resident on this device");
+    }
+    h->units1 = u1;
+    h->units2 = u2;
+  }
   const long long V = h->V, Vpad = h->Vpad, Tcap = h->Tcap;
   // worst-case partial-buffer sizes over every T <= max_tokens
   long long p1 = 0;
   int s2 = 1;
-  const int n_b1 = (int)(Vpad / kBN), n_a2 = (int)((V + kBM - 1) / kBM);
-  for (int n_a1 = 1; (long long)n_a1 * kBM < Tcap + kBM; ++n_a1) {
+  const int n_b1 = (int)(Vpad / kBN), n_a2 = (int)((V + res_rows - 1) / res_rows);
+  for (int n_a1 = 1; (long long)n_a1 * res_rows < Tcap + res_rows; ++n_a1) {
     const long long total = (long long)n_a1 * n_b1;
-    const int G = (int)std::min<long long>(h->num_sms, total);
-    p1 = std::max<long long>(p1, 2LL * max_segments(n_a1, n_b1, G) * n_a1 * kBM);
+    const int G = (int)std::min<long long>(h->units1, total);
+    p1 = std::max<long long>(p1, 2LL * max_segments(n_a1, n_b1, G) * n_a1 * res_rows);
   }
   for (int n_b2 = 1; (long long)n_b2 * kBN <= Tcap; ++n_b2) {
     const long long total = (long long)n_a2 * n_b2;
-    const int G = (int)std::min<long long>(h->num_sms, total);
+    const int G = (int)std::min<long long>(h->units2, total);
     s2 = std::max(s2, 2 * max_segments(n_a2, n_b2, G));
   }
   h->p1_cap = p1;
   h->gbp_segs = s2;
   const long long nparam_pad = (long long)d * R + Vpad * R;
-  const long long nparam = (long long)d * R + V * R;
+  const long long nparam = nparam_pad;
   rc = 0;
   if (!rc) rc = dalloc(&h->W, (size_t)V * d);
   if (!rc) rc = dalloc(&h->h16, (size_t)Tcap * d);
@@ -425,6 +512,7 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
   if (!rc) rc = dalloc(&h->dU, (size_t)Tcap * R);
   if (!rc) rc = dalloc(&h->gAp, (size_t)((Tcap + kDAChunk - 1) / kDAChunk) * d * R);
   if (!rc) rc = dalloc(&h->gBp, (size_t)s2 * Vpad * R);
+  if (!rc) rc = dalloc(&h->corr_fx, (size_t)Vpad * R);
   if (!rc) rc = dalloc(&h->norm_parts, 256);
   if (!rc) rc = dalloc(&h->err, 1);
   if (!rc) rc = dalloc(&h->d_loss, 2);
@@ -472,7 +560,7 @@ int lora_ce_set_adapter(lora_ce_handle* h, const float* A, const float* B, int32
   const int R = h->R, d = h->d, V = h->V;
   std::vector<float> Bt((size_t)h->Vpad * R, 0.f);
   for (int j = 0; j < R; ++j)
-    for (int v = 0; v < V; ++v) Bt[(size_t)v * R + j] = B[(size_t)j * V + v];
+    for (int v = 0; v < V; ++v) Bt[(size_t)bidx(v, j, R)] = B[(size_t)j * V + v];
   const size_t nA = (size_t)d * R;
   LCE_CUDA(cudaMemcpyAsync(h->params, A, nA * 4, cudaMemcpyHostToDevice, h->stream));
   LCE_CUDA(cudaMemcpyAsync(h->params + nA, Bt.data(), Bt.size() * 4, cudaMemcpyHostToDevice,
@@ -493,11 +581,11 @@ int lora_ce_get_adapter(lora_ce_handle* h, float* A, float* B, int32_t* step) {
   const int R = h->R, d = h->d, V = h->V;
   if (A) LCE_CUDA(cudaMemcpy(A, h->params, (size_t)d * R * 4, cudaMemcpyDeviceToHost));
   if (B) {
-    std::vector<float> Bt((size_t)V * R);
+    std::vector<float> Bt((size_t)h->Vpad * R);
     LCE_CUDA(cudaMemcpy(Bt.data(), h->params + (size_t)d * R, Bt.size() * 4,
                         cudaMemcpyDeviceToHost));
     for (int j = 0; j < R; ++j)
-      for (int v = 0; v < V; ++v) B[(size_t)j * V + v] = Bt[(size_t)v * R + j];
+      for (int v = 0; v < V; ++v) B[(size_t)j * V + v] = Bt[(size_t)bidx(v, j, R)];
   }
   if (step) *step = h->step;
   return 0;
@@ -511,12 +599,12 @@ int lora_ce_get_grads(lora_ce_handle* h, float* gA, float* gB, float* loss_sum, 
   const int R = h->R, d = h->d, V = h->V;
   if (gA) LCE_CUDA(cudaMemcpy(gA, h->gmean, (size_t)d * R * 4, cudaMemcpyDeviceToHost));
   if (gB) {
-    std::vector<float> t((size_t)V * R);
+    std::vector<float> t((size_t)h->Vpad * R);
     LCE_CUDA(cudaMemcpy(t.data(), h->gmean + (size_t)d * R, t.size() * 4, cudaMemcpyDeviceToHost));
     for (int j = 0; j < R; ++j)
-      for (int v = 0; v < V; ++v) gB[(size_t)j * V + v] = t[(size_t)v * R + j];
+      for (int v = 0; v < V; ++v) gB[(size_t)j * V + v] = t[(size_t)bidx(v, j, R)];
   }
-  const long long nparam = (long long)d * R + (long long)V * R;
+  const long long nparam = (long long)d * R + h->Vpad * R;
   float tail[2];
   LCE_CUDA(cudaMemcpy(tail, h->Gbuf + nparam, 8, cudaMemcpyDeviceToHost));
   if (loss_sum) *loss_sum = tail[0];
@@ -564,8 +652,9 @@ int lora_ce_step(lora_ce_handle* h, const void* H, int32_t dtype, int32_t T,
   memcpy(&e, &res[1], 4);
   if (e != 0) {
     h->poisoned = true;
-    return fail(LORA_CE_EDEVICE, e == kErrTarget ? "target id out of range"
-                                                 : "device pipeline error (bounded wait expired)");
+    return fail(LORA_CE_EDEVICE, e == kErrTarget  ? "target id out of range"
+                                 : e == kErrRange ? "s*U out of the supported range"
+                                                  : "device pipeline error (bounded wait expired)");
   }
   if (loss_out) *loss_out = res[0];
   return 0;

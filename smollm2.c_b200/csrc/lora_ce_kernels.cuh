@@ -36,17 +36,37 @@ namespace lce {
 constexpr int kBM = 128;               // resident rows per tile (TMEM lanes)
 constexpr int kBN = 256;               // streamed rows per tile (TMEM columns)
 constexpr int kBK = 64;                // K elements per 128-byte swizzle row
-constexpr int kStages = 2;             // streamed-operand ring depth
+constexpr int kRingBytes = 65536;      // streamed-operand ring (2 x 32 KB, or 4 x 16 KB per CTA in pairs)
+constexpr int kMaxStages = 4;
 constexpr int kAKBytes = kBM * kBK * 2;   // 16 KB per resident K-block
-constexpr int kBStageBytes = kBN * kBK * 2;  // 32 KB per streamed stage
+// Per-CTA streamed rows per tile and stage geometry for 1-CTA (kPair 1) and
+// CTA-pair (kPair 2, cta_group::2) tiles.
+__host__ __device__ constexpr int str_rows(int pair) { return kBN / pair; }
+__host__ __device__ constexpr int stage_bytes(int pair) { return str_rows(pair) * kBK * 2; }
+__host__ __device__ constexpr int num_stages(int pair) { return kRingBytes / stage_bytes(pair); }
 constexpr int kEpiWarps = 8;           // two per TMEM lane quarter
 constexpr int kEpiThreads = kEpiWarps * 32;
-constexpr int kThreads = 64 + kEpiThreads;  // warp0 TMA, warp1 MMA, warps 2.. epilogue
+constexpr int kRecWarp = 2 + kEpiWarps;  // per-tile column-record loader
+// warp 0 TMA producer, warp 1 MMA issuer, warps 2..9 epilogue, warp 10 records
+constexpr int kThreads = 32 * (kRecWarp + 1);
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kTmemCols = 512;    // two 256-column fp32 accumulators
 constexpr int kMaxKBlocks = 10;        // d <= 640
 
+// Pair-interleaved layouts.  B (vocab-major) and the per-position records
+// keep the same field of two consecutive columns side by side, so one
+// 16-byte load yields float2 operands for a column pair:
+//   B:   bidx(v, j)    = (v/2)*2R + 2j + v%2               (j < R)
+//   tok: tidx(t, f)    = (t/2)*2(R+4) + 2f + t%2, fields f:
+//        0..R-1 s*U[t][:], R: -M*log2(e), R+1: 1/S, R+2: target (int bits), R+3: 0
+// A whole 256-column tile is one contiguous block in either layout.
 __host__ __device__ constexpr int tok_stride(int R) { return R + 4; }
+__host__ __device__ inline long long bidx(long long v, int j, int R) {
+  return (v >> 1) * 2 * R + 2 * j + (v & 1);
+}
+__host__ __device__ inline long long tidx(long long t, int f, int R) {
+  return (t >> 1) * 2 * (R + 4) + 2 * f + (t & 1);
+}
 
 // CTA c of G processes the linear tile range [start(c), start(c+1)),
 // start(c) = floor(c * total / G); tiles are numbered a * n_b + b so the
@@ -82,8 +102,9 @@ struct SmemLayout {
   static __host__ __device__ constexpr int a_off() { return 0; }
   static __host__ __device__ constexpr int b_off(int kblocks) { return kblocks * kAKBytes; }
   static __host__ __device__ constexpr int rec_off(int kblocks) {
-    return b_off(kblocks) + kStages * kBStageBytes;
+    return b_off(kblocks) + kRingBytes;
   }
+  // two record buffers
   static __host__ __device__ constexpr int rec_bytes(int rec_floats) {
     return 2 * kBN * rec_floats * 4;
   }
@@ -120,14 +141,16 @@ __device__ __forceinline__ void st_vec(float* p, const float (&v)[N]) {
 
 // Barrier indices inside the barrier block.
 enum : int {
-  kBarFull = 0,                    // [kStages] stage loaded
-  kBarEmpty = kBarFull + kStages,  // [kStages] stage consumed by MMA
-  kBarAFull = kBarEmpty + kStages, // resident tile loaded
+  kBarFull = 0,                       // [kMaxStages] stage loaded
+  kBarEmpty = kBarFull + kMaxStages,  // [kMaxStages] stage consumed by MMA
+  kBarAFull = kBarEmpty + kMaxStages, // resident tile loaded
   kBarAEmpty,                      // resident tile no longer read
   kBarAccFull,                     // [2] accumulator ready
   kBarAccEmpty = kBarAccFull + 2,  // [2] accumulator drained
   kBarDrain = kBarAccEmpty + 2,    // end-of-kernel MMA drain
-  kNumBars
+  kBarRecFull,                     // [2] tile records loaded
+  kBarRecEmpty = kBarRecFull + 2,  // [2] tile records no longer read
+  kNumBars = kBarRecEmpty + 2
 };
 
 // Wait that ignores the shared error flag (used only to drain copies and
@@ -149,89 +172,104 @@ __device__ __forceinline__ void mbar_drain_wait(uint64_t* bar, uint32_t parity, 
 // tile in shared memory (or points at them in global memory, where the
 // layout is the same).
 
-// Pass 1: the thread owns position t; columns are vocab ids; the record of
-// column v is B[:, v] (R floats).
+__device__ __forceinline__ float2 f2(float x, float y) { return make_float2(x, y); }
+
+// Pass 1: the thread owns position t; columns are vocab ids; the records of
+// a column pair are B[:, v], B[:, v+1] interleaved (2R floats).
 template <int R>
 struct EpiLse {
-  static constexpr int kRec = R;
-  static constexpr int kCW = 16;
+  static constexpr int kRec = R;  // floats per column
+  static constexpr int kCW = R >= 16 ? 8 : 16;
   static constexpr float kLazy = 8.0f;   // move the reference max only past this
   static constexpr float kRedo = 80.0f;  // re-sum a chunk that jumped this far
   int t;
   bool valid;
   int tgt;
-  float sU[R];
-  float m, mL, s;  // reference max, m*log2(e), sum of e^(z-m)
-  float q[R];      // sum of e^(z-m) * B[:, v]
+  float2 sU2[R];  // (s*U[t][j], s*U[t][j])
+  float m, mL;    // reference max, m*log2(e)
+  float2 s2;      // sum of e^(z-m) over even / odd columns
+  float2 q2[R];   // sum of e^(z-m) * B[j][v] over even / odd columns
 
   __device__ static const float* global_recs(const GemmArgs& g, int b) {
     return g.Bt + (long long)b * kBN * R;
   }
-  __device__ static void load_rec(const GemmArgs& g, int b, int c, float (&r)[kRec]) {
-    ld_vec<R>(g.Bt + ((long long)b * kBN + c) * R, r);
-  }
+  __device__ static int limit(const GemmArgs& g) { return g.V; }
 
-  __device__ void begin(const GemmArgs& g, int a, int row) {
-    t = a * kBM + row;
+  __device__ void begin(const GemmArgs& g, int abs_row) {
+    t = abs_row;
     valid = t < g.T;
-    const float* tk = g.tok + (long long)(valid ? t : 0) * tok_stride(R);
-    ld_vec<R>(tk, sU);
-    tgt = valid ? __float_as_int(tk[R + 2]) : -1;
+    const long long tt = valid ? t : 0;
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+      const float u = g.tok[tidx(tt, j, R)];
+      sU2[j] = f2(u, u);
+    }
+    tgt = valid ? __float_as_int(g.tok[tidx(tt, R + 2, R)]) : -1;
     m = -INFINITY;
     mL = -INFINITY;
-    s = 0.f;
+    s2 = f2(0.f, 0.f);
 #pragma unroll
-    for (int j = 0; j < R; ++j) q[j] = 0.f;
+    for (int j = 0; j < R; ++j) q2[j] = f2(0.f, 0.f);
   }
 
-  // One pass per column: z = acc + sU.B[:,v], e = e^(z - m), s += e,
-  // q += e*B[:,v], where m only moves (and s, q are rescaled) when the
-  // chunk max exceeds it by more than kLazy, so terms up to e^kLazy are
-  // summed at full precision; a chunk more than kRedo above m (the first
-  // chunk, or a jump that could have overflowed) is summed again.
+  // Per column: z = acc + sU.B[:,v], e = e^(z - m), s += e, q += e*B[:,v],
+  // two columns per f32x2 instruction.  m only moves (and s, q are
+  // rescaled) when the chunk max exceeds it by more than kLazy, so terms up
+  // to e^kLazy are summed at full precision; a chunk more than kRedo above
+  // m (the first chunk, or a jump that could have overflowed) is summed
+  // again against its own max.
+  template <bool kTail>
   __device__ __forceinline__ void chunk(const GemmArgs& g, int v0, float (&acc)[kCW],
                                         const float* recs) {
-    if (v0 >= g.V) return;
-    const float s_old = s;
-    float q_old[R];
+    if (kTail && v0 >= g.V) return;
+    const float2 s_old = s2;
+    float2 q_old[R];
 #pragma unroll
-    for (int j = 0; j < R; ++j) q_old[j] = q[j];
-    const bool tail = v0 + kCW > g.V;
+    for (int j = 0; j < R; ++j) q_old[j] = q2[j];
+    const float2 L2 = f2(kLog2e, kLog2e);
+    const float2 nmL2 = f2(-mL, -mL);
     float cm = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < kCW; ++i) {
-      float bv[R];
-      ld_vec<R>(recs + i * R, bv);
-      float z = acc[i];
+    for (int p = 0; p < kCW / 2; ++p) {
+      float b[2 * R];
+      ld_vec<2 * R>(recs + p * 2 * R, b);
+      float2 z2 = f2(acc[2 * p], acc[2 * p + 1]);
 #pragma unroll
-      for (int j = 0; j < R; ++j) z = fmaf(sU[j], bv[j], z);
-      if (tail && v0 + i >= g.V) z = -INFINITY;
-      acc[i] = z;
-      cm = fmaxf(cm, z);
-      const float e = ex2f(fmaf(z, kLog2e, -mL));
-      s += e;
+      for (int j = 0; j < R; ++j) z2 = __ffma2_rn(sU2[j], f2(b[2 * j], b[2 * j + 1]), z2);
+      if (kTail) {
+        if (v0 + 2 * p >= g.V) z2.x = -INFINITY;
+        if (v0 + 2 * p + 1 >= g.V) z2.y = -INFINITY;
+      }
+      acc[2 * p] = z2.x;
+      acc[2 * p + 1] = z2.y;
+      cm = fmaxf(cm, fmaxf(z2.x, z2.y));
+      const float2 x2 = __ffma2_rn(z2, L2, nmL2);
+      const float2 e2 = f2(ex2f(x2.x), ex2f(x2.y));
+      s2 = __fadd2_rn(s2, e2);
 #pragma unroll
-      for (int j = 0; j < R; ++j) q[j] = fmaf(e, bv[j], q[j]);
+      for (int j = 0; j < R; ++j) q2[j] = __ffma2_rn(e2, f2(b[2 * j], b[2 * j + 1]), q2[j]);
     }
     if (cm > m + kLazy) {
+      const float f = ex2f((m - cm) * kLog2e);  // 0 when m = -inf
+      const float2 ff = f2(f, f);
       if (cm - m <= kRedo) {
-        const float f = ex2f((m - cm) * kLog2e);
-        s *= f;
+        s2 = __fmul2_rn(s2, ff);
 #pragma unroll
-        for (int j = 0; j < R; ++j) q[j] *= f;
+        for (int j = 0; j < R; ++j) q2[j] = __fmul2_rn(q2[j], ff);
       } else {
-        const float f = ex2f((m - cm) * kLog2e);  // 0 when m = -inf
-        const float cmL = cm * kLog2e;
-        s = s_old * f;
+        s2 = __fmul2_rn(s_old, ff);
 #pragma unroll
-        for (int j = 0; j < R; ++j) q[j] = q_old[j] * f;
+        for (int j = 0; j < R; ++j) q2[j] = __fmul2_rn(q_old[j], ff);
+        const float2 ncmL2 = f2(-cm * kLog2e, -cm * kLog2e);
         const volatile float* vr = recs;  // fresh loads: keeps the first loop's rows dead
 #pragma unroll
-        for (int i = 0; i < kCW; ++i) {
-          const float e = ex2f(fmaf(acc[i], kLog2e, -cmL));
-          s += e;
+        for (int p = 0; p < kCW / 2; ++p) {
+          const float2 x2 = __ffma2_rn(f2(acc[2 * p], acc[2 * p + 1]), L2, ncmL2);
+          const float2 e2 = f2(ex2f(x2.x), ex2f(x2.y));
+          s2 = __fadd2_rn(s2, e2);
 #pragma unroll
-          for (int j = 0; j < R; ++j) q[j] = fmaf(e, vr[i * R + j], q[j]);
+          for (int j = 0; j < R; ++j)
+            q2[j] = __ffma2_rn(e2, f2(vr[p * 2 * R + 2 * j], vr[p * 2 * R + 2 * j + 1]), q2[j]);
         }
       }
       m = cm;
@@ -255,77 +293,106 @@ struct EpiLse {
     if (!valid) return;
     const long long o = (long long)slot * g.Tcap + t;
     g.p_max[o] = m;
-    g.p_sum[o] = s;
+    g.p_sum[o] = s2.x + s2.y;
 #pragma unroll
-    for (int j = 0; j < R; ++j) g.p_q[o * R + j] = q[j];
+    for (int j = 0; j < R; ++j) g.p_q[o * R + j] = q2[j].x + q2[j].y;
   }
 };
 
-// Pass 2: the thread owns vocab row v; columns are positions; the record
-// of position t is {sU[0..R), M*log2(e), 1/S, target, 0}.
+// Pass 2: the thread owns vocab row v; columns are positions; the records
+// of a position pair are tok[] fields interleaved (2(R+4) floats).  This
+// pass accumulates the p part of dl = p - onehot; lce_onehot adds the
+// onehot part.
 template <int R>
 struct EpiGrad {
   static constexpr int kRec = R + 4;
-  static constexpr int kCW = 16;
+  static constexpr int kCW = R >= 16 ? 8 : 16;
   int v;
   bool valid;
-  float bv[R];
-  float gacc[R];
+  float2 bv2[R];  // (B[j][v], B[j][v])
+  float2 g2[R];   // dB[v][j] over even / odd positions
 
   __device__ static const float* global_recs(const GemmArgs& g, int b) {
     return g.tok + (long long)b * kBN * kRec;
   }
-  __device__ static void load_rec(const GemmArgs& g, int b, int c, float (&r)[kRec]) {
-    ld_vec<kRec>(g.tok + ((long long)b * kBN + c) * kRec, r);
-  }
+  __device__ static int limit(const GemmArgs& g) { return g.T; }
 
-  __device__ void begin(const GemmArgs& g, int a, int row) {
-    v = a * kBM + row;
+  __device__ void begin(const GemmArgs& g, int abs_row) {
+    v = abs_row;
     valid = v < g.V;
-    ld_vec<R>(g.Bt + (long long)(valid ? v : 0) * R, bv);
+    const long long vv = valid ? v : 0;
 #pragma unroll
-    for (int j = 0; j < R; ++j) gacc[j] = 0.f;
+    for (int j = 0; j < R; ++j) {
+      const float b = g.Bt[bidx(vv, j, R)];
+      bv2[j] = f2(b, b);
+      g2[j] = f2(0.f, 0.f);
+    }
   }
 
-  // p = e^(z - M) / S = 2^(z*log2(e) - M*log2(e)) * (1/S); dl = p - onehot;
-  // dB[v][:] += sU[t][:] * dl.
+  // p = e^(z - M) / S = 2^(z*log2(e) - M*log2(e)) * (1/S); dB[v][:] += sU * p.
+  template <bool kTail>
   __device__ __forceinline__ void chunk(const GemmArgs& g, int t0, float (&acc)[kCW],
                                         const float* recs) {
-    if (t0 >= g.T) return;  // padded positions contribute nothing
+    if (kTail && t0 >= g.T) return;  // fully padded chunk (zero records) adds nothing
+    const float2 L2 = f2(kLog2e, kLog2e);
 #pragma unroll
-    for (int i = 0; i < kCW; ++i) {
-      float su[R];
-      ld_vec<R>(recs + i * kRec, su);
-      const float4 mi = *reinterpret_cast<const float4*>(recs + i * kRec + R);
-      float z = acc[i];
+    for (int p = 0; p < kCW / 2; ++p) {
+      const float* rp = recs + p * 2 * kRec;
+      float su[2 * R];
+      ld_vec<2 * R>(rp, su);
+      const float4 mi = *reinterpret_cast<const float4*>(rp + 2 * R);  // -ML pair, 1/S pair
+      float2 z2 = f2(acc[2 * p], acc[2 * p + 1]);
 #pragma unroll
-      for (int j = 0; j < R; ++j) z = fmaf(bv[j], su[j], z);
-      float p = ex2f(fmaf(z, kLog2e, -mi.x)) * mi.y;
-      if (__float_as_int(mi.z) == v) p -= 1.0f;
+      for (int j = 0; j < R; ++j) z2 = __ffma2_rn(bv2[j], f2(su[2 * j], su[2 * j + 1]), z2);
+      const float2 x2 = __ffma2_rn(z2, L2, f2(mi.x, mi.y));
+      const float2 p2 = __fmul2_rn(f2(ex2f(x2.x), ex2f(x2.y)), f2(mi.z, mi.w));
 #pragma unroll
-      for (int j = 0; j < R; ++j) gacc[j] = fmaf(su[j], p, gacc[j]);
+      for (int j = 0; j < R; ++j) g2[j] = __ffma2_rn(f2(su[2 * j], su[2 * j + 1]), p2, g2[j]);
     }
   }
 
   __device__ void flush(const GemmArgs& g, int slot) {
     if (!valid) return;
-    float* o = g.gBp + ((long long)slot * g.Vpad + v) * R;
+    float* o = g.gBp + (long long)slot * g.Vpad * R;
 #pragma unroll
-    for (int j = 0; j < R; ++j) o[j] = gacc[j];
+    for (int j = 0; j < R; ++j) o[bidx(v, j, R)] = g2[j].x + g2[j].y;
   }
 };
 
+// Chunk dispatch: the masked variant only for tiles that reach past the
+// last column.
+template <class Epi>
+__device__ __forceinline__ void run_chunk(Epi& epi, const GemmArgs& g, bool tail, int col,
+                                          float (&acc)[Epi::kCW], const float* recs) {
+  if (tail) epi.template chunk<true>(g, col, acc, recs);
+  else epi.template chunk<false>(g, col, acc, recs);
+}
+
 // ------------------------------------------------------------- mainloop
+// One CTA (kPair 1) or a CTA pair launched as a 2-CTA cluster (kPair 2)
+// owns a run of consecutive tiles.  A tile is (kBM * kPair) resident rows x
+// kBN streamed rows; in a pair each CTA holds 128 resident rows and loads
+// kBN/2 of the streamed rows, and the leader CTA (rank 0) issues
+// tcgen05.mma.cta_group::2 over both CTAs' shared memory, so every W / h
+// byte a CTA streams serves 256 resident rows.  Barrier ownership in a
+// pair: `full`, `a_full`, `acc_empty` and `drain` live in the leader
+// (both CTAs' copies signal them); `empty`, `a_empty`, `acc_full` live in
+// both CTAs (the leader's commit reaches both).
 // kStage: stage the column records of each tile in shared memory (double
 // buffered, prefetched one tile ahead); otherwise read them from global.
-template <class Epi, bool kStage>
+template <class Epi, bool kStage, int kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     lce_gemm_kernel(const __grid_constant__ CUtensorMap map_res,
                     const __grid_constant__ CUtensorMap map_str, const GemmArgs g) {
   constexpr int kRecF = kStage ? Epi::kRec : 0;
+  constexpr int kSt = num_stages(kPair);
+  constexpr int kStBytes = stage_bytes(kPair);
+  constexpr int kStRows = str_rows(kPair);
+  constexpr int kResRows = kBM * kPair;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte alignment by index arithmetic on the shared array, so that
+  // pointers derived from it stay in the shared address space.
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* sA = smem + SmemLayout::a_off();
   uint8_t* sB = smem + SmemLayout::b_off(g.kblocks);
   float* srec = reinterpret_cast<float*>(smem + SmemLayout::rec_off(g.kblocks));
@@ -334,13 +401,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = kPair == 2 ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
   const long long total = (long long)g.n_a * g.n_b;
-  const int G = gridDim.x;
-  const long long x_begin = tile_start(blockIdx.x, total, G);
-  const long long x_end = tile_start(blockIdx.x + 1, total, G);
+  const int G = gridDim.x / kPair;              // tile-range owners (CTAs or pairs)
+  const int unit = blockIdx.x / kPair;
+  const long long x_begin = tile_start(unit, total, G);
+  const long long x_end = tile_start(unit + 1, total, G);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < kSt; ++i) {
       mbar_init(&bars[kBarFull + i], 1);
       mbar_init(&bars[kBarEmpty + i], 1);
     }
@@ -348,31 +418,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bars[kBarAEmpty], 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars[kBarAccFull + i], 1);
-      mbar_init(&bars[kBarAccEmpty + i], kEpiThreads / 32);
+      mbar_init(&bars[kBarAccEmpty + i], kPair * kEpiThreads / 32);
     }
     mbar_init(&bars[kBarDrain], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars[kBarRecFull + i], 1);
+      mbar_init(&bars[kBarRecEmpty + i], kEpiThreads / 32);
+    }
     fence_mbar_init();
     prefetch_tmap(&map_res);
     prefetch_tmap(&map_str);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
+    if constexpr (kPair == 2) {
+      tmem_alloc_pair(tmem_slot, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (kPair == 2) cluster_sync();  // peer barriers initialised before any signal
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------ TMA producer
+    // ------------------------------------------------ TMA producer (both CTAs)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int cur_a = -1;
       uint32_t a_uses = 0;
-      int issued_parity[kStages];
-      for (int i = 0; i < kStages; ++i) issued_parity[i] = -1;
+      int issued_parity[kMaxStages];
+      for (int i = 0; i < kMaxStages; ++i) issued_parity[i] = -1;
       bool ok = true;
       for (long long x = x_begin; x < x_end && ok; ++x) {
         const int a = (int)(x / g.n_b);
@@ -383,36 +463,53 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_expect_tx(&bars[kBarAFull], (uint32_t)(g.kblocks * kAKBytes));
-          for (int kb = 0; kb < g.kblocks; ++kb)
-            tma_load_2d(sA + kb * kAKBytes, &map_res, &bars[kBarAFull], kb * kBK, a * kBM);
+          if (leader)
+            mbar_expect_tx(&bars[kBarAFull], (uint32_t)(kPair * g.kblocks * kAKBytes));
+          const int row0 = a * kResRows + (int)rank * kBM;
+          for (int kb = 0; kb < g.kblocks; ++kb) {
+            if constexpr (kPair == 2)
+              tma_load_2d_pair(sA + kb * kAKBytes, &map_res,
+                               mapa_shared(smem_u32(&bars[kBarAFull]), 0), kb * kBK, row0);
+            else
+              tma_load_2d(sA + kb * kAKBytes, &map_res, &bars[kBarAFull], kb * kBK, row0);
+          }
           cur_a = a;
           ++a_uses;
         }
+        const int srow0 = b * kBN + (int)rank * kStRows;
         for (int kb = 0; kb < g.kblocks; ++kb) {
           if (!mbar_wait(&bars[kBarEmpty + stage], phase ^ 1, g.err, kErrWaitProducer)) {
             ok = false;
             break;
           }
-          mbar_expect_tx(&bars[kBarFull + stage], (uint32_t)kBStageBytes);
-          tma_load_2d(sB + stage * kBStageBytes, &map_str, &bars[kBarFull + stage], kb * kBK,
-                      b * kBN);
+          if (leader) mbar_expect_tx(&bars[kBarFull + stage], (uint32_t)(kPair * kStBytes));
+          if constexpr (kPair == 2)
+            tma_load_2d_pair(sB + stage * kStBytes, &map_str,
+                             mapa_shared(smem_u32(&bars[kBarFull + stage]), 0), kb * kBK, srow0);
+          else
+            tma_load_2d(sB + stage * kStBytes, &map_str, &bars[kBarFull + stage], kb * kBK,
+                        srow0);
           issued_parity[stage] = (int)phase;
-          if (++stage == kStages) {
+          if (++stage == kSt) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
-      // Never leave the CTA with bulk copies still landing in its smem.
-      for (int i = 0; i < kStages; ++i)
-        if (issued_parity[i] >= 0) mbar_drain_wait(&bars[kBarFull + i], (uint32_t)issued_parity[i], g.err);
-      if (a_uses > 0) mbar_drain_wait(&bars[kBarAFull], (a_uses - 1) & 1, g.err);
+      // Never leave with bulk copies still landing: the leader's full
+      // barriers count both CTAs' bytes, so the leader drains them (the
+      // closing cluster barrier keeps the peer resident meanwhile).
+      if (leader) {
+        for (int i = 0; i < kSt; ++i)
+          if (issued_parity[i] >= 0)
+            mbar_drain_wait(&bars[kBarFull + i], (uint32_t)issued_parity[i], g.err);
+        if (a_uses > 0) mbar_drain_wait(&bars[kBarAFull], (a_uses - 1) & 1, g.err);
+      }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t kIdesc = idesc_f16_f32(kBM, kBN);
+    // ------------------------------------------------ MMA issuer (leader CTA)
+    if (lane == 0 && leader) {
+      constexpr uint32_t kIdesc = idesc_f16_f32(kResRows, kBN);
       int stage = 0;
       uint32_t phase = 0;
       int cur_a = -1;
@@ -438,26 +535,39 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint64_t adesc = sw128_kmajor_desc(smem_u32(sA + kb * kAKBytes));
-          const uint64_t bdesc = sw128_kmajor_desc(smem_u32(sB + stage * kBStageBytes));
+          const uint64_t bdesc = sw128_kmajor_desc(smem_u32(sB + stage * kStBytes));
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k)
-            umma_f16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), kIdesc,
-                     (kb | k) != 0 ? 1u : 0u);
-          umma_commit(&bars[kBarEmpty + stage]);
-          if (++stage == kStages) {
+          for (int k = 0; k < kBK / 16; ++k) {
+            if constexpr (kPair == 2)
+              umma_f16_pair(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), kIdesc,
+                            (kb | k) != 0 ? 1u : 0u);
+            else
+              umma_f16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), kIdesc,
+                       (kb | k) != 0 ? 1u : 0u);
+          }
+          if constexpr (kPair == 2) umma_commit_pair(&bars[kBarEmpty + stage], 0x3);
+          else umma_commit(&bars[kBarEmpty + stage]);
+          if (++stage == kSt) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        umma_commit(&bars[kBarAccFull + buf]);
-        if (x + 1 == x_end || (int)((x + 1) / g.n_b) != a) umma_commit(&bars[kBarAEmpty]);
+        const bool last_of_a = x + 1 == x_end || (int)((x + 1) / g.n_b) != a;
+        if constexpr (kPair == 2) {
+          umma_commit_pair(&bars[kBarAccFull + buf], 0x3);
+          if (last_of_a) umma_commit_pair(&bars[kBarAEmpty], 0x3);
+        } else {
+          umma_commit(&bars[kBarAccFull + buf]);
+          if (last_of_a) umma_commit(&bars[kBarAEmpty]);
+        }
       }
       // All MMAs issued by this thread complete before TMEM is released.
-      umma_commit(&bars[kBarDrain]);
+      if constexpr (kPair == 2) umma_commit_pair(&bars[kBarDrain], 0x1);
+      else umma_commit(&bars[kBarDrain]);
       mbar_drain_wait(&bars[kBarDrain], 0, g.err);
     }
-  } else {
+  } else if (warp < kRecWarp) {
     // ------------------------------------------------ epilogue (warps 2..9)
     // Warp w reads TMEM lanes 32*(w%4)..+31; warps 2-5 take columns
     // 0..127 of each tile, warps 6-9 columns 128..255, so every resident
@@ -466,7 +576,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     const int half = e >> 2;
     const int row = quarter * 32 + lane;
-    const int ct = e * 32 + lane;  // the column this thread stages
     const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
     constexpr int CW = Epi::kCW;
     constexpr int NCH = (kBN / 2) / CW;
@@ -474,33 +583,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     int cur_a = -1;
     long long li = 0;
     bool failed = false;
-    float rec[Epi::kRec];
-    if (kStage && x_begin < x_end) Epi::load_rec(g, (int)(x_begin % g.n_b), ct, rec);
     for (long long x = x_begin; x < x_end; ++x, ++li) {
       const int a = (int)(x / g.n_b);
       const int b = (int)(x % g.n_b);
       if (a != cur_a) {
         if (cur_a >= 0 && !failed)
-          epi.flush(g, 2 * (blockIdx.x - tile_owner((long long)cur_a * g.n_b, total, G)) + half);
-        epi.begin(g, a, row);
+          epi.flush(g, 2 * (unit - tile_owner((long long)cur_a * g.n_b, total, G)) + half);
+        epi.begin(g, a * kResRows + (int)rank * kBM + row);
         cur_a = a;
       }
-      const float* recs;
-      if constexpr (kStage) {
-        // Every epilogue thread reaches this barrier once per tile, also
-        // after a failed wait, so the barrier count always matches.
-        float* buf = srec + (li & 1) * (kBN * Epi::kRec);
-        st_vec<Epi::kRec>(buf + ct * Epi::kRec, rec);
-        named_bar_sync(1, kEpiThreads);
-        if (x + 1 < x_end) Epi::load_rec(g, (int)((x + 1) % g.n_b), ct, rec);
-        recs = buf;
-      } else {
-        recs = Epi::global_recs(g, b);
-      }
+      const float* recs = kStage ? srec + (li & 1) * (kBN * Epi::kRec) : Epi::global_recs(g, b);
       if (failed) continue;
       const int buf = (int)(li & 1);
       const uint32_t use = (uint32_t)(li >> 1);
-      if (!mbar_wait(&bars[kBarAccFull + buf], use & 1, g.err, kErrWaitEpilogue)) {
+      if (!mbar_wait(&bars[kBarAccFull + buf], use & 1, g.err, kErrWaitEpilogue) ||
+          (kStage && !mbar_wait(&bars[kBarRecFull + buf], use & 1, g.err, kErrWaitEpilogue))) {
         failed = true;
         continue;
       }
@@ -512,32 +609,68 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t base = lane_addr + (uint32_t)(buf * kBN + col0);
         const float* rb = recs + col0 * Epi::kRec;
         const int gcol = b * kBN + col0;
+        // Only a tile that reaches past the last vocab id / position needs
+        // the masked chunk variant.
+        const bool tail = gcol + kBN / 2 > Epi::limit(g);
         float ca[CW], cb[CW];
         tmem_ld<CW>(base, ca);
         tmem_ld_wait<CW>(ca);
 #pragma unroll 1
         for (int c = 0; c < NCH; c += 2) {
           tmem_ld<CW>(base + (uint32_t)((c + 1) * CW), cb);
-          epi.chunk(g, gcol + c * CW, ca, rb + c * CW * Epi::kRec);
+          run_chunk<Epi>(epi, g, tail, gcol + c * CW, ca, rb + c * CW * Epi::kRec);
           tmem_ld_wait<CW>(cb);
           if (c + 2 < NCH) tmem_ld<CW>(base + (uint32_t)((c + 2) * CW), ca);
-          epi.chunk(g, gcol + (c + 1) * CW, cb, rb + (c + 1) * CW * Epi::kRec);
+          run_chunk<Epi>(epi, g, tail, gcol + (c + 1) * CW, cb,
+                                 rb + (c + 1) * CW * Epi::kRec);
           if (c + 2 < NCH) tmem_ld_wait<CW>(ca);
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars[kBarAccEmpty + buf]);
+      if (lane == 0) {
+        if (kStage) mbar_arrive(&bars[kBarRecEmpty + buf]);
+        if constexpr (kPair == 2)
+          mbar_arrive_cluster(mapa_shared(smem_u32(&bars[kBarAccEmpty + buf]), 0));
+        else
+          mbar_arrive(&bars[kBarAccEmpty + buf]);
+      }
     }
     if (cur_a >= 0 && !failed)
-      epi.flush(g, 2 * (blockIdx.x - tile_owner((long long)cur_a * g.n_b, total, G)) + half);
+      epi.flush(g, 2 * (unit - tile_owner((long long)cur_a * g.n_b, total, G)) + half);
+  } else if (warp == kRecWarp) {
+    // ------------------------------------------------ record loader (both CTAs)
+    // The records of tile li (256 columns, one contiguous block in global)
+    // go to buffer li%2 once the epilogue has released tile li-2.
+    if (kStage && lane == 0) {
+      constexpr uint32_t kBytes = (uint32_t)(kBN * Epi::kRec * 4);
+      long long li = 0;
+      int issued = 0;
+      for (long long x = x_begin; x < x_end; ++x, ++li) {
+        const int b = (int)(x % g.n_b);
+        const int buf = (int)(li & 1);
+        const uint32_t use = (uint32_t)(li >> 1);
+        if (use > 0 &&
+            !mbar_wait(&bars[kBarRecEmpty + buf], (use - 1) & 1, g.err, kErrWaitProducer))
+          break;
+        mbar_expect_tx(&bars[kBarRecFull + buf], kBytes);
+        bulk_load(srec + buf * (kBN * Epi::kRec), Epi::global_recs(g, b), kBytes,
+                  &bars[kBarRecFull + buf]);
+        ++issued;
+      }
+      // drain: the last load into each buffer has landed
+      for (int k = issued - 2 < 0 ? 0 : issued - 2; k < issued; ++k)
+        mbar_drain_wait(&bars[kBarRecFull + (k & 1)], (uint32_t)((k >> 1) & 1), g.err);
+    }
   }
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (kPair == 2) cluster_sync();  // peer done with the leader's barriers / MMAs done
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    if constexpr (kPair == 2) tmem_dealloc_pair(tmem_base, kTmemCols);
+    else tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
@@ -554,10 +687,9 @@ __global__ void lce_prep(const void* __restrict__ H, int dtype, int T, int Tpad,
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (w >= Tpad) return;
-  float* rec = tok + (long long)w * tok_stride(R);
-  if (w >= T) {
-    for (int j = lane; j < tok_stride(R); j += 32) rec[j] = 0.f;
-    if (lane == 0) rec[R + 2] = __int_as_float(-1);
+  if (w >= T) {  // padding position: all fields zero, target -1
+    for (int f = lane; f < tok_stride(R); f += 32)
+      tok[tidx(w, f, R)] = f == R + 2 ? __int_as_float(-1) : 0.f;
     return;
   }
   float u[R];
@@ -587,11 +719,11 @@ __global__ void lce_prep(const void* __restrict__ H, int dtype, int T, int Tpad,
       tg = 0;
     }
 #pragma unroll
-    for (int j = 0; j < R; ++j) rec[j] = scale * u[j];
-    rec[R] = 0.f;
-    rec[R + 1] = 0.f;
-    rec[R + 2] = __int_as_float(tg);
-    rec[R + 3] = 0.f;
+    for (int j = 0; j < R; ++j) tok[tidx(w, j, R)] = scale * u[j];
+    tok[tidx(w, R, R)] = 0.f;
+    tok[tidx(w, R + 1, R)] = 0.f;
+    tok[tidx(w, R + 2, R)] = __int_as_float(tg);
+    tok[tidx(w, R + 3, R)] = 0.f;
   }
 }
 
@@ -601,15 +733,16 @@ __global__ void lce_prep(const void* __restrict__ H, int dtype, int T, int Tpad,
 // (the reference's d_mid, src/train.c:161-168).  The record of t gets
 // M*log2(e) and 1/S for pass 2.
 template <int R>
-__global__ void lce_combine(int T, int n_b1, int G1, long long Tcap, const float* __restrict__ p_max,
+__global__ void lce_combine(int T, int res_rows, int n_b1, int G1, long long Tcap,
+                            const float* __restrict__ p_max,
                             const float* __restrict__ p_sum, const float* __restrict__ p_q,
                             const float* __restrict__ z_tgt, const float* __restrict__ Bt,
                             float scale, float* __restrict__ tok, float* __restrict__ dU,
                             float* __restrict__ loss_tok) {
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T) return;
-  const int a = t / kBM;
-  const long long total = (long long)((T + kBM - 1) / kBM) * n_b1;
+  const int a = t / res_rows;
+  const long long total = (long long)((T + res_rows - 1) / res_rows) * n_b1;
   const int s0 = tile_owner((long long)a * n_b1, total, G1);
   const int s1 = tile_owner((long long)a * n_b1 + n_b1 - 1, total, G1);
   const int nslot = 2 * (s1 - s0 + 1);
@@ -628,14 +761,37 @@ __global__ void lce_combine(int T, int n_b1, int G1, long long Tcap, const float
     for (int j = 0; j < R; ++j) Q[j] = fmaf(p_q[o * R + j], f, Q[j]);
   }
   const float inv = 1.0f / S;
-  float* rec = tok + (long long)t * tok_stride(R);
-  const int tg = __float_as_int(rec[R + 2]);
+  const int tg = __float_as_int(tok[tidx(t, R + 2, R)]);
   const float pt = expf(z_tgt[t] - M) * inv;
   loss_tok[t] = -logf(pt + 1e-12f);
-  rec[R] = M * kLog2e;
-  rec[R + 1] = inv;
+  tok[tidx(t, R, R)] = -(M * kLog2e);
+  tok[tidx(t, R + 1, R)] = inv;
 #pragma unroll
-  for (int j = 0; j < R; ++j) dU[(long long)t * R + j] = scale * (Q[j] * inv - Bt[(long long)tg * R + j]);
+  for (int j = 0; j < R; ++j) dU[(long long)t * R + j] = scale * (Q[j] * inv - Bt[bidx(tg, j, R)]);
+}
+
+// The onehot part of dl = p - onehot for dB: corr[v][j] = -(sum of
+// s*U[t][j] over the positions t whose target is v).  Each term is rounded
+// to a 64-bit fixed-point number (2^-30 resolution) and added with integer
+// atomics: integer sums do not depend on the order of the additions, so the
+// result is deterministic however the (Zipf-skewed) targets collide, and
+// the one final rounding to f32 (in lce_finalize) is at least as accurate
+// as a sequential f32 sum.  |s*U| must stay below 2^17 per position.
+constexpr float kFixScale = 1073741824.0f;  // 2^30
+constexpr double kFixInv = 1.0 / 1073741824.0;
+template <int R>
+__global__ void lce_onehot(int T, const float* __restrict__ tok,
+                           unsigned long long* __restrict__ corr_fx, int* err) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  const int tg = __float_as_int(tok[tidx(t, R + 2, R)]);
+#pragma unroll
+  for (int j = 0; j < R; ++j) {
+    const float u = tok[tidx(t, j, R)];
+    if (!(fabsf(u) < 131072.0f)) atomicCAS(err, 0, kErrRange);
+    const long long q = __float2ll_rn(u * kFixScale);
+    atomicAdd(&corr_fx[bidx(tg, j, R)], (unsigned long long)q);
+  }
 }
 
 // dA partials: gAp[c][i][j] = sum over the kDAChunk positions of chunk c
@@ -669,13 +825,14 @@ __global__ void lce_dA_partial(int T, int d, const __half* __restrict__ h16,
 // order, so the step is deterministic.
 template <int R>
 __global__ void lce_finalize(int T, int d, int V, long long Vpad, int n_chunks,
-                             const float* __restrict__ gAp, int n_b2, int G2,
-                             const float* __restrict__ gBp, const float* __restrict__ loss_tok,
-                             float* __restrict__ Gbuf) {
+                             const float* __restrict__ gAp, int res_rows, int n_b2, int G2,
+                             const float* __restrict__ gBp,
+                             unsigned long long* __restrict__ corr_fx,
+                             const float* __restrict__ loss_tok, float* __restrict__ Gbuf) {
   const long long nA = (long long)d * R;
-  const long long nB = (long long)V * R;
+  const long long nB = Vpad * R;  // pair layout, entries of vocab ids >= V stay zero
   const long long stride = (long long)gridDim.x * blockDim.x;
-  const int n_a2 = (V + kBM - 1) / kBM;
+  const int n_a2 = (V + res_rows - 1) / res_rows;
   const long long total2 = (long long)n_a2 * n_b2;
   for (long long k = (long long)blockIdx.x * blockDim.x + threadIdx.x; k < nA + nB; k += stride) {
     float s = 0.f;
@@ -683,11 +840,20 @@ __global__ void lce_finalize(int T, int d, int V, long long Vpad, int n_chunks,
       for (int c = 0; c < n_chunks; ++c) s += gAp[(long long)c * nA + k];
     } else {
       const long long e = k - nA;
-      const int v = (int)(e / R);
-      const int a = v / kBM;
+      const int v = (int)(2 * (e / (2 * R)) + (e & 1));
+      if (v >= V) {
+        Gbuf[k] = 0.f;
+        continue;
+      }
+      const int a = v / res_rows;
       const int s0 = tile_owner((long long)a * n_b2, total2, G2);
       const int s1 = tile_owner((long long)a * n_b2 + n_b2 - 1, total2, G2);
       for (int q = 0; q < 2 * (s1 - s0 + 1); ++q) s += gBp[(long long)q * Vpad * R + e];
+      const long long c = (long long)corr_fx[e];
+      if (c != 0) {
+        s -= (float)((double)c * kFixInv);
+        corr_fx[e] = 0ull;  // ready for the next step
+      }
     }
     Gbuf[k] = s;
   }
