@@ -4,6 +4,7 @@
 // or fails with an error code.
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <dlfcn.h>
 #include <nccl.h>
 
 #include <cmath>
@@ -74,6 +75,39 @@ bool make_map(CUtensorMap* m, const void* base, long long rows, int d, int box_r
 }
 
 long long round_up(long long x, long long m) { return (x + m - 1) / m * m; }
+
+// NCCL is loaded on first use (a communicator is only needed for
+// multi-GPU runs), preferring a libnccl already loaded in the process (for
+// example PyTorch's) so that two different NCCL builds never meet in one
+// process; otherwise the system libnccl.so.2.
+struct NcclApi {
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  bool ok = false;
+};
+
+const NcclApi& nccl() {
+  static NcclApi api;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!lib) lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+    if (lib) {
+      api.GetUniqueId = reinterpret_cast<decltype(api.GetUniqueId)>(dlsym(lib, "ncclGetUniqueId"));
+      api.CommInitRank =
+          reinterpret_cast<decltype(api.CommInitRank)>(dlsym(lib, "ncclCommInitRank"));
+      api.AllReduce = reinterpret_cast<decltype(api.AllReduce)>(dlsym(lib, "ncclAllReduce"));
+      api.CommDestroy =
+          reinterpret_cast<decltype(api.CommDestroy)>(dlsym(lib, "ncclCommDestroy"));
+      api.ok = api.GetUniqueId && api.CommInitRank && api.AllReduce && api.CommDestroy;
+    }
+  }
+  return api;
+}
 
 // Largest number of CTA segments any resident tile's run of n_b tiles is
 // split into, for n_a x n_b tiles over G CTAs.
@@ -331,8 +365,8 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
   // 7. data-parallel sum over ranks
   mark(h, kPhAllReduce);
   if (h->comm) {
-    if (ncclAllReduce(h->Gbuf, h->Gbuf, (size_t)(nparam + 2), ncclFloat, ncclSum, h->comm, st) !=
-        ncclSuccess)
+    if (nccl().AllReduce(h->Gbuf, h->Gbuf, (size_t)(nparam + 2), ncclFloat, ncclSum, h->comm,
+                         st) != ncclSuccess)
       return fail(LORA_CE_ENCCL, "ncclAllReduce failed");
   }
   // 8. clip norm (optional), 9. Adam
@@ -536,7 +570,7 @@ int lora_ce_destroy(lora_ce_handle* h) {
   if (!h) return 0;
   cudaSetDevice(h->cfg.device);
   if (h->stream) cudaStreamSynchronize(h->stream);
-  if (h->comm) ncclCommDestroy(h->comm);
+  if (h->comm) nccl().CommDestroy(h->comm);
   for (cudaEvent_t e : h->ev)
     if (e) cudaEventDestroy(e);
   free_all(h);
@@ -669,8 +703,9 @@ int lora_ce_sync(lora_ce_handle* h) {
 int lora_ce_nccl_unique_id(void* id128) {
   if (!id128) return fail(LORA_CE_EINVAL, "null id buffer");
   static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId size");
+  if (!nccl().ok) return fail(LORA_CE_ENCCL, "libnccl.so.2 could not be loaded");
   ncclUniqueId id;
-  if (ncclGetUniqueId(&id) != ncclSuccess) return fail(LORA_CE_ENCCL, "ncclGetUniqueId failed");
+  if (nccl().GetUniqueId(&id) != ncclSuccess) return fail(LORA_CE_ENCCL, "ncclGetUniqueId failed");
   memcpy(id128, &id, 128);
   return 0;
 }
@@ -680,9 +715,10 @@ int lora_ce_comm_init(lora_ce_handle* h, int32_t nranks, int32_t rank, const voi
     return fail(LORA_CE_EINVAL, "bad communicator arguments");
   if (h->comm) return fail(LORA_CE_ESTATE, "communicator already initialised");
   LCE_CUDA(cudaSetDevice(h->cfg.device));
+  if (!nccl().ok) return fail(LORA_CE_ENCCL, "libnccl.so.2 could not be loaded");
   ncclUniqueId id;
   memcpy(&id, id128, 128);
-  if (ncclCommInitRank(&h->comm, nranks, id, rank) != ncclSuccess)
+  if (nccl().CommInitRank(&h->comm, nranks, id, rank) != ncclSuccess)
     return fail(LORA_CE_ENCCL, "ncclCommInitRank failed");
   h->nranks = nranks;
   h->rank = rank;

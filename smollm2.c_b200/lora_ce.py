@@ -52,9 +52,9 @@ NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", 
 
 def build(verbose: bool = False) -> str:
     """Compile csrc/ into liblora_ce.so (sm_100a) next to this file."""
-    src = os.path.join(HERE, "csrc", "lora_ce_api.cu")
-    cmd = ["nvcc", *NVCC_FLAGS, "-I" + os.path.join(REPO, "include"), "-o", LIB_PATH, src,
-           "-lnccl"]
+    srcs = [os.path.join(HERE, "csrc", f) for f in ("lora_ce_api.cu",)]
+    cmd = ["nvcc", *NVCC_FLAGS, "-I" + os.path.join(REPO, "include"), "-o", LIB_PATH, *srcs,
+           "-ldl"]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     subprocess.run(cmd, check=True)
