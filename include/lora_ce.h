@@ -143,6 +143,30 @@ int32_t lora_ce_last_launches(lora_ce_handle* h);
 
 const char* lora_ce_last_error(void);
 
+/* Per-position loss -log(softmax(h.W^T + scale.(h.A).B)[target] + 1e-12)
+ * for callers that cannot allocate GPU memory at call time (a serving or
+ * evaluation process whose memory is reserved up front, or a runtime that
+ * must never fail or stall in an allocation mid-request).  No counterpart
+ * in the reference.  It allocates nothing: all scratch lives in statically
+ * sized device arrays (about 7.3 MB per GPU that loads the library, held
+ * until exit), and every argument is a device pointer on the current
+ * device: W [V][d] f16 bits, A [d][4], B [4][V] (reference layouts),
+ * H [T][d] of h_dtype, targets [T], loss out [T].  Work is enqueued on
+ * `stream` (a cudaStream_t; NULL = legacy default stream) and the call
+ * returns without waiting.  Limits: rank 4, T <= 4096, V <= 49152, d a
+ * multiple of 64 up to 576; larger sizes return LORA_CE_EINVAL.  A target
+ * outside [0, V) makes every output loss NaN.  All calls share the scratch
+ * arrays, so calls that can overlap on the GPU race and must be serialised
+ * by the caller; the first call on a device resolves the arrays' device
+ * addresses, so make it before any stream capture.  Errors are described
+ * by lora_ce_noalloc_last_error(). */
+int lora_ce_token_loss_noalloc(const uint16_t* d_W, int32_t vocab, int32_t dim,
+                               const float* d_A, const float* d_B, float scale,
+                               const void* d_H, int32_t h_dtype, int32_t T,
+                               const int32_t* d_targets, float* d_loss,
+                               void* stream);
+const char* lora_ce_noalloc_last_error(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -875,7 +875,7 @@ __global__ void lce_finalize(int T, int d, int V, long long Vpad, int n_chunks,
 }
 
 // Sum of squares of the mean gradient, per block (global-norm clip).
-__global__ void lce_sqnorm(long long n, const float* __restrict__ Gbuf, double* __restrict__ part) {
+static __global__ void lce_sqnorm(long long n, const float* __restrict__ Gbuf, double* __restrict__ part) {
   __shared__ double red[256];
   const float inv = 1.0f / Gbuf[n + 1];
   double s = 0.0;
@@ -904,7 +904,7 @@ struct AdamArgs {
 // g = G / n_pred (x clip coefficient); decoupled decay; Adam update
 // (src/train.c:175-196), written with explicitly rounded operations so the
 // update is the reference's f32 arithmetic, op for op.
-__global__ void lce_adam(AdamArgs a, float* __restrict__ params, float* __restrict__ mom1,
+static __global__ void lce_adam(AdamArgs a, float* __restrict__ params, float* __restrict__ mom1,
                          float* __restrict__ mom2, const float* __restrict__ Gbuf,
                          float* __restrict__ gmean, const double* __restrict__ norm_parts,
                          float* __restrict__ loss_out) {

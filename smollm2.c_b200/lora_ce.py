@@ -44,6 +44,7 @@ EXPORTS = [
     "lora_ce_get_grads", "lora_ce_get_token_loss", "lora_ce_nccl_unique_id",
     "lora_ce_comm_init", "lora_ce_sync", "lora_ce_stream", "lora_ce_last_launches",
     "lora_ce_last_error", "lora_ce_set_profiling", "lora_ce_phase_times", "lora_ce_phase_name",
+    "lora_ce_token_loss_noalloc", "lora_ce_noalloc_last_error",
 ]
 
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
@@ -52,7 +53,7 @@ NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", 
 
 def build(verbose: bool = False) -> str:
     """Compile csrc/ into liblora_ce.so (sm_100a) next to this file."""
-    srcs = [os.path.join(HERE, "csrc", f) for f in ("lora_ce_api.cu",)]
+    srcs = [os.path.join(HERE, "csrc", f) for f in ("lora_ce_api.cu", "lora_ce_noalloc.cu")]
     cmd = ["nvcc", *NVCC_FLAGS, "-I" + os.path.join(REPO, "include"), "-o", LIB_PATH, *srcs,
            "-ldl"]
     if verbose:
@@ -108,6 +109,11 @@ def load_library() -> C.CDLL:
     lib.lora_ce_phase_times.restype = C.c_int32
     lib.lora_ce_phase_name.argtypes = [C.c_int32]
     lib.lora_ce_phase_name.restype = C.c_char_p
+    lib.lora_ce_token_loss_noalloc.argtypes = [vp, C.c_int32, C.c_int32, vp, vp, C.c_float, vp,
+                                               C.c_int32, C.c_int32, vp, vp, vp]
+    lib.lora_ce_token_loss_noalloc.restype = C.c_int
+    lib.lora_ce_noalloc_last_error.argtypes = []
+    lib.lora_ce_noalloc_last_error.restype = C.c_char_p
     lib.lora_ce_last_error.argtypes = []
     lib.lora_ce_last_error.restype = C.c_char_p
     for name in ["lora_ce_create", "lora_ce_destroy", "lora_ce_set_weight_f16",
@@ -127,6 +133,22 @@ def _check(rc: int, what: str) -> None:
 
 def _ptr(a: np.ndarray) -> C.c_void_p:
     return C.c_void_p(a.ctypes.data)
+
+
+def token_loss_noalloc(d_W: int, vocab: int, dim: int, d_A: int, d_B: int, scale: float,
+                       d_H: int, h_dtype: int, T: int, d_targets: int, d_loss: int,
+                       stream: int = 0) -> None:
+    """lora_ce_token_loss_noalloc on device pointers (see include/lora_ce.h):
+    the per-position loss without any allocation, for callers that cannot
+    allocate GPU memory at call time.  Rank 4, T <= 4096, V <= 49152."""
+    lib = load_library()
+    rc = lib.lora_ce_token_loss_noalloc(
+        C.c_void_p(d_W), vocab, dim, C.c_void_p(d_A), C.c_void_p(d_B), float(scale),
+        C.c_void_p(d_H), h_dtype, T, C.c_void_p(d_targets), C.c_void_p(d_loss),
+        C.c_void_p(stream or None))
+    if rc != 0:
+        msg = lib.lora_ce_noalloc_last_error().decode(errors="replace")
+        raise LoraCEError(f"lora_ce_token_loss_noalloc failed: {ERRORS.get(rc, rc)}: {msg}")
 
 
 def default_config(dim, vocab, rank, max_tokens, **kw) -> Config:
