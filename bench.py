@@ -247,7 +247,7 @@ def main():
         import datetime
         import torch.distributed as dist
         dist.init_process_group(backend="cpu:gloo,cuda:nccl",
-                                timeout=datetime.timedelta(seconds=300))
+                                timeout=datetime.timedelta(seconds=120))
 
     # CPU baseline first (spawned pool, before any GPU work in this process)
     cpu = None
