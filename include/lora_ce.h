@@ -148,7 +148,7 @@ const char* lora_ce_last_error(void);
  * evaluation process whose memory is reserved up front, or a runtime that
  * must never fail or stall in an allocation mid-request).  No counterpart
  * in the reference.  It allocates nothing: all scratch lives in statically
- * sized device arrays (about 7.3 MB per GPU that loads the library, held
+ * sized device arrays (about 8.9 MB per GPU that loads the library, held
  * until exit), and every argument is a device pointer on the current
  * device: W [V][d] f16 bits, A [d][4], B [4][V] (reference layouts),
  * H [T][d] of h_dtype, targets [T], loss out [T].  Work is enqueued on

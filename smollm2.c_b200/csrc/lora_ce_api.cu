@@ -226,7 +226,7 @@ int resident_units(int pair, int kblocks, int num_sms) {
   if (pair == 1) return num_sms;
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3((unsigned)num_sms);
-  lc.blockDim = dim3(kThreads);
+  lc.blockDim = dim3(block_threads(Epi::kWarps));
   lc.dynamicSmemBytes = (size_t)smem;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -249,7 +249,7 @@ int launch_gemm(const CUtensorMap& map_res, const CUtensorMap& map_str, const Ge
   LCE_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3((unsigned)(units * pair));
-  lc.blockDim = dim3(kThreads);
+  lc.blockDim = dim3(block_threads(Epi::kWarps));
   lc.dynamicSmemBytes = (size_t)smem;
   lc.stream = st;
   cudaLaunchAttribute attr[1];
@@ -283,11 +283,11 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
   // 1. convert h, U = h.A, per-position records
   mark(h, kPhPrep);
   {
-    const int threads = 256;
-    const long long warps = Tpad;
-    const int blocks = (int)((warps * 32 + threads - 1) / threads);
-    lce_prep<R><<<blocks, threads, 0, st>>>(dH, dtype, T, (int)Tpad, d, h->params, h->cfg.scale,
-                                            dtg, V, h->h16, h->tok, h->err);
+    const int threads = 256;  // 8 warps per block, grid-stride over positions
+    const int blocks = (int)std::min<long long>((Tpad + 7) / 8, 4LL * h->num_sms);
+    lce_prep<R><<<blocks, threads, (size_t)d * R * 4, st>>>(dH, dtype, T, (int)Tpad, d, h->params,
+                                                           h->cfg.scale, dtg, V, h->h16, h->tok,
+                                                           h->err);
     ++launches;
   }
   const int pair = h->pair;
@@ -297,7 +297,8 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
   const int n_a1 = (T + res_rows - 1) / res_rows, n_b1 = (int)(h->Vpad / kBN);
   const long long total1 = (long long)n_a1 * n_b1;
   const int G1 = (int)std::min<long long>(h->units1, total1);
-  const int seg1 = 2 * max_segments(n_a1, n_b1, G1);
+  const int cp1 = col_parts(EpiLse<R>::kWarps), cp2 = col_parts(EpiGrad<R>::kWarps);
+  const int seg1 = cp1 * max_segments(n_a1, n_b1, G1);
   const long long stride1 = (long long)n_a1 * res_rows;
   if ((long long)seg1 * stride1 > h->p1_cap)
     return fail(LORA_CE_ESTATE, "pass-1 partial buffer too small");
@@ -326,19 +327,19 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
   }
   // 3. merge partials -> M, 1/S, loss_t, dU
   mark(h, kPhCombine);
-  lce_combine<R><<<(T + 255) / 256, 256, 0, st>>>(T, res_rows, n_b1, G1, stride1, h->p_max,
+  lce_combine<R><<<(T + 7) / 8, 256, 0, st>>>(T, cp1, res_rows, n_b1, G1, stride1, h->p_max,
                                                   h->p_sum,
                                                   h->p_q, h->z_tgt, g.Bt, h->cfg.scale, h->tok,
                                                   h->dU, h->loss_tok);
   ++launches;
   // onehot part of dB (order-independent fixed-point sums)
-  lce_onehot<R><<<(T + 255) / 256, 256, 0, st>>>(T, h->tok, h->corr_fx, h->err);
+  lce_onehot<R><<<(T + 63) / 64, 64, 0, st>>>(T, h->tok, h->corr_fx, h->err);
   ++launches;
   // 4. pass 2: dB per vocab row
   const int n_a2 = (V + res_rows - 1) / res_rows, n_b2 = (int)(Tpad / kBN);
   const long long total2 = (long long)n_a2 * n_b2;
   const int G2 = (int)std::min<long long>(h->units2, total2);
-  if (2 * max_segments(n_a2, n_b2, G2) > h->gbp_segs)
+  if (cp2 * max_segments(n_a2, n_b2, G2) > h->gbp_segs)
     return fail(LORA_CE_ESTATE, "pass-2 partial buffer too small");
   mark(h, kPhPass2);
   {
@@ -352,13 +353,14 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
   // 5. dA partials, 6. pack gradient sums
   const int n_chunks = (T + kDAChunk - 1) / kDAChunk;
   mark(h, kPhDA);
-  lce_dA_partial<R><<<n_chunks, 192, 0, st>>>(T, d, h->h16, h->dU, h->gAp);
+  lce_dA_partial<R><<<dim3(n_chunks, (d + 63) / 64), dim3(32, da_rows(R)), 0, st>>>(
+      T, d, h->h16, h->dU, h->gAp);
   ++launches;
   const long long nparam = (long long)d * R + h->Vpad * R;
   mark(h, kPhFinalize);
   {
     const int blocks = (int)std::min<long long>((nparam + 255) / 256, 8LL * h->num_sms);
-    lce_finalize<R><<<blocks, 256, 0, st>>>(T, d, V, h->Vpad, n_chunks, h->gAp, res_rows, n_b2, G2,
+    lce_finalize<R><<<blocks, 256, 0, st>>>(T, cp2, d, V, h->Vpad, n_chunks, h->gAp, res_rows, n_b2, G2,
                                             h->gBp, h->corr_fx, h->loss_tok, h->Gbuf);
     ++launches;
   }
@@ -422,6 +424,8 @@ int check_step_args(lora_ce_handle* h, const void* H, int dtype, int T, const in
   if (!H || !tg) return fail(LORA_CE_EINVAL, "null input");
   if (dtype < 0 || dtype > 2) return fail(LORA_CE_EINVAL, "bad hidden-state dtype");
   if (T < 1 || T > h->cfg.max_tokens) return fail(LORA_CE_EINVAL, "T out of range");
+  if ((reinterpret_cast<uintptr_t>(H) & 15) != 0)
+    return fail(LORA_CE_EINVAL, "hidden states must be 16-byte aligned");
   return 0;
 }
 
@@ -518,12 +522,13 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
   for (int n_a1 = 1; (long long)n_a1 * res_rows < Tcap + res_rows; ++n_a1) {
     const long long total = (long long)n_a1 * n_b1;
     const int G = (int)std::min<long long>(h->units1, total);
-    p1 = std::max<long long>(p1, 2LL * max_segments(n_a1, n_b1, G) * n_a1 * res_rows);
+    p1 = std::max<long long>(p1, (long long)col_parts(16) * max_segments(n_a1, n_b1, G) * n_a1 *
+                                     res_rows);
   }
   for (int n_b2 = 1; (long long)n_b2 * kBN <= Tcap; ++n_b2) {
     const long long total = (long long)n_a2 * n_b2;
     const int G = (int)std::min<long long>(h->units2, total);
-    s2 = std::max(s2, 2 * max_segments(n_a2, n_b2, G));
+    s2 = std::max(s2, col_parts(16) * max_segments(n_a2, n_b2, G));
   }
   h->p1_cap = p1;
   h->gbp_segs = s2;

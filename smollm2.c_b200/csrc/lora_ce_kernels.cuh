@@ -44,11 +44,12 @@ constexpr int kAKBytes = kBM * kBK * 2;   // 16 KB per resident K-block
 __host__ __device__ constexpr int str_rows(int pair) { return kBN / pair; }
 __host__ __device__ constexpr int stage_bytes(int pair) { return str_rows(pair) * kBK * 2; }
 __host__ __device__ constexpr int num_stages(int pair) { return kRingBytes / stage_bytes(pair); }
-constexpr int kEpiWarps = 8;           // two per TMEM lane quarter
-constexpr int kEpiThreads = kEpiWarps * 32;
-constexpr int kRecWarp = 2 + kEpiWarps;  // per-tile column-record loader
-// warp 0 TMA producer, warp 1 MMA issuer, warps 2..9 epilogue, warp 10 records
-constexpr int kThreads = 32 * (kRecWarp + 1);
+// Warp roles: warp 0 TMA producer, warp 1 MMA issuer, then kEpiWarps
+// epilogue warps (4 or 2 per TMEM lane quarter, set per epilogue by its
+// register needs), then one record-loader warp.
+__host__ __device__ constexpr int epi_threads(int epi_warps) { return 32 * epi_warps; }
+__host__ __device__ constexpr int col_parts(int epi_warps) { return epi_warps / 4; }
+__host__ __device__ constexpr int block_threads(int epi_warps) { return 32 * (epi_warps + 3); }
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kTmemCols = 512;    // two 256-column fp32 accumulators
 constexpr int kMaxKBlocks = 10;        // d <= 640
@@ -179,7 +180,8 @@ __device__ __forceinline__ float2 f2(float x, float y) { return make_float2(x, y
 template <int R>
 struct EpiLse {
   static constexpr int kRec = R;  // floats per column
-  static constexpr int kCW = R >= 16 ? 8 : 16;
+  static constexpr int kWarps = R == 4 ? 16 : 8;
+  static constexpr int kCW = (R >= 16 || kWarps == 16) ? 8 : 16;
   static constexpr float kLazy = 8.0f;   // move the reference max only past this
   static constexpr float kRedo = 80.0f;  // re-sum a chunk that jumped this far
   int t;
@@ -306,7 +308,8 @@ struct EpiLse {
 template <int R>
 struct EpiGrad {
   static constexpr int kRec = R + 4;
-  static constexpr int kCW = R >= 16 ? 8 : 16;
+  static constexpr int kWarps = R == 4 ? 16 : 8;
+  static constexpr int kCW = (R >= 16 || kWarps == 16) ? 8 : 16;
   int v;
   bool valid;
   float2 bv2[R];  // (B[j][v], B[j][v])
@@ -381,9 +384,13 @@ __device__ __forceinline__ void run_chunk(Epi& epi, const GemmArgs& g, bool tail
 // kStage: stage the column records of each tile in shared memory (double
 // buffered, prefetched one tile ahead); otherwise read them from global.
 template <class Epi, bool kStage, int kPair>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(block_threads(Epi::kWarps), 1)
     lce_gemm_kernel(const __grid_constant__ CUtensorMap map_res,
                     const __grid_constant__ CUtensorMap map_str, const GemmArgs g) {
+  constexpr int kEpiWarps = Epi::kWarps;
+  constexpr int kEpiThreads = epi_threads(kEpiWarps);
+  constexpr int kColParts = col_parts(kEpiWarps);
+  constexpr int kRecWarp = 2 + kEpiWarps;
   constexpr int kRecF = kStage ? Epi::kRec : 0;
   constexpr int kSt = num_stages(kPair);
   constexpr int kStBytes = stage_bytes(kPair);
@@ -568,17 +575,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_drain_wait(&bars[kBarDrain], 0, g.err);
     }
   } else if (warp < kRecWarp) {
-    // ------------------------------------------------ epilogue (warps 2..9)
-    // Warp w reads TMEM lanes 32*(w%4)..+31; warps 2-5 take columns
-    // 0..127 of each tile, warps 6-9 columns 128..255, so every resident
-    // row has two partial states, flushed to slots 2*segment + half.
+    // ------------------------------------------------ epilogue (warps 2..kRecWarp-1)
+    // Warp w reads TMEM lanes 32*(w%4)..+31; the four warps of a lane
+    // quarter take 64-column slices of each tile, so every resident row has
+    // kColParts partial states, flushed to slots kColParts*segment + part.
     const int e = warp - 2;
     const int quarter = warp & 3;
-    const int half = e >> 2;
+    const int half = e >> 2;  // column slice index
     const int row = quarter * 32 + lane;
     const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
     constexpr int CW = Epi::kCW;
-    constexpr int NCH = (kBN / 2) / CW;
+    constexpr int NCH = (kBN / kColParts) / CW;
     Epi epi;
     int cur_a = -1;
     long long li = 0;
@@ -588,7 +595,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int b = (int)(x % g.n_b);
       if (a != cur_a) {
         if (cur_a >= 0 && !failed)
-          epi.flush(g, 2 * (unit - tile_owner((long long)cur_a * g.n_b, total, G)) + half);
+          epi.flush(g, kColParts * (unit - tile_owner((long long)cur_a * g.n_b, total, G)) + half);
         epi.begin(g, a * kResRows + (int)rank * kBM + row);
         cur_a = a;
       }
@@ -605,13 +612,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       {
         // Two register buffers: the TMEM load of chunk c+1 is in flight
         // while chunk c is processed.
-        const int col0 = half * (kBN / 2);
+        const int col0 = half * (kBN / kColParts);
         const uint32_t base = lane_addr + (uint32_t)(buf * kBN + col0);
         const float* rb = recs + col0 * Epi::kRec;
         const int gcol = b * kBN + col0;
         // Only a tile that reaches past the last vocab id / position needs
         // the masked chunk variant.
-        const bool tail = gcol + kBN / 2 > Epi::limit(g);
+        const bool tail = gcol + kBN / kColParts > Epi::limit(g);
         float ca[CW], cb[CW];
         tmem_ld<CW>(base, ca);
         tmem_ld_wait<CW>(ca);
@@ -637,7 +644,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (cur_a >= 0 && !failed)
-      epi.flush(g, 2 * (unit - tile_owner((long long)cur_a * g.n_b, total, G)) + half);
+      epi.flush(g, kColParts * (unit - tile_owner((long long)cur_a * g.n_b, total, G)) + half);
   } else if (warp == kRecWarp) {
     // ------------------------------------------------ record loader (both CTAs)
     // The records of tile li (256 columns, one contiguous block in global)
@@ -677,53 +684,64 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ------------------------------------------------------------- small kernels
 // h (bf16 / f16 / f32) -> f16 rows; s*U = s*(h16 . A); per-position record
 // {sU[0..R), M, 1/S, target, 0} (M, 1/S filled by lce_combine).  One warp
-// per position; positions in [T, Tpad) get an all-zero record with target
-// -1 so that pass 2 can read whole tiles.
+// per position (grid-stride), lane l converting elements 2l, 2l+1 of each
+// 64-element slice, so global accesses are coalesced and the A rows read
+// from shared memory are contiguous across lanes.  Positions in [T, Tpad)
+// get an all-zero record with target -1 so pass 2 can read whole tiles.
 template <int R>
 __global__ void lce_prep(const void* __restrict__ H, int dtype, int T, int Tpad, int d,
                          const float* __restrict__ A, float scale,
                          const int32_t* __restrict__ targets, int V,
                          __half* __restrict__ h16, float* __restrict__ tok, int* err) {
-  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  extern __shared__ __align__(16) float sA[];  // [d][R]
+  for (int k = threadIdx.x; k < d * R; k += blockDim.x) sA[k] = A[k];
+  __syncthreads();
   const int lane = threadIdx.x & 31;
-  if (w >= Tpad) return;
-  if (w >= T) {  // padding position: all fields zero, target -1
-    for (int f = lane; f < tok_stride(R); f += 32)
-      tok[tidx(w, f, R)] = f == R + 2 ? __int_as_float(-1) : 0.f;
-    return;
-  }
-  float u[R];
+  const int nw = (gridDim.x * blockDim.x) >> 5;
+  for (int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < Tpad; w += nw) {
+    if (w >= T) {  // padding position: all fields zero, target -1
+      for (int f = lane; f < tok_stride(R); f += 32)
+        tok[tidx(w, f, R)] = f == R + 2 ? __int_as_float(-1) : 0.f;
+      continue;
+    }
+    float u[R];
 #pragma unroll
-  for (int j = 0; j < R; ++j) u[j] = 0.f;
-  for (int i = lane; i < d; i += 32) {
-    const long long o = (long long)w * d + i;
-    float x;
-    if (dtype == 0) x = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(H)[o]);
-    else if (dtype == 1) x = __half2float(reinterpret_cast<const __half*>(H)[o]);
-    else x = reinterpret_cast<const float*>(H)[o];
-    const __half hv = __float2half_rn(x);
-    h16[o] = hv;
-    const float hf = __half2float(hv);
+    for (int j = 0; j < R; ++j) u[j] = 0.f;
+    for (int i = 2 * lane; i < d; i += 64) {
+      const long long o = (long long)w * d + i;
+      float2 x;
+      if (dtype == 0) x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(
+                          reinterpret_cast<const __nv_bfloat16*>(H) + o));
+      else if (dtype == 1) x = __half22float2(*reinterpret_cast<const __half2*>(
+                               reinterpret_cast<const __half*>(H) + o));
+      else x = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(H) + o);
+      const __half2 hv = __floats2half2_rn(x.x, x.y);
+      *reinterpret_cast<__half2*>(h16 + o) = hv;
+      const float2 hf = __half22float2(hv);
+      float a0[R], a1[R];
+      ld_vec<R>(sA + i * R, a0);
+      ld_vec<R>(sA + (i + 1) * R, a1);
 #pragma unroll
-    for (int j = 0; j < R; ++j) u[j] = fmaf(hf, A[i * R + j], u[j]);
-  }
-#pragma unroll
-  for (int j = 0; j < R; ++j) {
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) u[j] += __shfl_xor_sync(0xffffffffu, u[j], off);
-  }
-  if (lane == 0) {
-    int tg = targets[w];
-    if (tg < 0 || tg >= V) {
-      atomicCAS(err, 0, kErrTarget);
-      tg = 0;
+      for (int j = 0; j < R; ++j) u[j] = fmaf(hf.y, a1[j], fmaf(hf.x, a0[j], u[j]));
     }
 #pragma unroll
-    for (int j = 0; j < R; ++j) tok[tidx(w, j, R)] = scale * u[j];
-    tok[tidx(w, R, R)] = 0.f;
-    tok[tidx(w, R + 1, R)] = 0.f;
-    tok[tidx(w, R + 2, R)] = __int_as_float(tg);
-    tok[tidx(w, R + 3, R)] = 0.f;
+    for (int j = 0; j < R; ++j) {
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) u[j] += __shfl_xor_sync(0xffffffffu, u[j], off);
+    }
+    if (lane == 0) {
+      int tg = targets[w];
+      if (tg < 0 || tg >= V) {
+        atomicCAS(err, 0, kErrTarget);
+        tg = 0;
+      }
+#pragma unroll
+      for (int j = 0; j < R; ++j) tok[tidx(w, j, R)] = scale * u[j];
+      tok[tidx(w, R, R)] = 0.f;
+      tok[tidx(w, R + 1, R)] = 0.f;
+      tok[tidx(w, R + 2, R)] = __int_as_float(tg);
+      tok[tidx(w, R + 3, R)] = 0.f;
+    }
   }
 }
 
@@ -733,33 +751,44 @@ __global__ void lce_prep(const void* __restrict__ H, int dtype, int T, int Tpad,
 // (the reference's d_mid, src/train.c:161-168).  The record of t gets
 // M*log2(e) and 1/S for pass 2.
 template <int R>
-__global__ void lce_combine(int T, int res_rows, int n_b1, int G1, long long Tcap,
+__global__ void lce_combine(int T, int cparts, int res_rows, int n_b1, int G1, long long Tcap,
                             const float* __restrict__ p_max,
                             const float* __restrict__ p_sum, const float* __restrict__ p_q,
                             const float* __restrict__ z_tgt, const float* __restrict__ Bt,
                             float scale, float* __restrict__ tok, float* __restrict__ dU,
                             float* __restrict__ loss_tok) {
-  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  // one warp per position; lane k merges slots k, k+32, ... (fixed order)
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
   if (t >= T) return;
   const int a = t / res_rows;
   const long long total = (long long)((T + res_rows - 1) / res_rows) * n_b1;
   const int s0 = tile_owner((long long)a * n_b1, total, G1);
   const int s1 = tile_owner((long long)a * n_b1 + n_b1 - 1, total, G1);
-  const int nslot = 2 * (s1 - s0 + 1);
+  const int nslot = cparts * (s1 - s0 + 1);
   float M = -INFINITY;
-  for (int k = 0; k < nslot; ++k) M = fmaxf(M, p_max[(long long)k * Tcap + t]);
+  for (int k = lane; k < nslot; k += 32) M = fmaxf(M, p_max[(long long)k * Tcap + t]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
   float S = 0.f, Q[R];
 #pragma unroll
   for (int j = 0; j < R; ++j) Q[j] = 0.f;
-  for (int k = 0; k < nslot; ++k) {
+  for (int k = lane; k < nslot; k += 32) {
     const long long o = (long long)k * Tcap + t;
     const float pm = p_max[o];
-    if (pm == -INFINITY) continue;  // a half that saw no valid column
+    if (pm == -INFINITY) continue;  // a slice that saw no valid column
     const float f = expf(pm - M);
     S = fmaf(p_sum[o], f, S);
 #pragma unroll
     for (int j = 0; j < R; ++j) Q[j] = fmaf(p_q[o * R + j], f, Q[j]);
   }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    S += __shfl_xor_sync(0xffffffffu, S, off);
+#pragma unroll
+    for (int j = 0; j < R; ++j) Q[j] += __shfl_xor_sync(0xffffffffu, Q[j], off);
+  }
+  if (lane != 0) return;
   const float inv = 1.0f / S;
   const int tg = __float_as_int(tok[tidx(t, R + 2, R)]);
   const float pt = expf(z_tgt[t] - M) * inv;
@@ -783,40 +812,87 @@ template <int R>
 __global__ void lce_onehot(int T, const float* __restrict__ tok,
                            unsigned long long* __restrict__ corr_fx, int* err) {
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= T) return;
-  const int tg = __float_as_int(tok[tidx(t, R + 2, R)]);
+  const int lane = threadIdx.x & 31;
+  const bool valid = t < T;
+  const int tg = valid ? __float_as_int(tok[tidx(t, R + 2, R)]) : -1;
+  long long q[R];
 #pragma unroll
   for (int j = 0; j < R; ++j) {
-    const float u = tok[tidx(t, j, R)];
+    const float u = valid ? tok[tidx(t, j, R)] : 0.f;
     if (!(fabsf(u) < 131072.0f)) atomicCAS(err, 0, kErrRange);
-    const long long q = __float2ll_rn(u * kFixScale);
-    atomicAdd(&corr_fx[bidx(tg, j, R)], (unsigned long long)q);
+    q[j] = __float2ll_rn(u * kFixScale);
+  }
+  // Positions of one warp that share a target are added up first (integer
+  // sums, so the grouping does not change the result) and the lowest lane
+  // of each group issues the atomics: Zipf-skewed targets collide often.
+  long long sum[R];
+#pragma unroll
+  for (int j = 0; j < R; ++j) sum[j] = 0;
+  for (int k = 0; k < 32; ++k) {
+    const int tk = __shfl_sync(0xffffffffu, tg, k);
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+      const long long qk = __shfl_sync(0xffffffffu, q[j], k);
+      if (tk == tg) sum[j] += qk;
+    }
+  }
+  const unsigned peers = __match_any_sync(0xffffffffu, tg);
+  if (valid && lane == __ffs(peers) - 1) {
+#pragma unroll
+    for (int j = 0; j < R; ++j) atomicAdd(&corr_fx[bidx(tg, j, R)], (unsigned long long)sum[j]);
   }
 }
 
 // dA partials: gAp[c][i][j] = sum over the kDAChunk positions of chunk c
-// of h16[t][i] * dU[t][j].
-constexpr int kDAChunk = 64;
+// of h16[t][i] * dU[t][j].  Grid (chunks, d / 64); a block of 32 x Y
+// threads: thread (x, y) sums columns 2x, 2x+1 of its 64-column slice over
+// every Y-th position of the chunk, then the Y partial sums are added in a
+// fixed order.
+constexpr int kDAChunk = 256;
+__host__ __device__ constexpr int da_rows(int R) { return R <= 8 ? 16 : 4; }
 template <int R>
-__global__ void lce_dA_partial(int T, int d, const __half* __restrict__ h16,
-                               const float* __restrict__ dU, float* __restrict__ gAp) {
-  __shared__ float sdU[kDAChunk * R];
+__global__ void __launch_bounds__(32 * da_rows(R)) lce_dA_partial(int T, int d,
+                                                                  const __half* __restrict__ h16,
+                                                                  const float* __restrict__ dU,
+                                                                  float* __restrict__ gAp) {
+  constexpr int Y = da_rows(R);
+  constexpr int NT = 32 * Y;
+  __shared__ __align__(16) float sdU[kDAChunk * R];
+  __shared__ float sred[Y][64 * R];
   const int c = blockIdx.x;
   const int t0 = c * kDAChunk;
   const int nt = min(kDAChunk, T - t0);
-  for (int k = threadIdx.x; k < nt * R; k += blockDim.x) sdU[k] = dU[(long long)t0 * R + k];
+  const int tid = threadIdx.y * 32 + threadIdx.x;
+  for (int k = tid; k < nt * R; k += NT) sdU[k] = dU[(long long)t0 * R + k];
   __syncthreads();
-  for (int i = threadIdx.x; i < d; i += blockDim.x) {
-    float acc[R];
+  const int i = blockIdx.y * 64 + 2 * threadIdx.x;
+  float a0[R], a1[R];
 #pragma unroll
-    for (int j = 0; j < R; ++j) acc[j] = 0.f;
-    for (int tt = 0; tt < nt; ++tt) {
-      const float hv = __half2float(h16[(long long)(t0 + tt) * d + i]);
+  for (int j = 0; j < R; ++j) a0[j] = a1[j] = 0.f;
+  if (i < d) {
+    const __half* hp = h16 + (long long)t0 * d + i;
+#pragma unroll 4
+    for (int tt = threadIdx.y; tt < nt; tt += Y) {
+      const float2 hv = __half22float2(*reinterpret_cast<const __half2*>(hp + (long long)tt * d));
 #pragma unroll
-      for (int j = 0; j < R; ++j) acc[j] = fmaf(hv, sdU[tt * R + j], acc[j]);
+      for (int j = 0; j < R; ++j) {
+        a0[j] = fmaf(hv.x, sdU[tt * R + j], a0[j]);
+        a1[j] = fmaf(hv.y, sdU[tt * R + j], a1[j]);
+      }
     }
+  }
 #pragma unroll
-    for (int j = 0; j < R; ++j) gAp[((long long)c * d + i) * R + j] = acc[j];
+  for (int j = 0; j < R; ++j) {
+    sred[threadIdx.y][(2 * threadIdx.x) * R + j] = a0[j];
+    sred[threadIdx.y][(2 * threadIdx.x + 1) * R + j] = a1[j];
+  }
+  __syncthreads();
+  for (int k = tid; k < 64 * R; k += NT) {
+    float v = 0.f;
+#pragma unroll
+    for (int y = 0; y < Y; ++y) v += sred[y][k];
+    const int ii = blockIdx.y * 64 + k / R;
+    if (ii < d) gAp[((long long)c * d + ii) * R + (k % R)] = v;
   }
 }
 
@@ -824,7 +900,7 @@ __global__ void lce_dA_partial(int T, int d, const __half* __restrict__ h16,
 // sum of losses | n_pred].  Every output element is summed in a fixed
 // order, so the step is deterministic.
 template <int R>
-__global__ void lce_finalize(int T, int d, int V, long long Vpad, int n_chunks,
+__global__ void lce_finalize(int T, int cparts, int d, int V, long long Vpad, int n_chunks,
                              const float* __restrict__ gAp, int res_rows, int n_b2, int G2,
                              const float* __restrict__ gBp,
                              unsigned long long* __restrict__ corr_fx,
@@ -848,7 +924,7 @@ __global__ void lce_finalize(int T, int d, int V, long long Vpad, int n_chunks,
       const int a = v / res_rows;
       const int s0 = tile_owner((long long)a * n_b2, total2, G2);
       const int s1 = tile_owner((long long)a * n_b2 + n_b2 - 1, total2, G2);
-      for (int q = 0; q < 2 * (s1 - s0 + 1); ++q) s += gBp[(long long)q * Vpad * R + e];
+      for (int q = 0; q < cparts * (s1 - s0 + 1); ++q) s += gBp[(long long)q * Vpad * R + e];
       const long long c = (long long)corr_fx[e];
       if (c != 0) {
         s -= (float)((double)c * kFixInv);

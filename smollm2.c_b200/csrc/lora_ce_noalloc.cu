@@ -17,7 +17,7 @@
 //
 // Limits (checked, with a clear error): rank 4, positions T <= 4096,
 // vocabulary V <= 49152, hidden size d a multiple of 64 up to 576.  The
-// arrays below take about 7.3 MB on every GPU that loads the library, until
+// arrays below take about 8.9 MB on every GPU that loads the library, until
 // the process exits.  All calls share them and they keep the last call's
 // contents: calls that can overlap on the GPU (different streams, or
 // different host threads on one device) race and must be serialised by the
@@ -26,6 +26,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <mutex>
 #include <string>
 
@@ -40,7 +41,7 @@ constexpr int kNaRank = 4;
 constexpr int kNaMaxT = 4096;
 constexpr int kNaMaxV = 49152;
 constexpr int kNaMaxD = 576;
-constexpr long long kNaP1Cap = 65536;  // pass-1 partial slots x positions
+constexpr long long kNaP1Cap = 131072;  // pass-1 partial slots x positions (worst case 100,352)
 
 // Scratch: one set per process, shared by all calls on a device.
 static __device__ __align__(256) __half g_h16[(size_t)kNaMaxT * kNaMaxD];
@@ -133,7 +134,7 @@ int setup_device(int dev, DeviceScratch** out) {
       return na_fail(LORA_CE_ECUDA, "cudaGetDeviceProperties failed");
     cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3((unsigned)prop.multiProcessorCount);
-    lc.blockDim = dim3(kThreads);
+    lc.blockDim = dim3(block_threads(EpiLse<kNaRank>::kWarps));
     lc.dynamicSmemBytes = (size_t)smem;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -213,7 +214,8 @@ extern "C" int lora_ce_token_loss_noalloc(const uint16_t* d_W, int32_t vocab, in
   const long long total1 = (long long)n_a1 * n_b1;
   const int G1 = (int)(total1 < s->units ? total1 : s->units);
   const long long stride1 = (long long)n_a1 * res_rows;
-  if (2LL * max_seg(n_a1, n_b1, G1) * stride1 > kNaP1Cap)
+  const int cp1 = col_parts(EpiLse<R>::kWarps);
+  if ((long long)cp1 * max_seg(n_a1, n_b1, G1) * stride1 > kNaP1Cap)
     return na_fail(LORA_CE_ESTATE, "pass-1 partials exceed the static scratch");
   CUtensorMap mapH, mapW;
   if (!na_map(&mapH, s->h16, T, d, kBM) || !na_map(&mapW, d_W, V, d, kBM))
@@ -227,7 +229,9 @@ extern "C" int lora_ce_token_loss_noalloc(const uint16_t* d_W, int32_t vocab, in
     return na_fail(LORA_CE_ECUDA, "cudaMemcpyAsync failed");
   float* Bp = s->params + (size_t)d * R;
   na_pack_B<<<256, 256, 0, st>>>(d_B, V, Vpad, Bp);
-  lce_prep<R><<<(int)((Tpad * 32 + 255) / 256), 256, 0, st>>>(
+  if ((reinterpret_cast<uintptr_t>(d_H) & 15) != 0)
+    return na_fail(LORA_CE_EINVAL, "hidden states must be 16-byte aligned");
+  lce_prep<R><<<(int)std::min<long long>((Tpad + 7) / 8, 592), 256, (size_t)d * R * 4, st>>>(
       d_H, h_dtype, T, (int)Tpad, d, s->params, scale, d_targets, V, s->h16, s->tok, s->err);
   GemmArgs g{};
   g.kblocks = kblocks;
@@ -254,7 +258,7 @@ extern "C" int lora_ce_token_loss_noalloc(const uint16_t* d_W, int32_t vocab, in
       return na_fail(LORA_CE_ECUDA, "cudaFuncSetAttribute failed");
     cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3((unsigned)(G1 * 2));
-    lc.blockDim = dim3(kThreads);
+    lc.blockDim = dim3(block_threads(EpiLse<kNaRank>::kWarps));
     lc.dynamicSmemBytes = (size_t)smem;
     lc.stream = st;
     cudaLaunchAttribute attr[1];
@@ -267,7 +271,7 @@ extern "C" int lora_ce_token_loss_noalloc(const uint16_t* d_W, int32_t vocab, in
     if (cudaLaunchKernelEx(&lc, kern, mapH, mapW, g) != cudaSuccess)
       return na_fail(LORA_CE_ECUDA, "pass-1 launch failed");
   }
-  lce_combine<R><<<(T + 255) / 256, 256, 0, st>>>(T, res_rows, n_b1, G1, stride1, s->pmax,
+  lce_combine<R><<<(T + 7) / 8, 256, 0, st>>>(T, cp1, res_rows, n_b1, G1, stride1, s->pmax,
                                                   s->psum, s->pq, s->ztgt, Bp, scale, s->tok,
                                                   s->dU, d_loss);
   na_poison<<<(T + 255) / 256, 256, 0, st>>>(s->err, d_loss, T);

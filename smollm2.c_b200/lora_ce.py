@@ -58,6 +58,8 @@ def build(verbose: bool = False) -> str:
            "-ldl"]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
+    if os.path.exists(LIB_PATH):
+        os.remove(LIB_PATH)  # a failed build must not leave a stale library behind
     subprocess.run(cmd, check=True)
     return LIB_PATH
 
