@@ -219,6 +219,108 @@ def run_reference_arm(args):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------- merge
+def run_merge(args):
+    """Merge of the adapter into the tied lm_head (train_merge's
+    lora_patched_weight): W [49152x576] f16 in, patched f16 out.  HBM-bound;
+    algorithmic bytes per launch = 2*V*d (read W) + 2*V*d (write out) +
+    4*(d+V)*r (A, B).  The CPU leg times the oracle restatement of the same
+    merge (single thread) on the same inputs."""
+    import ctypes as C
+    import numpy as np
+    import torch
+    import lora_ce
+    import workload as wl
+
+    args.warmup = max(args.warmup, 3)
+    r = args.merge_rank
+    cpu = None
+    if not args.no_cpu_baseline:
+        import oracle as orc
+        o = orc.Oracle()
+        Wc = wl.make_weight(1, V, D)
+        rng = np.random.default_rng(5)
+        Ac = rng.standard_normal((D, r), dtype=np.float32)
+        Bc = rng.standard_normal((r, V), dtype=np.float32) * np.float32(1e-2)
+        t0 = time.perf_counter()
+        n = 0
+        while time.perf_counter() - t0 < 10.0:
+            o.merge(Wc, Ac, Bc, ALPHA / r)
+            n += 1
+        dt = time.perf_counter() - t0
+        cpu = {"value": n * 4.0 * V * D / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+               "sample": f"{n} full merges of W [49152x576], r {r} (oracle restatement of "
+                         "lora_patched_weight, one thread)"}
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lib = lora_ce.load_library()
+    W = torch.from_numpy(wl.make_weight(1, V, D).view(np.int16)).to(dev)
+    g = torch.Generator(device="cpu").manual_seed(5)
+    A = torch.randn(D, r, generator=g).to(dev)
+    B = (torch.randn(r, V, generator=g) * 1e-2).to(dev)
+    out = torch.empty_like(W)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    st = torch.cuda.current_stream(dev)
+
+    def launch():
+        rc = lib.lora_ce_merge_weight_device(C.c_void_p(W.data_ptr()), C.c_void_p(A.data_ptr()),
+                                             C.c_void_p(B.data_ptr()), D, r, V,
+                                             float(ALPHA / r), C.c_void_p(out.data_ptr()),
+                                             C.c_void_p(st.cuda_stream))
+        if rc != 0:
+            raise RuntimeError(lib.lora_ce_merge_last_error().decode())
+
+    for _ in range(args.warmup):
+        flush.fill_(1.0)
+        launch()
+    torch.cuda.synchronize(dev)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    with ClockSampler(0) as clk:
+        for s_, e_ in evs:
+            flush.fill_(1.0)
+            s_.record(st)
+            launch()
+            e_.record(st)
+        torch.cuda.synchronize(dev)
+    ms = [s_.elapsed_time(e_) for s_, e_ in evs]
+    t_ms = sum(ms) / len(ms)
+    alg = 4.0 * V * D + 4.0 * (D + V) * r
+    gbs = alg / (t_ms * 1e-3) / 1e9
+    # end to end through lora_ce_merge_weight (host buffers, copies inside)
+    Wh = wl.make_weight(1, V, D)
+    Ah, Bh = A.cpu().numpy(), B.cpu().numpy()
+    lora_ce.merge_weight(Wh, Ah, Bh, ALPHA / r)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        lora_ce.merge_weight(Wh, Ah, Bh, ALPHA / r)
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    _, hbm, peak_kind = peaks()
+    traffic = None
+    tp = os.path.join(REPO, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        with open(tp) as f:
+            traffic = json.load(f).get(f"merge_r{r}")
+    line = {
+        "metric": "LoRA merge into lm_head GB/s", "value": gbs, "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_ms,
+        "higher_is_better": True, "scaling": "replicas only", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded; W f16 N(0,0.02), A N(0,1), B N(0,1e-2))",
+        "config": {"workload": f"merge W [49152x576] f16 + (alpha/r) A B, r {r}, alpha 8",
+                   "rank": r, "l2": "flushed (256 MB write) before every launch"},
+        "roofline": {"kernel": "lce_merge", "bound": "hbm", "achieved": gbs, "peak": hbm,
+                     "unit": "GB/s", "frac": gbs / hbm, "peak_kind": f"{peak_kind} copy",
+                     "bytes_per_launch": alg, "traffic": traffic},
+        "cpu_baseline": cpu,
+        "e2e": {"value": alg / e2e_s / 1e9, "unit": "GB/s",
+                "h2d_bytes_per_step": int(2 * V * D + 4 * (D + V) * r),
+                "d2h_bytes_per_step": int(2 * V * D), "timer": "host wall clock"},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 # ----------------------------------------------------------------- GPU leg
 def main():
     ap = argparse.ArgumentParser()
@@ -227,9 +329,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--op", default="step", choices=["step", "merge"])
+    ap.add_argument("--merge-rank", type=int, default=R)
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference_arm(args)
+        return
+    if args.op == "merge":
+        run_merge(args)
         return
     args.warmup = max(args.warmup, 3)
 

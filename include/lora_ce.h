@@ -143,6 +143,27 @@ int32_t lora_ce_last_launches(lora_ce_handle* h);
 
 const char* lora_ce_last_error(void);
 
+/* LoRA merge into the tied lm_head, replacing lora_patched_weight
+ * (src/train.c:415-460, called by train_merge :465-542):
+ * out[v][i] = f16trunc(f32(W[v][i]) + scale * sum_k A[i][k] * B[k][v]) with
+ * the reference's exact arithmetic, including its merge-path f16 -> f32
+ * conversion (f16 subnormals halved) and its f32 -> f16 conversion, which
+ * keeps the low 16 bits of a mis-rebiased intermediate (src/train.c:392-407)
+ * and so differs from IEEE f16 for almost every weight: the output is
+ * bit-identical to the reference's merged tensor, defect included.
+ * Host buffers (W, out [V][d] f16
+ * bits; A [d][r], B [r][V]); rank <= 256 as LORA_MAX_RANK; d a multiple
+ * of 8.  The _device variant takes device pointers (W and out 16-byte
+ * aligned) and enqueues on `stream` without waiting. */
+int lora_ce_merge_weight(const uint16_t* W, const float* A_dxr, const float* B_rxv,
+                         int32_t dim, int32_t rank, int32_t vocab, float scale,
+                         uint16_t* out, int32_t device);
+int lora_ce_merge_weight_device(const uint16_t* d_W, const float* d_A,
+                                const float* d_B, int32_t dim, int32_t rank,
+                                int32_t vocab, float scale, uint16_t* d_out,
+                                void* stream);
+const char* lora_ce_merge_last_error(void);
+
 /* Per-position loss -log(softmax(h.W^T + scale.(h.A).B)[target] + 1e-12)
  * for callers that cannot allocate GPU memory at call time (a serving or
  * evaluation process whose memory is reserved up front, or a runtime that

@@ -390,6 +390,12 @@ float oracle_grad_check_softmax_ce(int vocab, float eps) {
 }
 
 /* Truncating f32 -> f16 of the merge path (src/train.c:393-409). */
+/* The merge path's f32 -> f16 conversion (src/train.c:392-407), restated
+ * as written: the normal branch adds 0x0C800000 and the subnormal branch
+ * shifts too little, so the intermediate exceeds 16 bits and the return
+ * type keeps the low 16 (the reference's own (uint16_t) cast).  The result
+ * differs from an IEEE conversion for almost every finite input; the
+ * forward path's converter (src/forward.c:250-258) does not have this. */
 uint16_t oracle_merge_f32_to_f16(float f) {
     uint32_t x;
     memcpy(&x, &f, 4);
@@ -408,6 +414,29 @@ uint16_t oracle_merge_f32_to_f16(float f) {
     return (uint16_t)(sign | ((em + 0xc800000) >> 13));
 }
 
+/* f16 -> f32 as the merge path converts it (src/train.c:433-454): exact for
+ * normal values, but an f16 subnormal m * 2^-24 comes out as m * 2^-25,
+ * because that normalisation loop starts from exponent 0 rather than 1.
+ * Reproduced here because the merged weights must match the reference's. */
+static float merge_f16_to_f32(uint16_t h) {
+    uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    uint32_t exp = (h >> 10) & 0x1fu;
+    uint32_t mant = h & 0x3ffu;
+    float f;
+    if (exp == 0) {
+        f = mant ? ldexpf((float)mant, -25) : 0.0f;
+        uint32_t u;
+        memcpy(&u, &f, 4);
+        u |= sign;
+        memcpy(&f, &u, 4);
+        return f;
+    }
+    /* exponent 31 (f16 inf / NaN) maps to 2^16 * 1.f, as the same formula does there */
+    uint32_t u = sign | ((exp + 112u) << 23) | (mant << 13);
+    memcpy(&f, &u, 4);
+    return f;
+}
+
 /* W' = f16trunc(f32(W) + scale * (A.B)^T), row v, col i (src/train.c:415-460). */
 void oracle_merge(const uint16_t* W, const float* A, const float* B, int d,
                   int r, int V, float scale, uint16_t* out) {
@@ -417,7 +446,7 @@ void oracle_merge(const uint16_t* W, const float* A, const float* B, int d,
             float s = 0.0f;
             for (int k = 0; k < r; k++) s += arow[k] * B[(size_t)k * V + v];
             float delta = scale * s;
-            float base = oracle_f16_to_f32(W[(size_t)v * d + i]);
+            float base = merge_f16_to_f32(W[(size_t)v * d + i]);
             out[(size_t)v * d + i] = oracle_merge_f32_to_f16(base + delta);
         }
     }

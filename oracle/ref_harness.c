@@ -142,3 +142,15 @@ int ref_save_adapter(int d, int V, int rank, int alpha, int step,
 float ref_grad_check_softmax_ce(int vocab, float eps) {
     return grad_check_softmax_ce(vocab, eps);
 }
+
+/* The reference's own merge arithmetic (lora_patched_weight, src/train.c:
+ * 415-460, with its truncating f32 -> f16 conversion), for pinning the
+ * oracle's restatement and the GPU merge kernel. */
+int ref_merge_weight(const uint16_t* W, const float* A, const float* B, int dim,
+                     int rank, int vocab, float scale, uint16_t* out) {
+    uint16_t* p = lora_patched_weight(W, A, B, dim, rank, vocab, scale, "token_embd.weight");
+    if (!p) return -1;
+    memcpy(out, p, (size_t)vocab * dim * sizeof(uint16_t));
+    free(p);
+    return 0;
+}

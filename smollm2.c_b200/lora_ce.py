@@ -44,7 +44,8 @@ EXPORTS = [
     "lora_ce_get_grads", "lora_ce_get_token_loss", "lora_ce_nccl_unique_id",
     "lora_ce_comm_init", "lora_ce_sync", "lora_ce_stream", "lora_ce_last_launches",
     "lora_ce_last_error", "lora_ce_set_profiling", "lora_ce_phase_times", "lora_ce_phase_name",
-    "lora_ce_token_loss_noalloc", "lora_ce_noalloc_last_error",
+    "lora_ce_token_loss_noalloc", "lora_ce_noalloc_last_error", "lora_ce_merge_weight",
+    "lora_ce_merge_weight_device", "lora_ce_merge_last_error",
 ]
 
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
@@ -53,7 +54,7 @@ NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", 
 
 def build(verbose: bool = False) -> str:
     """Compile csrc/ into liblora_ce.so (sm_100a) next to this file."""
-    srcs = [os.path.join(HERE, "csrc", f) for f in ("lora_ce_api.cu", "lora_ce_noalloc.cu")]
+    srcs = [os.path.join(HERE, "csrc", f) for f in ("lora_ce_api.cu", "lora_ce_noalloc.cu", "lora_ce_merge.cu")]
     cmd = ["nvcc", *NVCC_FLAGS, "-I" + os.path.join(REPO, "include"), "-o", LIB_PATH, *srcs,
            "-ldl"]
     if verbose:
@@ -116,6 +117,14 @@ def load_library() -> C.CDLL:
     lib.lora_ce_token_loss_noalloc.restype = C.c_int
     lib.lora_ce_noalloc_last_error.argtypes = []
     lib.lora_ce_noalloc_last_error.restype = C.c_char_p
+    lib.lora_ce_merge_weight.argtypes = [vp, vp, vp, C.c_int32, C.c_int32, C.c_int32, C.c_float,
+                                         vp, C.c_int32]
+    lib.lora_ce_merge_weight.restype = C.c_int
+    lib.lora_ce_merge_weight_device.argtypes = [vp, vp, vp, C.c_int32, C.c_int32, C.c_int32,
+                                                C.c_float, vp, vp]
+    lib.lora_ce_merge_weight_device.restype = C.c_int
+    lib.lora_ce_merge_last_error.argtypes = []
+    lib.lora_ce_merge_last_error.restype = C.c_char_p
     lib.lora_ce_last_error.argtypes = []
     lib.lora_ce_last_error.restype = C.c_char_p
     for name in ["lora_ce_create", "lora_ce_destroy", "lora_ce_set_weight_f16",
@@ -135,6 +144,26 @@ def _check(rc: int, what: str) -> None:
 
 def _ptr(a: np.ndarray) -> C.c_void_p:
     return C.c_void_p(a.ctypes.data)
+
+
+def merge_weight(W16: np.ndarray, A_dr: np.ndarray, B_rv: np.ndarray, scale: float,
+                 device: int = 0) -> np.ndarray:
+    """LoRA merge into the tied lm_head on the GPU (lora_patched_weight's
+    arithmetic, bit-exact): returns the patched [V][d] f16 bit patterns."""
+    W16 = np.ascontiguousarray(W16, np.uint16)
+    A = np.ascontiguousarray(A_dr, np.float32)
+    B = np.ascontiguousarray(B_rv, np.float32)
+    V, d = W16.shape
+    r = A.shape[1]
+    assert A.shape == (d, r) and B.shape == (r, V)
+    out = np.empty_like(W16)
+    lib = load_library()
+    rc = lib.lora_ce_merge_weight(_ptr(W16), _ptr(A), _ptr(B), d, r, V, float(scale), _ptr(out),
+                                  device)
+    if rc != 0:
+        msg = lib.lora_ce_merge_last_error().decode(errors="replace")
+        raise LoraCEError(f"lora_ce_merge_weight failed: {ERRORS.get(rc, rc)}: {msg}")
+    return out
 
 
 def token_loss_noalloc(d_W: int, vocab: int, dim: int, d_A: int, d_B: int, scale: float,

@@ -40,6 +40,21 @@ def sha(a: np.ndarray) -> str:
     return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
 
 
+EDGE_F16 = [0x0001, 0x8001, 0x03FF, 0x83FF, 0x0200, 0x7C00, 0xFC00, 0x7E00, 0x0000, 0x8000,
+            0x7BFF, 0xFBFF, 0x0400, 0x8400]
+
+
+def merge_inputs():
+    """Seeded W (4099 x 576) with f16 edge patterns, A [576][8], B [8][4099]."""
+    W = wl.make_weight(77, 4099, 576)
+    W[0, :len(EDGE_F16)] = np.array(EDGE_F16, np.uint16)
+    W[4098, -len(EDGE_F16):] = np.array(EDGE_F16, np.uint16)
+    rng = np.random.default_rng(77)
+    A = rng.standard_normal((576, 8), dtype=np.float32)
+    B = (rng.standard_normal((8, 4099), dtype=np.float32) * np.float32(0.3)).astype(np.float32)
+    return W, A, B
+
+
 def case_inputs(V, d, r, T, seed):
     W = wl.make_weight(seed, V, d)
     h, tgt, A, B = wl.make_step_inputs(seed, T, V, d, r)
@@ -82,6 +97,18 @@ def main() -> None:
         data = open(p, "rb").read()
     meta["lora0001_seed9"] = {"size": len(data), "sha": hashlib.sha256(data).hexdigest(),
                               "alpha": 8, "step": 7}
+    # the reference's merge (lora_patched_weight): seeded W with f16 edge
+    # patterns (subnormals, inf, NaN, zeros), A, B, scale 2
+    Wm, Am, Bm = merge_inputs()
+    out = np.empty_like(Wm)
+    f = ref.lib.ref_merge_weight
+    u16 = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
+    f32 = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+    import ctypes as C
+    f.argtypes = [u16, f32, f32, C.c_int, C.c_int, C.c_int, C.c_float, u16]
+    f.restype = C.c_int
+    assert f(Wm, Am, Bm, Wm.shape[1], Am.shape[1], Wm.shape[0], 2.0, out) == 0
+    meta["merge_4099x576_r8"] = {"sha": sha(out), "changed": int((out != Wm).sum())}
     with open(os.path.join(HERE, "golden.json"), "w") as f:
         json.dump(meta, f, indent=1, sort_keys=True)
     print("grad_check", meta["grad_check_softmax_ce"], "lora0001 bytes", len(data))

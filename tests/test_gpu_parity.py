@@ -219,3 +219,39 @@ def test_full_size_isolated_op(oracle):
     assert rel(sums[0][1] + sums[1][1], gB * n) <= 1e-5
     assert abs(sums[0][2] + sums[1][2] - lsum) <= 1e-5 * lsum
     m.close()
+
+
+@pytest.mark.parametrize("rank", [4, 64, 256])
+def test_merge_bit_exact(oracle, rank):
+    """GPU merge == the reference's merge arithmetic, bit for bit, on the
+    full 49152 x 576 lm_head with f16 edge patterns."""
+    V, d = 49152, 576
+    W = wl.make_weight(90 + rank, V, d)
+    edge = np.array([0x0001, 0x8001, 0x03FF, 0x83FF, 0x0200, 0x7C00, 0xFC00, 0x7E00, 0x0000,
+                     0x8000, 0x7BFF, 0xFBFF, 0x0400, 0x8400], np.uint16)
+    W[0, :len(edge)] = edge
+    W[V - 1, -len(edge):] = edge
+    rng = np.random.default_rng(rank)
+    A = rng.standard_normal((d, rank), dtype=np.float32) * np.float32(1.0 / np.sqrt(d))
+    B = rng.standard_normal((rank, V), dtype=np.float32) * np.float32(1e-2)
+    got = lora_ce.merge_weight(W, A, B, 16.0 / rank)
+    if rank == 4:
+        ref = oracle.merge(W, A, B, 16.0 / rank)
+    else:  # the full oracle merge at rank 256 takes minutes; check a row sample
+        rows = np.r_[0:64, V - 64:V]
+        ref_rows = oracle.merge(np.ascontiguousarray(W[rows]), A, np.ascontiguousarray(B[:, rows]),
+                                16.0 / rank)
+        got, ref = got[rows], ref_rows
+    np.testing.assert_array_equal(got, ref)
+
+
+@pytest.mark.parametrize("V,d,r", [(4099, 1096, 256), (1000, 64, 1), (333, 2048, 5)])
+def test_merge_ragged_shapes(oracle, V, d, r):
+    """Column tiles that do not divide d, V off the row tile, rank 1, and
+    the k-chunked path (rank 256 at d = 1096)."""
+    W = wl.make_weight(V + d + r, V, d)
+    rng = np.random.default_rng(V * r)
+    A = rng.standard_normal((d, r), dtype=np.float32) * np.float32(0.05)
+    B = rng.standard_normal((r, V), dtype=np.float32) * np.float32(0.05)
+    np.testing.assert_array_equal(lora_ce.merge_weight(W, A, B, 8.0 / r),
+                                  oracle.merge(W, A, B, 8.0 / r))

@@ -117,3 +117,15 @@ def test_target_indexing_edge_cases(oracle):
     W, H, tokens, A, B = case_inputs(512, 64, 4, 5, 2)
     assert oracle.train_step_tokens(W, A, B, H, tokens[:1], 4096, 2.0, 1e-3)["loss"] == -1.0
     assert oracle.train_step_tokens(W, A, B, H, tokens, 1, 2.0, 1e-3)["loss"] == -1.0
+
+
+def test_merge_matches_reference_fixture(oracle, golden):
+    """oracle/lora_oracle.c's merge reproduces the reference's
+    lora_patched_weight bit for bit (f16 edge patterns included)."""
+    import sys
+    sys.path.insert(0, GOLDEN)
+    from make_golden import merge_inputs
+    W, A, B = merge_inputs()
+    out = oracle.merge(W, A, B, 2.0)
+    assert sha(out) == golden["merge_4099x576_r8"]["sha"]
+    assert int((out != W).sum()) == golden["merge_4099x576_r8"]["changed"]
