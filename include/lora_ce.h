@@ -50,7 +50,8 @@ extern "C" {
 typedef struct lora_ce_config {
     int32_t dim;        /* d: hidden size, multiple of 64, <= 640 (576) */
     int32_t vocab;      /* V: vocabulary size (49152) */
-    int32_t rank;       /* r: 4, 8 or 16 */
+    int32_t rank;       /* r: 1..16 (run at 4, 8 or 16 with zero padding,
+                           which leaves every result unchanged) */
     float scale;        /* alpha / r (train_create: src/train.c:62-63) */
     float lr;           /* learning rate */
     float beta1;        /* 0.9   (ADAM_B1, src/train.c:23) */
@@ -87,6 +88,10 @@ int lora_ce_set_weight_f16(lora_ce_handle* h, const uint16_t* W);
  * carries no optimizer state). */
 int lora_ce_set_adapter(lora_ce_handle* h, const float* A_dxr,
                         const float* B_rxv, int32_t step);
+
+/* Set the LoRA scale alpha/r used by the following steps (train_load takes
+ * the scale stored in the LORA0001 file, src/train.c:278). */
+int lora_ce_set_scale(lora_ce_handle* h, float scale);
 
 /* Read the adapter back in the reference layouts (what train_save writes,
  * src/train.c:244-259).  Any pointer may be NULL. */

@@ -154,3 +154,38 @@ int ref_merge_weight(const uint16_t* W, const float* A, const float* B, int dim,
     free(p);
     return 0;
 }
+
+/* The reference's own train_run (src/train.c:295-389) over a packed dataset,
+ * every sample's hidden rows served from H by position, with the adapter
+ * from train_create (seeded Kaiming A, B = 0).  Returns train_run's rc. */
+int ref_train_run(int d, int V, int rank, int alpha, float lr, int seq_max, int seed,
+                  int epochs, int max_steps, int checkpoint_every, const uint16_t* W,
+                  const float* H, int n_pos, const char* packed, const char* out_dir) {
+    forward_ctx f = {d, V, W, H, n_pos, 0, NULL};
+    f.wrow = (float*)malloc((size_t)d * sizeof(float));
+    train_params p;
+    memset(&p, 0, sizeof(p));
+    p.mode = TRAIN_LORA;
+    p.lora_rank = rank;
+    p.lora_alpha = alpha;
+    p.seq_max = seq_max;
+    p.batch = 1;
+    p.lr = lr;
+    p.epochs = epochs;
+    p.max_steps = max_steps;
+    p.checkpoint_every = checkpoint_every;
+    p.seed = seed;
+    train_state* t = train_create(&f, &p);
+    int rc = t ? train_run(t, packed, &p, out_dir) : -1;
+    fflush(stdout);
+    if (t) train_free(t);
+    free(f.wrow);
+    return rc;
+}
+
+/* The reference's own train_merge (src/train.c:465-542). */
+int ref_train_merge(const char* base_gguf, const char* adapter, const char* out_gguf) {
+    int rc = train_merge(base_gguf, adapter, out_gguf);
+    fflush(stdout);
+    return rc;
+}

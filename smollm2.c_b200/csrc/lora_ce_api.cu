@@ -126,7 +126,11 @@ int max_segments(int n_a, int n_b, int G) {
 
 struct lora_ce_handle {
   lora_ce_config cfg{};
-  int R = 0, d = 0, V = 0;
+  // r: the adapter's rank; R: the rank the kernels run at, r rounded up to
+  // 4, 8 or 16.  The extra columns of A and rows of B are zero and stay
+  // zero (their U, dU, dA and dB terms are exactly 0, so Adam leaves them at
+  // 0), which makes a rank-r step identical to the reference's.
+  int r = 0, R = 0, d = 0, V = 0;
   long long Vpad = 0, Tcap = 0;
   int num_sms = 0;
   int pair = 2;             // 2: CTA-pair (cta_group::2) GEMM tiles; 1: single-CTA tiles
@@ -195,8 +199,7 @@ int check_cfg(const lora_ce_config* c) {
   if (c->dim < 64 || c->dim % 64 != 0 || c->dim > 64 * kMaxKBlocks)
     return fail(LORA_CE_EINVAL, "dim must be a multiple of 64 in [64, 640]");
   if (c->vocab < 1) return fail(LORA_CE_EINVAL, "vocab must be positive");
-  if (c->rank != 4 && c->rank != 8 && c->rank != 16)
-    return fail(LORA_CE_EINVAL, "rank must be 4, 8 or 16");
+  if (c->rank < 1 || c->rank > 16) return fail(LORA_CE_EINVAL, "rank must be in [1, 16]");
   if (c->max_tokens < 1) return fail(LORA_CE_EINVAL, "max_tokens must be positive");
   if (!(c->lr >= 0.f) || !(c->eps > 0.f) || !(c->beta1 >= 0.f && c->beta1 < 1.f) ||
       !(c->beta2 >= 0.f && c->beta2 < 1.f) || !(c->weight_decay >= 0.f) ||
@@ -484,7 +487,8 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
   lora_ce_handle* h = new (std::nothrow) lora_ce_handle();
   if (!h) return fail(LORA_CE_ENOMEM, "host allocation failed");
   h->cfg = *cfg;
-  h->R = cfg->rank;
+  h->r = cfg->rank;
+  h->R = cfg->rank <= 4 ? 4 : cfg->rank <= 8 ? 8 : 16;
   h->d = cfg->dim;
   h->V = cfg->vocab;
   h->Vpad = round_up(cfg->vocab, kBN);
@@ -596,12 +600,15 @@ int lora_ce_set_weight_f16(lora_ce_handle* h, const uint16_t* W) {
 int lora_ce_set_adapter(lora_ce_handle* h, const float* A, const float* B, int32_t step) {
   if (!h || !A || !B || step < 0) return fail(LORA_CE_EINVAL, "bad argument");
   LCE_CUDA(cudaSetDevice(h->cfg.device));
-  const int R = h->R, d = h->d, V = h->V;
+  const int r = h->r, R = h->R, d = h->d, V = h->V;
   std::vector<float> Bt((size_t)h->Vpad * R, 0.f);
-  for (int j = 0; j < R; ++j)
+  for (int j = 0; j < r; ++j)
     for (int v = 0; v < V; ++v) Bt[(size_t)bidx(v, j, R)] = B[(size_t)j * V + v];
   const size_t nA = (size_t)d * R;
-  LCE_CUDA(cudaMemcpyAsync(h->params, A, nA * 4, cudaMemcpyHostToDevice, h->stream));
+  std::vector<float> Ap(nA, 0.f);
+  for (int i = 0; i < d; ++i)
+    for (int j = 0; j < r; ++j) Ap[(size_t)i * R + j] = A[(size_t)i * r + j];
+  LCE_CUDA(cudaMemcpyAsync(h->params, Ap.data(), nA * 4, cudaMemcpyHostToDevice, h->stream));
   LCE_CUDA(cudaMemcpyAsync(h->params + nA, Bt.data(), Bt.size() * 4, cudaMemcpyHostToDevice,
                            h->stream));
   const size_t np = nA + Bt.size();
@@ -612,18 +619,29 @@ int lora_ce_set_adapter(lora_ce_handle* h, const float* A, const float* B, int32
   return 0;
 }
 
+int lora_ce_set_scale(lora_ce_handle* h, float scale) {
+  if (!h || !std::isfinite(scale)) return fail(LORA_CE_EINVAL, "bad argument");
+  h->cfg.scale = scale;
+  return 0;
+}
+
 int lora_ce_get_adapter(lora_ce_handle* h, float* A, float* B, int32_t* step) {
   if (!h) return fail(LORA_CE_EINVAL, "null handle");
   LCE_CUDA(cudaSetDevice(h->cfg.device));
   int rc = check_device_error(h);
   if (rc) return rc;
-  const int R = h->R, d = h->d, V = h->V;
-  if (A) LCE_CUDA(cudaMemcpy(A, h->params, (size_t)d * R * 4, cudaMemcpyDeviceToHost));
+  const int r = h->r, R = h->R, d = h->d, V = h->V;
+  if (A) {
+    std::vector<float> Ap((size_t)d * R);
+    LCE_CUDA(cudaMemcpy(Ap.data(), h->params, Ap.size() * 4, cudaMemcpyDeviceToHost));
+    for (int i = 0; i < d; ++i)
+      for (int j = 0; j < r; ++j) A[(size_t)i * r + j] = Ap[(size_t)i * R + j];
+  }
   if (B) {
     std::vector<float> Bt((size_t)h->Vpad * R);
     LCE_CUDA(cudaMemcpy(Bt.data(), h->params + (size_t)d * R, Bt.size() * 4,
                         cudaMemcpyDeviceToHost));
-    for (int j = 0; j < R; ++j)
+    for (int j = 0; j < r; ++j)
       for (int v = 0; v < V; ++v) B[(size_t)j * V + v] = Bt[(size_t)bidx(v, j, R)];
   }
   if (step) *step = h->step;
@@ -635,12 +653,17 @@ int lora_ce_get_grads(lora_ce_handle* h, float* gA, float* gB, float* loss_sum, 
   LCE_CUDA(cudaSetDevice(h->cfg.device));
   int rc = check_device_error(h);
   if (rc) return rc;
-  const int R = h->R, d = h->d, V = h->V;
-  if (gA) LCE_CUDA(cudaMemcpy(gA, h->gmean, (size_t)d * R * 4, cudaMemcpyDeviceToHost));
+  const int r = h->r, R = h->R, d = h->d, V = h->V;
+  if (gA) {
+    std::vector<float> t((size_t)d * R);
+    LCE_CUDA(cudaMemcpy(t.data(), h->gmean, t.size() * 4, cudaMemcpyDeviceToHost));
+    for (int i = 0; i < d; ++i)
+      for (int j = 0; j < r; ++j) gA[(size_t)i * r + j] = t[(size_t)i * R + j];
+  }
   if (gB) {
     std::vector<float> t((size_t)h->Vpad * R);
     LCE_CUDA(cudaMemcpy(t.data(), h->gmean + (size_t)d * R, t.size() * 4, cudaMemcpyDeviceToHost));
-    for (int j = 0; j < R; ++j)
+    for (int j = 0; j < r; ++j)
       for (int v = 0; v < V; ++v) gB[(size_t)j * V + v] = t[(size_t)bidx(v, j, R)];
   }
   const long long nparam = (long long)d * R + h->Vpad * R;

@@ -21,17 +21,6 @@ int merge_fail(int code, const char* msg) {
   return code;
 }
 
-__device__ __forceinline__ float merge_f16_bits_to_f32(uint32_t h) {
-  const uint32_t sign = (h & 0x8000u) << 16;
-  const uint32_t exp = (h >> 10) & 0x1fu;
-  const uint32_t mant = h & 0x3ffu;
-  if (exp == 0) {
-    const float f = mant ? __fmul_rn((float)mant, 2.98023223876953125e-8f /* 2^-25 */) : 0.0f;
-    return __uint_as_float(__float_as_uint(f) | sign);
-  }
-  return __uint_as_float(sign | ((exp + 112u) << 23) | (mant << 13));
-}
-
 // The merge path's f32 -> f16 conversion, as the reference writes it
 // (src/train.c:392-407).  Its normal-range branch adds 0x0C800000 (not the
 // 0xC8000000 that rebiases the exponent) and its subnormal branch shifts the
@@ -91,7 +80,10 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 // results differ took the fused value), and the reference rounds the
 // product and the sum separately.
 
-// merge_f16_bits_to_f32 without a branch.  For exponent 1..31,
+// The merge path's f16 -> f32 conversion (src/train.c:433-454): exact for
+// exponent 1..30, exponent 31 (inf / NaN) becomes 2^16 * 1.f, and a
+// subnormal mant * 2^-24 becomes mant * 2^-25 (its normalisation loop starts
+// from exponent 0).  Written without a branch: for exponent 1..31,
 // ((h & 0x7fff) << 13) + (112 << 23) is (exp + 112) << 23 | mant << 13 (no
 // carry: exp + 112 <= 143).  For exponent 0 the same bits are
 // 2^-15 * (1 + mant * 2^-10) = 2^-15 + mant * 2^-25, so subtracting 2^-15

@@ -45,7 +45,7 @@ EXPORTS = [
     "lora_ce_comm_init", "lora_ce_sync", "lora_ce_stream", "lora_ce_last_launches",
     "lora_ce_last_error", "lora_ce_set_profiling", "lora_ce_phase_times", "lora_ce_phase_name",
     "lora_ce_token_loss_noalloc", "lora_ce_noalloc_last_error", "lora_ce_merge_weight",
-    "lora_ce_merge_weight_device", "lora_ce_merge_last_error",
+    "lora_ce_merge_weight_device", "lora_ce_merge_last_error", "lora_ce_set_scale",
 ]
 
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
@@ -94,6 +94,7 @@ def load_library() -> C.CDLL:
     lib.lora_ce_destroy.argtypes = [vp]
     lib.lora_ce_set_weight_f16.argtypes = [vp, vp]
     lib.lora_ce_set_adapter.argtypes = [vp, vp, vp, C.c_int32]
+    lib.lora_ce_set_scale.argtypes = [vp, C.c_float]
     lib.lora_ce_get_adapter.argtypes = [vp, vp, vp, C.POINTER(C.c_int32)]
     lib.lora_ce_step.argtypes = [vp, vp, C.c_int32, C.c_int32, vp, C.POINTER(C.c_float)]
     lib.lora_ce_step_device.argtypes = [vp, vp, C.c_int32, C.c_int32, vp, vp]
@@ -255,6 +256,10 @@ class LoraCE:
         assert A.shape == (self.cfg.dim, self.cfg.rank)
         assert B.shape == (self.cfg.rank, self.cfg.vocab)
         _check(self.lib.lora_ce_set_adapter(self.h, _ptr(A), _ptr(B), step), "set_adapter")
+
+    def set_scale(self, scale: float) -> None:
+        _check(self.lib.lora_ce_set_scale(self.h, float(scale)), "set_scale")
+        self.cfg.scale = float(scale)
 
     def get_adapter(self):
         A = np.empty((self.cfg.dim, self.cfg.rank), np.float32)

@@ -1,0 +1,143 @@
+"""Test infrastructure for the trainer API (smollm2.c_b200/liblora_train.so):
+files in the reference's formats and the ctypes glue.
+
+- write_gguf: a GGUF v3 file (the public format the reference's
+  src/gguf.c reads: magic, version 3, tensor and key/value counts, the
+  key/value table, the tensor table, data aligned to 32 bytes).
+- write_packed: a packed dataset as src/data.c writes it: <path> holds the
+  int32 token ids, <path>.idx the 16-byte sample_idx records
+  {int32 n_tokens, pad, int64 offset} and the 20-byte trailer
+  {int32 n_samples, int32 total_tokens, int32 fmt, "STUDIO\\0\\0"}.
+- TrainerEnv: loads oracle/_ref/libstudio_env.so (the stand-in body forward
+  plus the reference's gguf / gguf_write / hw_probe code) into the global
+  symbol scope, then liblora_train.so, which resolves against it.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import struct
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(HERE)
+ENV_SO = os.path.join(REPO, "oracle", "_ref", "libstudio_env.so")
+TRAIN_SO = os.path.join(REPO, "smollm2.c_b200", "liblora_train.so")
+
+GGUF_F32, GGUF_F16 = 0, 1
+GGUF_V_UINT32, GGUF_V_STRING = 4, 8
+
+
+def _gguf_str(s: str) -> bytes:
+    b = s.encode()
+    return struct.pack("<Q", len(b)) + b
+
+
+def write_gguf(path: str, tensors, kv=()) -> None:
+    """tensors: (name, dims (innermost first), dtype, raw bytes); kv:
+    (key, "u32" | "str", value)."""
+    head = struct.pack("<IIQQ", 0x46554747, 3, len(tensors), len(kv))
+    for key, typ, val in kv:
+        head += _gguf_str(key)
+        if typ == "u32":
+            head += struct.pack("<II", GGUF_V_UINT32, val)
+        else:
+            head += struct.pack("<I", GGUF_V_STRING) + _gguf_str(val)
+    offs, off = [], 0
+    for _, _, _, raw in tensors:
+        offs.append(off)
+        off = (off + len(raw) + 31) // 32 * 32
+    for (name, dims, dtype, _), o in zip(tensors, offs):
+        head += _gguf_str(name) + struct.pack("<I", len(dims))
+        head += b"".join(struct.pack("<Q", x) for x in dims)
+        head += struct.pack("<IQ", dtype, o)
+    pad = (-len(head)) % 32
+    with open(path, "wb") as f:
+        f.write(head + b"\0" * pad)
+        for (_, _, _, raw), o in zip(tensors, offs):
+            f.write(raw)
+            f.write(b"\0" * ((-len(raw)) % 32))
+
+
+def write_packed(path: str, samples) -> None:
+    idx = b""
+    off = 0
+    total = 0
+    with open(path, "wb") as f:
+        for s in samples:
+            a = np.asarray(s, np.int32)
+            f.write(a.tobytes())
+            idx += struct.pack("<iiq", len(a), 0, off)
+            off += a.nbytes
+            total += len(a)
+    with open(path + ".idx", "wb") as f:
+        f.write(idx + struct.pack("<iii", len(samples), total, 0) + b"STUDIO\0\0")
+
+
+class TrainParams(C.Structure):
+    """src/train.h:11-23."""
+    _fields_ = [("mode", C.c_int), ("lora_rank", C.c_int), ("lora_alpha", C.c_int),
+                ("seq_max", C.c_int), ("batch", C.c_int), ("lr", C.c_float),
+                ("epochs", C.c_int), ("checkpoint_every", C.c_int), ("max_steps", C.c_int),
+                ("seed", C.c_int), ("simulate_mem_kb", C.c_long)]
+
+
+def available() -> bool:
+    return os.path.exists(ENV_SO) and os.path.exists(TRAIN_SO)
+
+
+class TrainerEnv:
+    def __init__(self) -> None:
+        vp = C.c_void_p
+        self.env = C.CDLL(ENV_SO, mode=C.RTLD_GLOBAL)
+        self.lib = C.CDLL(TRAIN_SO)
+        self.libc = C.CDLL(None)
+        e, t = self.env, self.lib
+        e.env_forward_create.argtypes = [C.c_int, C.c_int, vp, C.c_int]
+        e.env_forward_create.restype = vp
+        e.env_forward_free.argtypes = [vp]
+        e.env_forward_calls.argtypes = [vp, C.POINTER(C.c_int)]
+        e.env_gguf_open.argtypes = [C.c_char_p]
+        e.env_gguf_open.restype = vp
+        e.env_gguf_close.argtypes = [vp]
+        e.env_gguf_tensor.argtypes = [C.c_char_p, C.c_char_p, C.POINTER(C.c_uint64),
+                                      C.POINTER(C.c_int), vp, C.c_size_t]
+        e.gguf_patch_tensor.argtypes = [C.c_char_p, C.c_char_p, C.c_char_p, vp, C.c_size_t]
+        t.train_create.argtypes = [vp, C.POINTER(TrainParams)]
+        t.train_create.restype = vp
+        t.train_free.argtypes = [vp]
+        t.train_step.argtypes = [vp, vp, C.c_int]
+        t.train_step.restype = C.c_float
+        t.train_save.argtypes = [vp, C.c_char_p]
+        t.train_load.argtypes = [vp, C.c_char_p]
+        t.train_run.argtypes = [vp, C.c_char_p, C.POINTER(TrainParams), C.c_char_p]
+        t.train_merge.argtypes = [C.c_char_p, C.c_char_p, C.c_char_p]
+        t.lora_train_set_lm_head.argtypes = [vp, vp]
+        t.lora_train_set_lm_head_gguf.argtypes = [vp, vp]
+
+    def forward(self, H: np.ndarray, vocab: int):
+        """A stand-in forward serving the rows of H (kept alive by the caller)."""
+        return self.env.env_forward_create(H.shape[1], vocab, H.ctypes.data, H.shape[0])
+
+    def forward_calls(self, f):
+        c = (C.c_int * 3)()
+        self.env.env_forward_calls(f, c)
+        return tuple(c)
+
+    def gguf_tensor(self, path: str, name: str, nbytes: int):
+        dims = (C.c_uint64 * 2)()
+        dt = C.c_int()
+        out = np.empty(nbytes, np.uint8)
+        rc = self.env.env_gguf_tensor(path.encode(), name.encode(), dims, C.byref(dt),
+                                      out.ctypes.data, nbytes)
+        return rc, (dims[0], dims[1]), dt.value, out
+
+    def flush(self) -> None:
+        self.libc.fflush(None)
+
+
+def params(rank=4, alpha=8, seq_max=256, lr=1e-3, epochs=1, checkpoint_every=0, max_steps=0,
+           seed=42, simulate_mem_kb=0) -> TrainParams:
+    return TrainParams(0, rank, alpha, seq_max, 1, lr, epochs, checkpoint_every, max_steps, seed,
+                       simulate_mem_kb)
