@@ -38,11 +38,41 @@ T_PER_GPU = 8192
 LR, WD = 1e-3, 0.01
 METRIC = "LoRA lm_head CE fwd+bwd tokens/s"
 UNIT = "tokens/s"
-# FLOPs per predicted token of the whole step (two GEMM passes with the
-# rank-r terms, dA): 4*V*d + 8*V*r + 4*d*r.
-F_TOK = 4 * V * D + 8 * V * R + 4 * D * R
-# FLOPs per token of one GEMM pass kernel: 2*V*d (tensor) + 4*V*r (rank terms).
-F_PASS = 2 * V * D + 4 * V * R
+# The workloads (--config): 2 is the default bench line; 3 and 4 are the
+# rank-16 strong-scaling and the Q4_K (QLoRA) lm_head configurations.
+CONFIGS = {
+    2: dict(rank=4, alpha=8, tokens=8192, scaling="weak", q4k=False,
+            desc="isolated fused LoRA lm_head CE fwd+bwd+AdamW step: h [8192x576] bf16 per GPU, "
+                 "W [49152x576] f16, r 4, alpha 8"),
+    3: dict(rank=16, alpha=32, tokens=65536, scaling="strong", q4k=False,
+            desc="rank 16, 65536 positions split evenly over the GPUs, W [49152x576] f16, "
+                 "alpha 32, dA/dB all-reduce before AdamW"),
+    4: dict(rank=8, alpha=16, tokens=32768, scaling="weak", q4k=True,
+            desc="QLoRA lm_head: W [49152x576] as Q4_K super-blocks (dequantised once into the "
+                 "f16 GEMM operand), r 8, alpha 16, h [32768x576] bf16 per GPU"),
+}
+CONFIG = CONFIGS[2]
+
+
+def flops(rank):
+    """(whole step, one GEMM pass) FLOPs per predicted token:
+    4*V*d + 8*V*r + 4*d*r and 2*V*d (tensor) + 4*V*r (rank terms)."""
+    return 4 * V * D + 8 * V * rank + 4 * D * rank, 2 * V * D + 4 * V * rank
+
+
+F_TOK, F_PASS = flops(R)
+
+
+def step_tokens(world: int) -> int:
+    """Predicted positions one step processes over all ranks."""
+    return CONFIG["tokens"] if CONFIG["scaling"] == "strong" else CONFIG["tokens"] * world
+
+
+def apply_config(n: int) -> None:
+    global CONFIG, R, ALPHA, T_PER_GPU, F_TOK, F_PASS
+    CONFIG = CONFIGS[n]
+    R, ALPHA, T_PER_GPU = CONFIG["rank"], CONFIG["alpha"], CONFIG["tokens"]
+    F_TOK, F_PASS = flops(R)
 
 
 def env_int(name, default):
@@ -125,13 +155,13 @@ def _ref_worker(args):
     returns its own wall time."""
     import numpy as np
     import workload as wl
-    seed, T = args
+    seed, T, r, alpha = args
     W = wl.make_weight(1, V, D)
-    h, tgt, A, B = wl.make_step_inputs(seed, T, V, D, R)
+    h, tgt, A, B = wl.make_step_inputs(seed, T, V, D, r)
     H = wl.oracle_hidden(h)
     tokens = np.concatenate([[1], tgt]).astype(np.int32)
     t0 = time.perf_counter()
-    _REF.train_steps(W, H, tokens, R, ALPHA, LR, 1 << 30, n_steps=1, A_dr=A, B_rv=B)
+    _REF.train_steps(W, H, tokens, r, alpha, LR, 1 << 30, n_steps=1, A_dr=A, B_rv=B)
     return time.perf_counter() - t0
 
 
@@ -139,13 +169,13 @@ def _oracle_worker(args):
     import numpy as np
     import oracle as orc
     import workload as wl
-    seed, T, threads = args
+    seed, T, threads, r, alpha = args
     W = wl.make_weight(1, V, D)
-    h, tgt, A, B = wl.make_step_inputs(seed, T, V, D, R)
+    h, tgt, A, B = wl.make_step_inputs(seed, T, V, D, r)
     H = wl.oracle_hidden(h)
     o = orc.Oracle()
     t0 = time.perf_counter()
-    o.step(W, A, B, H, tgt, ALPHA / R, LR, wd=WD, nthreads=threads)
+    o.step(W, A, B, H, tgt, alpha / r, LR, wd=WD, nthreads=threads)
     return time.perf_counter() - t0
 
 
@@ -164,7 +194,8 @@ class CpuReference:
         ctx = mp.get_context("spawn")
         if self.kind == "reference":
             self.pool = ctx.Pool(self.procs, initializer=_ref_worker_init, initargs=(None,))
-            t_cal = max(self.pool.map(_ref_worker, [(100 + i, 2) for i in range(self.procs)]))
+            t_cal = max(self.pool.map(_ref_worker,
+                                      [(100 + i, 2, R, ALPHA) for i in range(self.procs)]))
             self.per_tok = max(t_cal / 2, 1e-3)
         else:
             self.pool = ctx.Pool(1)
@@ -174,13 +205,14 @@ class CpuReference:
         if self.kind == "reference":
             n_tok = max(2, int(target_seconds / self.per_tok))
             # the slowest worker's own train_step time (input generation excluded)
-            wall = max(self.pool.map(_ref_worker, [(200 + i, n_tok) for i in range(self.procs)]))
+            wall = max(self.pool.map(_ref_worker,
+                                     [(200 + i, n_tok, R, ALPHA) for i in range(self.procs)]))
             total, used = n_tok * self.procs, self.procs
-            sample = (f"{self.procs} processes x {n_tok} positions of the isolated-op shape "
-                      f"(V {V}, d {D}, r {R}); the reference train_step in each")
+            sample = (f"{self.procs} processes x {n_tok} positions (V {V}, d {D}, r {R}, f16 W); "
+                      "the reference train_step in each")
         else:
             n_tok = max(self.cores, int(target_seconds / self.per_tok))
-            wall = max(self.pool.map(_oracle_worker, [(300, n_tok, self.cores)]))
+            wall = max(self.pool.map(_oracle_worker, [(300, n_tok, self.cores, R, ALPHA)]))
             total, used = n_tok, self.cores
             sample = f"{n_tok} positions on {self.cores} threads (oracle port)"
         return {"value": total / wall, "unit": UNIT, "cores": used, "kind": self.kind,
@@ -206,12 +238,13 @@ def run_reference_arm(args):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1e3 * T_PER_GPU * world / value,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded; bf16 h, f16 W, Zipf(1.1) targets)",
-        "config": {"workload": "isolated fused LoRA lm_head CE fwd+bwd+Adam: h [8192x576] per "
-                               "GPU, W [49152x576] f16, r 4, alpha 8; each step a sample of "
-                               "positions", "T_per_gpu": T_PER_GPU, "parallelism": f"dp{world}"},
+        "ms_per_step": 1e3 * step_tokens(world) / value,
+        "higher_is_better": True, "scaling": CONFIG["scaling"], "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded; bf16 h, f16 W, Zipf(1.1) targets)",
+        "config": {"workload": CONFIG["desc"] + "; each step a sample of positions on the "
+                               "reference's CPU path (f16 W: the reference has no Q4_K)",
+                   "tokens_per_step": step_tokens(world), "rank": R,
+                   "parallelism": f"dp{world}"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": steps[0]["cores"],
                          "kind": steps[0]["kind"], "sample": steps[0]["sample"]},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -321,6 +354,97 @@ def run_merge(args):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------- Q4_K
+def run_q4k(args):
+    """Dequantisation of the Q4_K lm_head (config 4's weight: 110,592
+    super-blocks) into the f16 GEMM operand.  HBM-bound; algorithmic bytes
+    per launch = 144 in + 512 out per super-block.  The CPU leg times the
+    oracle restatement (f32 output, one thread) on the same blocks."""
+    import ctypes as C
+    import numpy as np
+    import torch
+    import lora_ce
+    import workload as wl
+
+    args.warmup = max(args.warmup, 3)
+    blocks_h = wl.make_weight_q4k(1, V, D)
+    n = blocks_h.shape[0]
+    alg = n * (144.0 + 512.0)
+    cpu = None
+    if not args.no_cpu_baseline:
+        import oracle as orc
+        o = orc.Oracle()
+        t0 = time.perf_counter()
+        k = 0
+        while time.perf_counter() - t0 < 10.0:
+            o.q4k_dequant(blocks_h)
+            k += 1
+        dt = time.perf_counter() - t0
+        cpu = {"value": k * n * (144.0 + 1024.0) / dt / 1e9, "unit": "GB/s", "cores": 1,
+               "kind": "port", "sample": f"{k} dequantisations of the {n}-block lm_head to f32 "
+                                         "(oracle restatement, one thread; no reference "
+                                         "implementation exists)"}
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lib = lora_ce.load_library()
+    blocks = torch.from_numpy(blocks_h).to(dev)
+    out = torch.empty(n * 256, dtype=torch.int16, device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    st = torch.cuda.current_stream(dev)
+
+    def launch():
+        rc = lib.lora_ce_q4k_dequant_device(C.c_void_p(blocks.data_ptr()), n,
+                                            C.c_void_p(out.data_ptr()), lora_ce.F16,
+                                            C.c_void_p(st.cuda_stream))
+        if rc != 0:
+            raise RuntimeError(lib.lora_ce_q4k_last_error().decode())
+
+    for _ in range(args.warmup):
+        flush.fill_(1.0)
+        launch()
+    torch.cuda.synchronize(dev)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    with ClockSampler(0) as clk:
+        for s_, e_ in evs:
+            flush.fill_(1.0)
+            s_.record(st)
+            launch()
+            e_.record(st)
+        torch.cuda.synchronize(dev)
+    t_ms = sum(s_.elapsed_time(e_) for s_, e_ in evs) / args.steps
+    gbs = alg / (t_ms * 1e-3) / 1e9
+    lora_ce.q4k_dequant(blocks_h, lora_ce.F16)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        lora_ce.q4k_dequant(blocks_h, lora_ce.F16)
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    _, hbm, peak_kind = peaks()
+    traffic = None
+    tp = os.path.join(REPO, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        with open(tp) as f:
+            traffic = json.load(f).get("q4k_dequant")
+    line = {
+        "metric": "Q4_K lm_head dequantisation GB/s", "value": gbs, "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t_ms,
+        "higher_is_better": True, "scaling": "replicas only", "vs_baseline": None,
+        "dtype": "u8", "data": "synthetic (seeded Q4_K super-blocks: uniform quant and scale "
+                               "bytes, d/dmin f16 in [4e-5, 1.2e-4])",
+        "config": {"workload": f"Q4_K W [49152x576] ({n} super-blocks) -> f16",
+                   "l2": "flushed (256 MB write) before every launch"},
+        "roofline": {"kernel": "lce_q4k_dequant", "bound": "hbm", "achieved": gbs, "peak": hbm,
+                     "unit": "GB/s", "frac": gbs / hbm, "peak_kind": f"{peak_kind} copy",
+                     "bytes_per_launch": alg, "traffic": traffic},
+        "cpu_baseline": cpu,
+        "e2e": {"value": alg / e2e_s / 1e9, "unit": "GB/s", "h2d_bytes_per_step": int(n * 144),
+                "d2h_bytes_per_step": int(n * 512), "timer": "host wall clock"},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 # ----------------------------------------------------------------- GPU leg
 def main():
     ap = argparse.ArgumentParser()
@@ -329,14 +453,19 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--op", default="step", choices=["step", "merge"])
+    ap.add_argument("--op", default="step", choices=["step", "merge", "q4k"])
+    ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
     ap.add_argument("--merge-rank", type=int, default=R)
     args = ap.parse_args()
+    apply_config(args.config)
     if args.impl == "reference":
         run_reference_arm(args)
         return
     if args.op == "merge":
         run_merge(args)
+        return
+    if args.op == "q4k":
+        run_q4k(args)
         return
     args.warmup = max(args.warmup, 3)
 
@@ -363,14 +492,16 @@ def main():
         cpu = ref.sample(15.0)
         ref.close()
 
-    T = T_PER_GPU
-    W = wl.make_weight(1, V, D)
+    T = step_tokens(world) // world  # this rank's positions (strong scaling splits the total)
     h, tgt, A, B = wl.make_step_inputs(1000 + rank, T, V, D, R)
-    _, _, A, B = wl.make_step_inputs(1000, T, V, D, R)  # same adapter on every rank
+    _, _, A, B = wl.make_step_inputs(1000, 8, V, D, R)  # same adapter on every rank
     cfg = lora_ce.default_config(D, V, R, T, scale=ALPHA / R, lr=LR, weight_decay=WD,
                                  device=local)
     m = lora_ce.LoraCE(cfg)
-    m.set_weight(W)
+    if CONFIG["q4k"]:
+        m.set_weight_q4k(wl.make_weight_q4k(1, V, D))
+    else:
+        m.set_weight(wl.make_weight(1, V, D))
     m.set_adapter(A, B, 0)
     if world > 1:
         uid = [lora_ce.LoraCE.nccl_unique_id() if rank == 0 else None]
@@ -463,10 +594,11 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
-            "data": "synthetic (seeded; h bf16 N(0,1), W f16 N(0,0.02), Zipf(1.1) targets)",
-            "config": {"workload": "isolated fused LoRA lm_head CE fwd+bwd+AdamW step: "
-                                   "h [8192x576] bf16 per GPU, W [49152x576] f16, r 4, alpha 8",
+            "higher_is_better": True, "scaling": CONFIG["scaling"], "vs_baseline": None,
+            "dtype": "f16",
+            "data": "synthetic (seeded; h bf16 N(0,1), W " +
+                    ("Q4_K blocks" if CONFIG["q4k"] else "f16 N(0,0.02)") + ", Zipf(1.1) targets)",
+            "config": {"workload": CONFIG["desc"], "config": args.config,
                        "T_per_gpu": T, "vocab": V, "dim": D, "rank": R, "lr": LR,
                        "weight_decay": WD, "parallelism": f"dp{world}",
                        "l2": "flushed (256 MB write) before every timed step"},

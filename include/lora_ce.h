@@ -83,6 +83,24 @@ int lora_ce_destroy(lora_ce_handle* h);
  * stored in the GGUF (dims[0] = d innermost; src/train.c:498-516). */
 int lora_ce_set_weight_f16(lora_ce_handle* h, const uint16_t* W);
 
+/* Upload the lm_head weight as Q4_K (GGUF / ggml type 12) super-blocks:
+ * V*d/256 blocks of 144 bytes over the flattened [V][d] tensor (V*d must
+ * be a multiple of 256).  The weight is dequantised once on the GPU into
+ * the f16 operand of the logits GEMM (it is frozen during LoRA training), so
+ * a QLoRA step costs what an f16 step costs.  No counterpart in the
+ * reference (QLoRA is refused, src/studio.c:187-191). */
+int lora_ce_set_weight_q4k(lora_ce_handle* h, const void* blocks);
+
+/* Q4_K super-blocks -> weights, y = (d*sc)*q - (dmin*m) with each product
+ * and the difference rounded separately; out_dtype LORA_CE_F32 gives y,
+ * LORA_CE_F16 gives y rounded to nearest f16.  Host buffers (device
+ * `device`), or device pointers (16-byte aligned) enqueued on `stream`. */
+int lora_ce_q4k_dequant(const void* blocks, int64_t n_blocks, void* out,
+                        int32_t out_dtype, int32_t device);
+int lora_ce_q4k_dequant_device(const void* d_blocks, int64_t n_blocks,
+                               void* d_out, int32_t out_dtype, void* stream);
+const char* lora_ce_q4k_last_error(void);
+
 /* Load an adapter (reference layouts) and the Adam step counter; resets
  * the Adam moments, as train_load does (src/train.c:261-283: LORA0001
  * carries no optimizer state). */

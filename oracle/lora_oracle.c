@@ -20,6 +20,10 @@
  *   Kaiming A init       src/train.c:83-93       (glibc rand, Box-Muller)
  *   softmax-CE gradcheck src/backward.c:450-503  (grad_check_softmax_ce)
  *   merge                src/train.c:393-460     (lora_patched_weight)
+ *   Q4_K dequantisation  not in the reference (src/gguf.h:43 only names
+ *                        GGUF_DT_Q4_K = 12; src/gguf.c:323 gives it size 0);
+ *                        restated from the public GGUF / ggml format, so
+ *                        its parity is unpinned by the reference
  *
  * Extensions that the reference does not have (weight decay, grad-clip) are
  * applied after the mean exactly where an AdamW implementation applies
@@ -448,6 +452,59 @@ void oracle_merge(const uint16_t* W, const float* A, const float* B, int d,
             float delta = scale * s;
             float base = merge_f16_to_f32(W[(size_t)v * d + i]);
             out[(size_t)v * d + i] = oracle_merge_f32_to_f16(base + delta);
+        }
+    }
+}
+
+/* ------------------------------------------------------------------ Q4_K
+ * The ggml / GGUF Q4_K super-block (type 12), 144 bytes per 256 weights:
+ *   f16 d, f16 dmin, uint8 scales[12], uint8 qs[128].
+ * scales packs eight 6-bit (scale, min) pairs, one per 32-weight sub-block j:
+ *   j < 4:  sc = scales[j] & 63,  m = scales[j+4] & 63
+ *   j >= 4: sc = (scales[j+4] & 15) | ((scales[j-4] >> 6) << 4)
+ *           m  = (scales[j+4] >> 4) | ((scales[j]   >> 6) << 4)
+ * The 256 weights are four runs of 64; run c reads qs[32c .. 32c+31]: the
+ * low nibbles are sub-block 2c, the high nibbles sub-block 2c+1, and
+ *   y = (d * sc) * q - (dmin * m)
+ * with d, dmin converted exactly from f16 and every product and the
+ * difference rounded separately (ggml's scalar order, no contraction).
+ * Blocks run over the flattened tensor (for W [V][d], d = 576, a block can
+ * span two rows).  This restatement is the parity anchor of the GPU
+ * dequantisation. */
+static void q4k_scale_min(int j, const uint8_t* q, int* sc, int* m) {
+    if (j < 4) {
+        *sc = q[j] & 63;
+        *m = q[j + 4] & 63;
+    } else {
+        *sc = (q[j + 4] & 15) | ((q[j - 4] >> 6) << 4);
+        *m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+}
+
+void oracle_q4k_dequant(const uint8_t* blocks, int64_t n_blocks, float* out) {
+    for (int64_t b = 0; b < n_blocks; b++) {
+        const uint8_t* blk = blocks + b * 144;
+        uint16_t dh, mh;
+        memcpy(&dh, blk, 2);
+        memcpy(&mh, blk + 2, 2);
+        const float d = oracle_f16_to_f32(dh), dmin = oracle_f16_to_f32(mh);
+        const uint8_t* scales = blk + 4;
+        const uint8_t* qs = blk + 16;
+        float* y = out + b * 256;
+        for (int c = 0; c < 4; c++) {
+            int sc, m;
+            q4k_scale_min(2 * c, scales, &sc, &m);
+            const float d1 = d * (float)sc, m1 = dmin * (float)m;
+            q4k_scale_min(2 * c + 1, scales, &sc, &m);
+            const float d2 = d * (float)sc, m2 = dmin * (float)m;
+            for (int l = 0; l < 32; l++) {
+                const float p1 = d1 * (float)(qs[32 * c + l] & 15);
+                y[64 * c + l] = p1 - m1;
+            }
+            for (int l = 0; l < 32; l++) {
+                const float p2 = d2 * (float)(qs[32 * c + l] >> 4);
+                y[64 * c + 32 + l] = p2 - m2;
+            }
         }
     }
 }

@@ -68,6 +68,8 @@ class Oracle:
         lib.oracle_merge.argtypes = [_u16p, _f32p, _f32p, C.c_int, C.c_int, C.c_int,
                                      C.c_float, _u16p]
         lib.oracle_merge.restype = None
+        lib.oracle_q4k_dequant.argtypes = [C.c_void_p, C.c_int64, _f32p]
+        lib.oracle_q4k_dequant.restype = None
         self.lib = lib
 
     def base_logits(self, W16: np.ndarray, h: np.ndarray) -> np.ndarray:
@@ -146,6 +148,15 @@ class Oracle:
 
     def grad_check_softmax_ce(self, vocab: int = 32, eps: float = 1e-3) -> float:
         return float(self.lib.oracle_grad_check_softmax_ce(vocab, eps))
+
+    def q4k_dequant(self, blocks: np.ndarray) -> np.ndarray:
+        """Q4_K super-blocks (uint8, 144 bytes each) -> f32 weights."""
+        blocks = np.ascontiguousarray(blocks, np.uint8).ravel()
+        assert blocks.size % 144 == 0
+        n = blocks.size // 144
+        out = np.empty(n * 256, np.float32)
+        self.lib.oracle_q4k_dequant(blocks.ctypes.data, n, out)
+        return out
 
     def merge(self, W16, A_dr, B_rv, scale) -> np.ndarray:
         V, d = W16.shape

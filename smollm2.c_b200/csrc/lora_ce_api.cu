@@ -597,6 +597,29 @@ int lora_ce_set_weight_f16(lora_ce_handle* h, const uint16_t* W) {
   return 0;
 }
 
+int lora_ce_set_weight_q4k(lora_ce_handle* h, const void* blocks) {
+  if (!h || !blocks) return fail(LORA_CE_EINVAL, "bad argument");
+  const long long n = (long long)h->V * h->d;
+  if (n % 256 != 0) return fail(LORA_CE_EINVAL, "vocab*dim must be a multiple of 256 for Q4_K");
+  LCE_CUDA(cudaSetDevice(h->cfg.device));
+  void* tmp = nullptr;
+  if (cudaMalloc(&tmp, (size_t)(n / 256) * 144) != cudaSuccess)
+    return fail(LORA_CE_ENOMEM, "cudaMalloc failed");
+  int rc = 0;
+  if (cudaMemcpyAsync(tmp, blocks, (size_t)(n / 256) * 144, cudaMemcpyHostToDevice, h->stream) !=
+      cudaSuccess)
+    rc = fail(LORA_CE_ECUDA, "Q4_K upload failed");
+  if (!rc) {
+    rc = lora_ce_q4k_dequant_device(tmp, n / 256, h->W, LORA_CE_F16, h->stream);
+    if (rc) fail(rc, lora_ce_q4k_last_error());
+  }
+  if (cudaStreamSynchronize(h->stream) != cudaSuccess && !rc)
+    rc = fail(LORA_CE_ECUDA, "Q4_K dequantisation failed");
+  cudaFree(tmp);
+  if (!rc) h->have_weight = true;
+  return rc;
+}
+
 int lora_ce_set_adapter(lora_ce_handle* h, const float* A, const float* B, int32_t step) {
   if (!h || !A || !B || step < 0) return fail(LORA_CE_EINVAL, "bad argument");
   LCE_CUDA(cudaSetDevice(h->cfg.device));

@@ -46,6 +46,8 @@ EXPORTS = [
     "lora_ce_last_error", "lora_ce_set_profiling", "lora_ce_phase_times", "lora_ce_phase_name",
     "lora_ce_token_loss_noalloc", "lora_ce_noalloc_last_error", "lora_ce_merge_weight",
     "lora_ce_merge_weight_device", "lora_ce_merge_last_error", "lora_ce_set_scale",
+    "lora_ce_set_weight_q4k", "lora_ce_q4k_dequant", "lora_ce_q4k_dequant_device",
+    "lora_ce_q4k_last_error",
 ]
 
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
@@ -54,7 +56,8 @@ NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", 
 
 def build(verbose: bool = False) -> str:
     """Compile csrc/ into liblora_ce.so (sm_100a) next to this file."""
-    srcs = [os.path.join(HERE, "csrc", f) for f in ("lora_ce_api.cu", "lora_ce_noalloc.cu", "lora_ce_merge.cu")]
+    srcs = [os.path.join(HERE, "csrc", f) for f in ("lora_ce_api.cu", "lora_ce_noalloc.cu", "lora_ce_merge.cu",
+                                                         "lora_ce_q4k.cu")]
     cmd = ["nvcc", *NVCC_FLAGS, "-I" + os.path.join(REPO, "include"), "-o", LIB_PATH, *srcs,
            "-ldl"]
     if verbose:
@@ -95,6 +98,11 @@ def load_library() -> C.CDLL:
     lib.lora_ce_set_weight_f16.argtypes = [vp, vp]
     lib.lora_ce_set_adapter.argtypes = [vp, vp, vp, C.c_int32]
     lib.lora_ce_set_scale.argtypes = [vp, C.c_float]
+    lib.lora_ce_set_weight_q4k.argtypes = [vp, vp]
+    lib.lora_ce_q4k_dequant.argtypes = [vp, C.c_int64, vp, C.c_int32, C.c_int32]
+    lib.lora_ce_q4k_dequant_device.argtypes = [vp, C.c_int64, vp, C.c_int32, vp]
+    lib.lora_ce_q4k_last_error.argtypes = []
+    lib.lora_ce_q4k_last_error.restype = C.c_char_p
     lib.lora_ce_get_adapter.argtypes = [vp, vp, vp, C.POINTER(C.c_int32)]
     lib.lora_ce_step.argtypes = [vp, vp, C.c_int32, C.c_int32, vp, C.POINTER(C.c_float)]
     lib.lora_ce_step_device.argtypes = [vp, vp, C.c_int32, C.c_int32, vp, vp]
@@ -164,6 +172,20 @@ def merge_weight(W16: np.ndarray, A_dr: np.ndarray, B_rv: np.ndarray, scale: flo
     if rc != 0:
         msg = lib.lora_ce_merge_last_error().decode(errors="replace")
         raise LoraCEError(f"lora_ce_merge_weight failed: {ERRORS.get(rc, rc)}: {msg}")
+    return out
+
+
+def q4k_dequant(blocks: np.ndarray, dtype: int = 2, device: int = 0) -> np.ndarray:
+    """Q4_K super-blocks -> f32 (dtype F32) or f16 bits (dtype F16) on the GPU."""
+    b = np.ascontiguousarray(blocks, np.uint8).ravel()
+    assert b.size % 144 == 0
+    n = b.size // 144
+    out = np.empty(n * 256, np.float32 if dtype == F32 else np.uint16)
+    lib = load_library()
+    rc = lib.lora_ce_q4k_dequant(_ptr(b), n, _ptr(out), dtype, device)
+    if rc != 0:
+        msg = lib.lora_ce_q4k_last_error().decode(errors="replace")
+        raise LoraCEError(f"lora_ce_q4k_dequant failed: {ERRORS.get(rc, rc)}: {msg}")
     return out
 
 
@@ -256,6 +278,12 @@ class LoraCE:
         assert A.shape == (self.cfg.dim, self.cfg.rank)
         assert B.shape == (self.cfg.rank, self.cfg.vocab)
         _check(self.lib.lora_ce_set_adapter(self.h, _ptr(A), _ptr(B), step), "set_adapter")
+
+    def set_weight_q4k(self, blocks: np.ndarray) -> None:
+        """lm_head as Q4_K super-blocks (uint8, V*d/256 x 144)."""
+        b = np.ascontiguousarray(blocks, np.uint8)
+        assert b.size == self.cfg.vocab * self.cfg.dim // 256 * 144
+        _check(self.lib.lora_ce_set_weight_q4k(self.h, _ptr(b)), "set_weight_q4k")
 
     def set_scale(self, scale: float) -> None:
         _check(self.lib.lora_ce_set_scale(self.h, float(scale)), "set_scale")

@@ -61,3 +61,41 @@ def make_step_inputs(seed: int, T: int, V: int, d: int, r: int):
 def oracle_hidden(h_bf16: np.ndarray) -> np.ndarray:
     """Hidden rows as the kernels consume them (bf16 -> f16 RN), in f32."""
     return f16_exact(bf16_bits_to_f32(h_bf16))
+
+
+def make_weight_q4k(seed: int, V: int, d: int) -> np.ndarray:
+    """W [V][d] as Q4_K super-blocks over the flattened tensor
+    (V*d/256 blocks of 144 bytes): d and dmin f16 drawn uniformly from
+    [4e-5, 1.2e-4] (weights of about the spread of N(0, 0.02)), the 12 scale
+    bytes (eight 6-bit scale / min pairs) and the
+    128 quant bytes (4-bit values) uniform random bytes."""
+    assert (V * d) % 256 == 0
+    n = V * d // 256
+    rng = np.random.default_rng(seed)
+    blocks = rng.integers(0, 256, size=(n, 144), dtype=np.uint8)
+    dd = rng.uniform(4e-5, 1.2e-4, size=(n, 2)).astype(np.float16)
+    blocks[:, 0:4] = dd.view(np.uint8).reshape(n, 4)
+    return blocks
+
+
+def q4k_dequant_np(blocks: np.ndarray) -> np.ndarray:
+    """Q4_K -> f32 in numpy (float32 arithmetic, each product and the
+    difference rounded separately): an independent restatement of the
+    format used to cross-check the C restatement in the tests."""
+    b = np.ascontiguousarray(blocks, np.uint8).reshape(-1, 144)
+    n = b.shape[0]
+    d = b[:, 0:2].copy().view(np.float16).astype(np.float32)[:, 0]
+    dmin = b[:, 2:4].copy().view(np.float16).astype(np.float32)[:, 0]
+    q = b[:, 4:16].astype(np.int32)
+    sc = np.empty((n, 8), np.int32)
+    mn = np.empty((n, 8), np.int32)
+    sc[:, :4] = q[:, 0:4] & 63
+    mn[:, :4] = q[:, 4:8] & 63
+    sc[:, 4:] = (q[:, 8:12] & 15) | ((q[:, 0:4] >> 6) << 4)
+    mn[:, 4:] = (q[:, 8:12] >> 4) | ((q[:, 4:8] >> 6) << 4)
+    qs = b[:, 16:144].reshape(n, 4, 32).astype(np.int32)
+    nib = np.stack([qs & 15, qs >> 4], axis=2).reshape(n, 8, 32)  # sub-block 2c, 2c+1
+    dsc = (d[:, None] * sc.astype(np.float32)).astype(np.float32)
+    mm = (dmin[:, None] * mn.astype(np.float32)).astype(np.float32)
+    p = (dsc[:, :, None] * nib.astype(np.float32)).astype(np.float32)
+    return (p - mm[:, :, None]).astype(np.float32).reshape(-1)

@@ -109,6 +109,9 @@ def main() -> None:
     f.restype = C.c_int
     assert f(Wm, Am, Bm, Wm.shape[1], Am.shape[1], Wm.shape[0], 2.0, out) == 0
     meta["merge_4099x576_r8"] = {"sha": sha(out), "changed": int((out != Wm).sum())}
+    # Q4_K has no reference implementation: the digest pins the restatement
+    # of the public format against drift
+    meta["q4k_seed4_49152x576_sha"] = sha(orc.Oracle().q4k_dequant(wl.make_weight_q4k(4, 49152, 576)))
     with open(os.path.join(HERE, "golden.json"), "w") as f:
         json.dump(meta, f, indent=1, sort_keys=True)
     print("grad_check", meta["grad_check_softmax_ce"], "lora0001 bytes", len(data))

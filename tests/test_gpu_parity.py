@@ -258,3 +258,36 @@ def test_merge_ragged_shapes(oracle, V, d, r):
     B = rng.standard_normal((r, V), dtype=np.float32) * np.float32(0.05)
     np.testing.assert_array_equal(lora_ce.merge_weight(W, A, B, 8.0 / r),
                                   oracle.merge(W, A, B, 8.0 / r))
+
+
+def test_q4k_dequant_bit_exact(oracle):
+    """Q4_K -> f32 on the GPU == the oracle's restatement, bit for bit, over
+    the QLoRA lm_head (110,592 super-blocks); the f16 output is that value
+    rounded to nearest."""
+    blocks = wl.make_weight_q4k(4, 49152, 576)
+    want = oracle.q4k_dequant(blocks)
+    got = lora_ce.q4k_dequant(blocks, lora_ce.F32)
+    np.testing.assert_array_equal(got.view(np.uint32), want.view(np.uint32))
+    got16 = lora_ce.q4k_dequant(blocks, lora_ce.F16)
+    np.testing.assert_array_equal(got16, want.astype(np.float16).view(np.uint16))
+
+
+def test_q4k_step_matches_oracle(oracle):
+    """The QLoRA step (r 8, Q4_K lm_head dequantised once into the f16
+    operand) against the oracle on the same f16 weights."""
+    V, d, r, T = 49152, 576, 8, 512
+    blocks = wl.make_weight_q4k(6, V, d)
+    W16 = oracle.q4k_dequant(blocks).astype(np.float16).view(np.uint16).reshape(V, d)
+    h, tgt, A, B = wl.make_step_inputs(6, T, V, d, r)
+    m = lora_ce.LoraCE(lora_ce.default_config(d, V, r, T, scale=2.0, lr=1e-3))
+    m.set_weight_q4k(blocks)
+    m.set_adapter(A, B, 0)
+    loss = m.step(h, tgt)
+    gA, gB, _, _ = m.get_grads()
+    A1, B1, _ = m.get_adapter()
+    m.close()
+    ref = oracle.step(W16, A, B, wl.oracle_hidden(h), tgt, 2.0, 1e-3, nthreads=NTHREADS)
+    assert abs(loss - ref["loss"]) <= LOSS_RTOL * ref["loss"]
+    for name, a, b in (("dA", gA, ref["gA"]), ("dB", gB, ref["gB"]), ("A", A1, ref["A"]),
+                       ("B", B1, ref["B"])):
+        assert rel(a, b) <= L2_RTOL, (name, rel(a, b))

@@ -129,3 +129,40 @@ def test_merge_matches_reference_fixture(oracle, golden):
     out = oracle.merge(W, A, B, 2.0)
     assert sha(out) == golden["merge_4099x576_r8"]["sha"]
     assert int((out != W).sum()) == golden["merge_4099x576_r8"]["changed"]
+
+
+def _pack_q4k_scales(sc, m):
+    """Inverse of the Q4_K 6-bit (scale, min) packing, from the format's definition."""
+    q = np.zeros(12, np.uint8)
+    for j in range(4):
+        q[j] = (sc[j] & 63) | ((sc[j + 4] >> 4) << 6)
+        q[j + 4] = (m[j] & 63) | ((m[j + 4] >> 4) << 6)
+        q[j + 8] = (sc[j + 4] & 15) | ((m[j + 4] & 15) << 4)
+    return q
+
+
+def test_q4k_known_answer(oracle):
+    """A hand-packed super-block whose weights follow from the format:
+    sub-block j holds d*sc_j*q - dmin*m_j, runs of 64 = (low, high) nibbles."""
+    sc = [1, 2, 3, 63, 17, 33, 48, 5]
+    m = [0, 1, 62, 63, 16, 32, 7, 40]
+    qs = (np.arange(128) * 7 % 256).astype(np.uint8)
+    blk = np.concatenate([np.array([1.0, 0.5], np.float16).view(np.uint8), _pack_q4k_scales(sc, m),
+                          qs])
+    assert blk.size == 144
+    want = np.empty(256, np.float64)
+    for c in range(4):
+        for l in range(32):
+            want[64 * c + l] = 1.0 * sc[2 * c] * (qs[32 * c + l] & 15) - 0.5 * m[2 * c]
+            want[64 * c + 32 + l] = 1.0 * sc[2 * c + 1] * (qs[32 * c + l] >> 4) - 0.5 * m[2 * c + 1]
+    np.testing.assert_array_equal(oracle.q4k_dequant(blk), want.astype(np.float32))
+    np.testing.assert_array_equal(wl.q4k_dequant_np(blk), want.astype(np.float32))
+
+
+def test_q4k_restatements_agree(oracle, golden):
+    """The C restatement and the independent numpy one, bit for bit, on the
+    seeded QLoRA weight (110,592 blocks), and the committed digest."""
+    blocks = wl.make_weight_q4k(4, 49152, 576)
+    a = oracle.q4k_dequant(blocks)
+    np.testing.assert_array_equal(a.view(np.uint32), wl.q4k_dequant_np(blocks).view(np.uint32))
+    assert sha(a) == golden["q4k_seed4_49152x576_sha"]
