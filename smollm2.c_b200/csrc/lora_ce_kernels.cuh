@@ -180,7 +180,7 @@ __device__ __forceinline__ float2 f2(float x, float y) { return make_float2(x, y
 template <int R>
 struct EpiLse {
   static constexpr int kRec = R;  // floats per column
-  static constexpr int kWarps = R == 4 ? 16 : 8;
+  static constexpr int kWarps = R == 4 ? 16 : 8;  // 16 at rank 8 would spill
   static constexpr int kCW = (R >= 16 || kWarps == 16) ? 8 : 16;
   static constexpr float kLazy = 8.0f;   // move the reference max only past this
   static constexpr float kRedo = 80.0f;  // re-sum a chunk that jumped this far
@@ -308,7 +308,7 @@ struct EpiLse {
 template <int R>
 struct EpiGrad {
   static constexpr int kRec = R + 4;
-  static constexpr int kWarps = R == 4 ? 16 : 8;
+  static constexpr int kWarps = R <= 8 ? 16 : 8;
   static constexpr int kCW = (R >= 16 || kWarps == 16) ? 8 : 16;
   int v;
   bool valid;
