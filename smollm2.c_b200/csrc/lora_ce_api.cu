@@ -167,6 +167,10 @@ struct lora_ce_handle {
   void* in_H = nullptr;     // staging for host inputs
   int32_t* in_tgt = nullptr;
   CUtensorMap mapW_res{}, mapW_str{};
+  // rank augmentation (R >= 8): waug [Vpad][64], haug [Tcap][64] f16
+  __half* w_aug = nullptr;
+  __half* h_aug = nullptr;
+  CUtensorMap mapWa_res{}, mapWa_str{};
   ncclComm_t comm = nullptr;
   int nranks = 1, rank = 0;
   // optional per-phase timing (events on the handle's stream)
@@ -189,7 +193,7 @@ void free_all(lora_ce_handle* h) {
   void* ptrs[] = {h->W,     h->h16,   h->tok,      h->params, h->mom1,  h->mom2,
                   h->Gbuf,  h->gmean, h->p_max,    h->p_sum,  h->p_q,   h->z_tgt,
                   h->loss_tok, h->dU, h->gAp,      h->gBp,    h->norm_parts, h->err, h->corr_fx,
-                  h->d_loss, h->in_H, h->in_tgt};
+                  h->d_loss, h->in_H, h->in_tgt, h->w_aug, h->h_aug};
   for (void* p : ptrs)
     if (p) cudaFree(p);
 }
@@ -200,6 +204,9 @@ int check_cfg(const lora_ce_config* c) {
     return fail(LORA_CE_EINVAL, "dim must be a multiple of 64 in [64, 640]");
   if (c->vocab < 1) return fail(LORA_CE_EINVAL, "vocab must be positive");
   if (c->rank < 1 || c->rank > 16) return fail(LORA_CE_EINVAL, "rank must be in [1, 16]");
+  const int r_kernel = c->rank <= 4 ? 4 : c->rank <= 8 ? 8 : 16;
+  if (r_kernel >= LCE_AUG_MIN_RANK && c->dim / 64 + 1 > kMaxKBlocks)
+    return fail(LORA_CE_EINVAL, "this rank needs dim <= 576 (one K-block for the rank term)");
   if (c->max_tokens < 1) return fail(LORA_CE_EINVAL, "max_tokens must be positive");
   if (!(c->lr >= 0.f) || !(c->eps > 0.f) || !(c->beta1 >= 0.f && c->beta1 < 1.f) ||
       !(c->beta2 >= 0.f && c->beta2 < 1.f) || !(c->weight_decay >= 0.f) ||
@@ -208,12 +215,21 @@ int check_cfg(const lora_ce_config* c) {
   return 0;
 }
 
+using GemmKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap,
+                           const CUtensorMap, const GemmArgs);
+
+// K-blocks of a GEMM tile: d / 64, plus one when the rank term is augmented.
 template <class Epi>
-void (*gemm_kernel(int pair, int kblocks, int* smem_out))(const CUtensorMap, const CUtensorMap,
-                                                          const GemmArgs) {
-  const int smem_staged = SmemLayout::bytes(kblocks, Epi::kRec);
+int tile_kblocks(int d) {
+  return d / kBK + (Epi::kAug ? 1 : 0);
+}
+
+template <class Epi>
+GemmKernel gemm_kernel(int pair, int kblocks, int* smem_out) {
+  const int smem_staged = SmemLayout::bytes(kblocks, Epi::kRec * Epi::kRecBufs,
+                                            pair == 2 ? Epi::kRing : kRingBytes);
   const bool staged = smem_staged <= kMaxDynSmem;
-  *smem_out = staged ? smem_staged : SmemLayout::bytes(kblocks, 0);
+  *smem_out = staged ? smem_staged : SmemLayout::bytes(kblocks, 0, kRingBytes);
   if (pair == 2) return staged ? lce_gemm_kernel<Epi, true, 2> : lce_gemm_kernel<Epi, false, 2>;
   return staged ? lce_gemm_kernel<Epi, true, 1> : lce_gemm_kernel<Epi, false, 1>;
 }
@@ -245,7 +261,8 @@ int resident_units(int pair, int kblocks, int num_sms) {
 
 // Launch one GEMM pass: `units` tile-range owners (CTAs, or 2-CTA clusters).
 template <class Epi>
-int launch_gemm(const CUtensorMap& map_res, const CUtensorMap& map_str, const GemmArgs& g,
+int launch_gemm(const CUtensorMap& map_res, const CUtensorMap& map_str,
+                const CUtensorMap& map_res_aug, const CUtensorMap& map_str_aug, const GemmArgs& g,
                 int units, int pair, int kblocks, cudaStream_t st) {
   int smem = 0;
   auto kern = gemm_kernel<Epi>(pair, kblocks, &smem);
@@ -262,7 +279,7 @@ int launch_gemm(const CUtensorMap& map_res, const CUtensorMap& map_str, const Ge
   attr[0].val.clusterDim.z = 1;
   lc.attrs = attr;
   lc.numAttrs = pair == 2 ? 1 : 0;
-  LCE_CUDA(cudaLaunchKernelEx(&lc, kern, map_res, map_str, g));
+  LCE_CUDA(cudaLaunchKernelEx(&lc, kern, map_res, map_str, map_res_aug, map_str_aug, g));
   return 0;
 }
 
@@ -275,13 +292,20 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
              float* d_loss_out) {
   cudaStream_t st = h->stream;
   const int d = h->d, V = h->V;
-  const int kblocks = d / kBK;
+  constexpr bool kAug = EpiLse<R>::kAug;
+  static_assert(EpiGrad<R>::kAug == kAug, "both passes augment the rank term or neither");
+  const int kmain = d / kBK;
+  const int kblocks = tile_kblocks<EpiLse<R>>(d);
   const long long Tpad = round_up(T, kBN);
   int launches = 0;
 
   CUtensorMap mapH_res, mapH_str;
   if (!make_map(&mapH_res, h->h16, T, d, kBM) || !make_map(&mapH_str, h->h16, T, d, kBN))
     return fail(LORA_CE_ECUDA, "cuTensorMapEncodeTiled failed for h");
+  CUtensorMap mapHa_res = mapH_res, mapHa_str = mapH_str;  // unused unless kAug
+  if (kAug && (!make_map(&mapHa_res, h->h_aug, T, kBK, kBM) ||
+               !make_map(&mapHa_str, h->h_aug, T, kBK, kBN)))
+    return fail(LORA_CE_ECUDA, "cuTensorMapEncodeTiled failed for the rank augmentation");
 
   // 1. convert h, U = h.A, per-position records
   mark(h, kPhPrep);
@@ -290,7 +314,12 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
     const int blocks = (int)std::min<long long>((Tpad + 7) / 8, 4LL * h->num_sms);
     lce_prep<R><<<blocks, threads, (size_t)d * R * 4, st>>>(dH, dtype, T, (int)Tpad, d, h->params,
                                                            h->cfg.scale, dtg, V, h->h16, h->tok,
-                                                           h->err);
+                                                           h->err, kAug ? h->h_aug : nullptr);
+    ++launches;
+  }
+  if constexpr (kAug) {  // [B_hi | B_lo | B_hi] rows from the current B
+    const int blocks = (int)std::min<long long>((h->Vpad * 8 + 255) / 256, 8LL * h->num_sms);
+    lce_aug_b<R><<<blocks, 256, 0, st>>>(h->params + (long long)d * R, h->Vpad, h->w_aug);
     ++launches;
   }
   const int pair = h->pair;
@@ -307,6 +336,7 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
     return fail(LORA_CE_ESTATE, "pass-1 partial buffer too small");
   GemmArgs g{};
   g.kblocks = kblocks;
+  g.kmain = kmain;
   g.T = T;
   g.V = V;
   g.R = R;
@@ -323,8 +353,9 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
   g.n_b = n_b1;
   g.Tcap = stride1;
   {
-    int rc = launch_gemm<EpiLse<R>>(mapH_res, pair == 2 ? h->mapW_res : h->mapW_str, g, G1, pair,
-                                    kblocks, st);
+    int rc = launch_gemm<EpiLse<R>>(mapH_res, pair == 2 ? h->mapW_res : h->mapW_str, mapHa_res,
+                                    pair == 2 ? h->mapWa_res : h->mapWa_str, g, G1, pair, kblocks,
+                                    st);
     if (rc) return rc;
     ++launches;
   }
@@ -348,8 +379,8 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
   {
     g.n_a = n_a2;
     g.n_b = n_b2;
-    int rc = launch_gemm<EpiGrad<R>>(h->mapW_res, pair == 2 ? mapH_res : mapH_str, g, G2, pair,
-                                     kblocks, st);
+    int rc = launch_gemm<EpiGrad<R>>(h->mapW_res, pair == 2 ? mapH_res : mapH_str, h->mapWa_res,
+                                     pair == 2 ? mapHa_res : mapHa_str, g, G2, pair, kblocks, st);
     if (rc) return rc;
     ++launches;
   }
@@ -501,15 +532,18 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
   const int R = h->R, d = h->d;
   const int res_rows = kBM * h->pair;
   {
-    const int kb = d / kBK;
     int u1 = 0, u2 = 0;
     switch (R) {
-      case 4: u1 = resident_units<EpiLse<4>>(h->pair, kb, h->num_sms);
-              u2 = resident_units<EpiGrad<4>>(h->pair, kb, h->num_sms); break;
-      case 8: u1 = resident_units<EpiLse<8>>(h->pair, kb, h->num_sms);
-              u2 = resident_units<EpiGrad<8>>(h->pair, kb, h->num_sms); break;
-      default: u1 = resident_units<EpiLse<16>>(h->pair, kb, h->num_sms);
-               u2 = resident_units<EpiGrad<16>>(h->pair, kb, h->num_sms); break;
+      case 4: u1 = resident_units<EpiLse<4>>(h->pair, tile_kblocks<EpiLse<4>>(d), h->num_sms);
+              u2 = resident_units<EpiGrad<4>>(h->pair, tile_kblocks<EpiGrad<4>>(d), h->num_sms);
+              break;
+      case 8: u1 = resident_units<EpiLse<8>>(h->pair, tile_kblocks<EpiLse<8>>(d), h->num_sms);
+              u2 = resident_units<EpiGrad<8>>(h->pair, tile_kblocks<EpiGrad<8>>(d), h->num_sms);
+              break;
+      default: u1 = resident_units<EpiLse<16>>(h->pair, tile_kblocks<EpiLse<16>>(d), h->num_sms);
+               u2 = resident_units<EpiGrad<16>>(h->pair, tile_kblocks<EpiGrad<16>>(d),
+                                                h->num_sms);
+               break;
     }
     if (u1 < 1 || u2 < 1) {
       delete h;
@@ -561,10 +595,20 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
   if (!rc) rc = dalloc(&h->d_loss, 2);
   if (!rc) rc = dalloc(reinterpret_cast<char**>(&h->in_H), (size_t)Tcap * d * 4);
   if (!rc) rc = dalloc(&h->in_tgt, (size_t)Tcap);
+  const bool aug = R >= LCE_AUG_MIN_RANK;
+  if (!rc && aug) rc = dalloc(&h->w_aug, (size_t)Vpad * kBK);
+  if (!rc && aug) rc = dalloc(&h->h_aug, (size_t)Tcap * kBK);
   if (!rc && cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess)
     rc = fail(LORA_CE_ECUDA, "cudaStreamCreate failed");
   if (!rc && !(make_map(&h->mapW_res, h->W, V, d, kBM) && make_map(&h->mapW_str, h->W, V, d, kBN)))
     rc = fail(LORA_CE_ECUDA, "cuTensorMapEncodeTiled failed for W");
+  if (!rc && aug && !(make_map(&h->mapWa_res, h->w_aug, V, kBK, kBM) &&
+                       make_map(&h->mapWa_str, h->w_aug, V, kBK, kBN)))
+    rc = fail(LORA_CE_ECUDA, "cuTensorMapEncodeTiled failed for the rank augmentation");
+  if (!aug) {  // never read without augmentation; any valid map fills the kernel parameter
+    h->mapWa_res = h->mapW_res;
+    h->mapWa_str = h->mapW_str;
+  }
   if (rc) {
     free_all(h);
     if (h->stream) cudaStreamDestroy(h->stream);

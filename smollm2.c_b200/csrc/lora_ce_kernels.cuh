@@ -26,6 +26,16 @@
 //           positions.
 // Neither epilogue needs a reduction across threads, and the T x V logits
 // never leave TMEM/registers.
+//
+// Rank augmentation (ranks 8 and 16): the LoRA term of the logits,
+// s*U[t].B[:,v], joins the tensor-core product as one more 64-wide K-block,
+//   haug[t] = [sU_hi | sU_hi | sU_lo | 0],  waug[v] = [B_hi | B_lo | B_hi | 0]
+// (x_hi = f16(x), x_lo = f16(x - x_hi)), so the accumulator holds
+// h.W + sU_hi.B_hi + sU_hi.B_lo + sU_lo.B_hi: the rank term to about 2^-22
+// relative (only the lo.lo product is dropped), and the epilogues skip r
+// multiply-adds per logit.  At rank 4 the extra K-block (11% more MMA
+// work) costs more than the four multiply-adds it saves, so rank 4 keeps
+// the term in the epilogue.
 #pragma once
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
@@ -44,6 +54,13 @@ constexpr int kAKBytes = kBM * kBK * 2;   // 16 KB per resident K-block
 __host__ __device__ constexpr int str_rows(int pair) { return kBN / pair; }
 __host__ __device__ constexpr int stage_bytes(int pair) { return str_rows(pair) * kBK * 2; }
 __host__ __device__ constexpr int num_stages(int pair) { return kRingBytes / stage_bytes(pair); }
+// A pass whose column records are staged in shared memory may run a smaller
+// ring (Epi::kRing, at least three 16 KB stages in a CTA pair) to make room
+// for them next to the resident tile; otherwise the ring is kRingBytes.
+template <class Epi, bool kStage, int kPair>
+__host__ __device__ constexpr int ring_bytes() {
+  return (kStage && kPair == 2) ? Epi::kRing : kRingBytes;
+}
 // Warp roles: warp 0 TMA producer, warp 1 MMA issuer, then kEpiWarps
 // epilogue warps (4 or 2 per TMEM lane quarter, set per epilogue by its
 // register needs), then one record-loader warp.
@@ -53,6 +70,10 @@ __host__ __device__ constexpr int block_threads(int epi_warps) { return 32 * (ep
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kTmemCols = 512;    // two 256-column fp32 accumulators
 constexpr int kMaxKBlocks = 10;        // d <= 640
+// Smallest rank whose LoRA term joins the MMA as an extra K-block.
+#ifndef LCE_AUG_MIN_RANK
+#define LCE_AUG_MIN_RANK 8
+#endif
 
 // Pair-interleaved layouts.  B (vocab-major) and the per-position records
 // keep the same field of two consecutive columns side by side, so one
@@ -81,7 +102,8 @@ __host__ __device__ inline int tile_owner(long long x, long long total, int G) {
 
 struct GemmArgs {
   int n_a, n_b;      // resident-tile count, streamed-tile count
-  int kblocks;       // d / 64
+  int kblocks;       // K-blocks per tile: kmain, plus one rank block when augmented
+  int kmain;         // d / 64 K-blocks of h / W
   int T, V, R;
   long long Tcap;    // partial-buffer row stride (positions)
   long long Vpad;    // rows of Bt / gBp
@@ -97,23 +119,23 @@ struct GemmArgs {
   float* gBp;         // [seg][Vpad][R]
 };
 
-// Dynamic shared memory: [resident K-blocks | streamed ring | staged
+// Dynamic shared memory: [resident K-blocks | streamed ring (ring bytes) | staged
 // column records (2 x kBN x rec floats, optional) | barriers].
 struct SmemLayout {
   static __host__ __device__ constexpr int a_off() { return 0; }
   static __host__ __device__ constexpr int b_off(int kblocks) { return kblocks * kAKBytes; }
-  static __host__ __device__ constexpr int rec_off(int kblocks) {
-    return b_off(kblocks) + kRingBytes;
+  static __host__ __device__ constexpr int rec_off(int kblocks, int ring) {
+    return b_off(kblocks) + ring;
   }
-  // two record buffers
+  // rec_floats: floats per column summed over the record buffers
   static __host__ __device__ constexpr int rec_bytes(int rec_floats) {
-    return 2 * kBN * rec_floats * 4;
+    return kBN * rec_floats * 4;
   }
-  static __host__ __device__ constexpr int bar_off(int kblocks, int rec_floats) {
-    return rec_off(kblocks) + rec_bytes(rec_floats);
+  static __host__ __device__ constexpr int bar_off(int kblocks, int rec_floats, int ring) {
+    return rec_off(kblocks, ring) + rec_bytes(rec_floats);
   }
-  static __host__ __device__ constexpr int bytes(int kblocks, int rec_floats) {
-    return 1024 /*align slack*/ + bar_off(kblocks, rec_floats) + 256;
+  static __host__ __device__ constexpr int bytes(int kblocks, int rec_floats, int ring) {
+    return 1024 /*align slack*/ + bar_off(kblocks, rec_floats, ring) + 256;
   }
 };
 constexpr int kMaxDynSmem = 232448;  // 227 KB opt-in per CTA on sm_100
@@ -177,9 +199,14 @@ __device__ __forceinline__ float2 f2(float x, float y) { return make_float2(x, y
 
 // Pass 1: the thread owns position t; columns are vocab ids; the records of
 // a column pair are B[:, v], B[:, v+1] interleaved (2R floats).
-template <int R>
+template <int R, bool kAug_ = (R >= LCE_AUG_MIN_RANK)>
 struct EpiLse {
+  static constexpr bool kAug = kAug_;  // rank term in the accumulator
   static constexpr int kRec = R;  // floats per column
+  // ring when records are staged: 3 stages beside 10 resident K-blocks at
+  // rank 8, 2 at rank 16 (which then fits its 32 KB of records)
+  static constexpr int kRing = !kAug ? kRingBytes : R >= 16 ? 32768 : 49152;
+  static constexpr int kRecBufs = 2;  // staged record buffers (tile i+1 loads during tile i)
   static constexpr int kWarps = R == 4 ? 16 : 8;  // 16 at rank 8 would spill
   static constexpr int kCW = (R >= 16 || kWarps == 16) ? 8 : 16;
   static constexpr float kLazy = 8.0f;   // move the reference max only past this
@@ -201,10 +228,12 @@ struct EpiLse {
     t = abs_row;
     valid = t < g.T;
     const long long tt = valid ? t : 0;
+    if constexpr (!kAug) {
 #pragma unroll
-    for (int j = 0; j < R; ++j) {
-      const float u = g.tok[tidx(tt, j, R)];
-      sU2[j] = f2(u, u);
+      for (int j = 0; j < R; ++j) {
+        const float u = g.tok[tidx(tt, j, R)];
+        sU2[j] = f2(u, u);
+      }
     }
     tgt = valid ? __float_as_int(g.tok[tidx(tt, R + 2, R)]) : -1;
     m = -INFINITY;
@@ -236,8 +265,10 @@ struct EpiLse {
       float b[2 * R];
       ld_vec<2 * R>(recs + p * 2 * R, b);
       float2 z2 = f2(acc[2 * p], acc[2 * p + 1]);
+      if constexpr (!kAug) {
 #pragma unroll
-      for (int j = 0; j < R; ++j) z2 = __ffma2_rn(sU2[j], f2(b[2 * j], b[2 * j + 1]), z2);
+        for (int j = 0; j < R; ++j) z2 = __ffma2_rn(sU2[j], f2(b[2 * j], b[2 * j + 1]), z2);
+      }
       if (kTail) {
         if (v0 + 2 * p >= g.V) z2.x = -INFINITY;
         if (v0 + 2 * p + 1 >= g.V) z2.y = -INFINITY;
@@ -305,9 +336,16 @@ struct EpiLse {
 // of a position pair are tok[] fields interleaved (2(R+4) floats).  This
 // pass accumulates the p part of dl = p - onehot; lce_onehot adds the
 // onehot part.
-template <int R>
+template <int R, bool kAug_ = (R >= LCE_AUG_MIN_RANK)>
 struct EpiGrad {
+  static constexpr bool kAug = kAug_;  // rank term in the accumulator
   static constexpr int kRec = R + 4;
+  // 2 stages beside 10 resident K-blocks when staging (rank 8 fits, rank 16
+  // does not and reads its records from global memory with the full ring)
+  static constexpr int kRing = !kAug ? kRingBytes : 32768;
+  // rank 16 stages one record buffer (its 2 x 20 KB do not fit beside 10
+  // resident K-blocks); the loader then waits for the previous tile's release
+  static constexpr int kRecBufs = (kAug && R >= 16) ? 1 : 2;
   static constexpr int kWarps = R <= 8 ? 16 : 8;
   static constexpr int kCW = (R >= 16 || kWarps == 16) ? 8 : 16;
   int v;
@@ -326,8 +364,10 @@ struct EpiGrad {
     const long long vv = valid ? v : 0;
 #pragma unroll
     for (int j = 0; j < R; ++j) {
-      const float b = g.Bt[bidx(vv, j, R)];
-      bv2[j] = f2(b, b);
+      if constexpr (!kAug) {
+        const float b = g.Bt[bidx(vv, j, R)];
+        bv2[j] = f2(b, b);
+      }
       g2[j] = f2(0.f, 0.f);
     }
   }
@@ -345,8 +385,10 @@ struct EpiGrad {
       ld_vec<2 * R>(rp, su);
       const float4 mi = *reinterpret_cast<const float4*>(rp + 2 * R);  // -ML pair, 1/S pair
       float2 z2 = f2(acc[2 * p], acc[2 * p + 1]);
+      if constexpr (!kAug) {
 #pragma unroll
-      for (int j = 0; j < R; ++j) z2 = __ffma2_rn(bv2[j], f2(su[2 * j], su[2 * j + 1]), z2);
+        for (int j = 0; j < R; ++j) z2 = __ffma2_rn(bv2[j], f2(su[2 * j], su[2 * j + 1]), z2);
+      }
       const float2 x2 = __ffma2_rn(z2, L2, f2(mi.x, mi.y));
       const float2 p2 = __fmul2_rn(f2(ex2f(x2.x), ex2f(x2.y)), f2(mi.z, mi.w));
 #pragma unroll
@@ -386,14 +428,19 @@ __device__ __forceinline__ void run_chunk(Epi& epi, const GemmArgs& g, bool tail
 template <class Epi, bool kStage, int kPair>
 __global__ void __launch_bounds__(block_threads(Epi::kWarps), 1)
     lce_gemm_kernel(const __grid_constant__ CUtensorMap map_res,
-                    const __grid_constant__ CUtensorMap map_str, const GemmArgs g) {
+                    const __grid_constant__ CUtensorMap map_str,
+                    const __grid_constant__ CUtensorMap map_res_aug,
+                    const __grid_constant__ CUtensorMap map_str_aug, const GemmArgs g) {
   constexpr int kEpiWarps = Epi::kWarps;
   constexpr int kEpiThreads = epi_threads(kEpiWarps);
   constexpr int kColParts = col_parts(kEpiWarps);
   constexpr int kRecWarp = 2 + kEpiWarps;
-  constexpr int kRecF = kStage ? Epi::kRec : 0;
-  constexpr int kSt = num_stages(kPair);
+  constexpr int kRecF = kStage ? Epi::kRec * Epi::kRecBufs : 0;
+  constexpr int kRB = Epi::kRecBufs;
+  constexpr int kRingB = ring_bytes<Epi, kStage, kPair>();
   constexpr int kStBytes = stage_bytes(kPair);
+  constexpr int kSt = kRingB / kStBytes;
+  static_assert(kSt >= 2 && kSt <= kMaxStages, "ring stages");
   constexpr int kStRows = str_rows(kPair);
   constexpr int kResRows = kBM * kPair;
   extern __shared__ uint8_t smem_raw[];
@@ -402,8 +449,8 @@ __global__ void __launch_bounds__(block_threads(Epi::kWarps), 1)
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* sA = smem + SmemLayout::a_off();
   uint8_t* sB = smem + SmemLayout::b_off(g.kblocks);
-  float* srec = reinterpret_cast<float*>(smem + SmemLayout::rec_off(g.kblocks));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SmemLayout::bar_off(g.kblocks, kRecF));
+  float* srec = reinterpret_cast<float*>(smem + SmemLayout::rec_off(g.kblocks, kRingB));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SmemLayout::bar_off(g.kblocks, kRecF, kRingB));
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
 
   const int warp = threadIdx.x >> 5;
@@ -435,6 +482,10 @@ __global__ void __launch_bounds__(block_threads(Epi::kWarps), 1)
     fence_mbar_init();
     prefetch_tmap(&map_res);
     prefetch_tmap(&map_str);
+    if (g.kblocks > g.kmain) {
+      prefetch_tmap(&map_res_aug);
+      prefetch_tmap(&map_str_aug);
+    }
   }
   if (warp == 1) {
     if constexpr (kPair == 2) {
@@ -474,11 +525,14 @@ __global__ void __launch_bounds__(block_threads(Epi::kWarps), 1)
             mbar_expect_tx(&bars[kBarAFull], (uint32_t)(kPair * g.kblocks * kAKBytes));
           const int row0 = a * kResRows + (int)rank * kBM;
           for (int kb = 0; kb < g.kblocks; ++kb) {
+            // K-blocks past kmain come from the rank-augmentation map, at x = 0
+            const CUtensorMap* m = kb < g.kmain ? &map_res : &map_res_aug;
+            const int kx = (kb < g.kmain ? kb : kb - g.kmain) * kBK;
             if constexpr (kPair == 2)
-              tma_load_2d_pair(sA + kb * kAKBytes, &map_res,
-                               mapa_shared(smem_u32(&bars[kBarAFull]), 0), kb * kBK, row0);
+              tma_load_2d_pair(sA + kb * kAKBytes, m,
+                               mapa_shared(smem_u32(&bars[kBarAFull]), 0), kx, row0);
             else
-              tma_load_2d(sA + kb * kAKBytes, &map_res, &bars[kBarAFull], kb * kBK, row0);
+              tma_load_2d(sA + kb * kAKBytes, m, &bars[kBarAFull], kx, row0);
           }
           cur_a = a;
           ++a_uses;
@@ -490,12 +544,13 @@ __global__ void __launch_bounds__(block_threads(Epi::kWarps), 1)
             break;
           }
           if (leader) mbar_expect_tx(&bars[kBarFull + stage], (uint32_t)(kPair * kStBytes));
+          const CUtensorMap* m = kb < g.kmain ? &map_str : &map_str_aug;
+          const int kx = (kb < g.kmain ? kb : kb - g.kmain) * kBK;
           if constexpr (kPair == 2)
-            tma_load_2d_pair(sB + stage * kStBytes, &map_str,
-                             mapa_shared(smem_u32(&bars[kBarFull + stage]), 0), kb * kBK, srow0);
+            tma_load_2d_pair(sB + stage * kStBytes, m,
+                             mapa_shared(smem_u32(&bars[kBarFull + stage]), 0), kx, srow0);
           else
-            tma_load_2d(sB + stage * kStBytes, &map_str, &bars[kBarFull + stage], kb * kBK,
-                        srow0);
+            tma_load_2d(sB + stage * kStBytes, m, &bars[kBarFull + stage], kx, srow0);
           issued_parity[stage] = (int)phase;
           if (++stage == kSt) {
             stage = 0;
@@ -599,12 +654,14 @@ __global__ void __launch_bounds__(block_threads(Epi::kWarps), 1)
         epi.begin(g, a * kResRows + (int)rank * kBM + row);
         cur_a = a;
       }
-      const float* recs = kStage ? srec + (li & 1) * (kBN * Epi::kRec) : Epi::global_recs(g, b);
+      const int rbuf = (int)(li % kRB);
+      const uint32_t ruse = (uint32_t)(li / kRB);
+      const float* recs = kStage ? srec + rbuf * (kBN * Epi::kRec) : Epi::global_recs(g, b);
       if (failed) continue;
       const int buf = (int)(li & 1);
       const uint32_t use = (uint32_t)(li >> 1);
       if (!mbar_wait(&bars[kBarAccFull + buf], use & 1, g.err, kErrWaitEpilogue) ||
-          (kStage && !mbar_wait(&bars[kBarRecFull + buf], use & 1, g.err, kErrWaitEpilogue))) {
+          (kStage && !mbar_wait(&bars[kBarRecFull + rbuf], ruse & 1, g.err, kErrWaitEpilogue))) {
         failed = true;
         continue;
       }
@@ -636,7 +693,7 @@ __global__ void __launch_bounds__(block_threads(Epi::kWarps), 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        if (kStage) mbar_arrive(&bars[kBarRecEmpty + buf]);
+        if (kStage) mbar_arrive(&bars[kBarRecEmpty + rbuf]);
         if constexpr (kPair == 2)
           mbar_arrive_cluster(mapa_shared(smem_u32(&bars[kBarAccEmpty + buf]), 0));
         else
@@ -648,15 +705,15 @@ __global__ void __launch_bounds__(block_threads(Epi::kWarps), 1)
   } else if (warp == kRecWarp) {
     // ------------------------------------------------ record loader (both CTAs)
     // The records of tile li (256 columns, one contiguous block in global)
-    // go to buffer li%2 once the epilogue has released tile li-2.
+    // go to buffer li % kRB once the epilogue has released tile li - kRB.
     if (kStage && lane == 0) {
       constexpr uint32_t kBytes = (uint32_t)(kBN * Epi::kRec * 4);
       long long li = 0;
       int issued = 0;
       for (long long x = x_begin; x < x_end; ++x, ++li) {
         const int b = (int)(x % g.n_b);
-        const int buf = (int)(li & 1);
-        const uint32_t use = (uint32_t)(li >> 1);
+        const int buf = (int)(li % kRB);
+        const uint32_t use = (uint32_t)(li / kRB);
         if (use > 0 &&
             !mbar_wait(&bars[kBarRecEmpty + buf], (use - 1) & 1, g.err, kErrWaitProducer))
           break;
@@ -666,8 +723,8 @@ __global__ void __launch_bounds__(block_threads(Epi::kWarps), 1)
         ++issued;
       }
       // drain: the last load into each buffer has landed
-      for (int k = issued - 2 < 0 ? 0 : issued - 2; k < issued; ++k)
-        mbar_drain_wait(&bars[kBarRecFull + (k & 1)], (uint32_t)((k >> 1) & 1), g.err);
+      for (int k = issued - kRB < 0 ? 0 : issued - kRB; k < issued; ++k)
+        mbar_drain_wait(&bars[kBarRecFull + (k % kRB)], (uint32_t)((k / kRB) & 1), g.err);
     }
   }
 
@@ -692,7 +749,8 @@ template <int R>
 __global__ void lce_prep(const void* __restrict__ H, int dtype, int T, int Tpad, int d,
                          const float* __restrict__ A, float scale,
                          const int32_t* __restrict__ targets, int V,
-                         __half* __restrict__ h16, float* __restrict__ tok, int* err) {
+                         __half* __restrict__ h16, float* __restrict__ tok, int* err,
+                         __half* __restrict__ haug) {
   extern __shared__ __align__(16) float sA[];  // [d][R]
   for (int k = threadIdx.x; k < d * R; k += blockDim.x) sA[k] = A[k];
   __syncthreads();
@@ -702,6 +760,8 @@ __global__ void lce_prep(const void* __restrict__ H, int dtype, int T, int Tpad,
     if (w >= T) {  // padding position: all fields zero, target -1
       for (int f = lane; f < tok_stride(R); f += 32)
         tok[tidx(w, f, R)] = f == R + 2 ? __int_as_float(-1) : 0.f;
+      if (haug) *reinterpret_cast<__half2*>(haug + (long long)w * 64 + 2 * lane) =
+          __floats2half2_rn(0.f, 0.f);
       continue;
     }
     float u[R];
@@ -729,6 +789,21 @@ __global__ void lce_prep(const void* __restrict__ H, int dtype, int T, int Tpad,
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) u[j] += __shfl_xor_sync(0xffffffffu, u[j], off);
     }
+    if (haug) {
+      // lane l writes augmentation columns 2l, 2l+1: [sU_hi | sU_hi | sU_lo | 0]
+      __half hv2[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int c = 2 * lane + k, part = c / R, jc = c - part * R;
+        float su = 0.f;
+#pragma unroll
+        for (int j = 0; j < R; ++j) su = (j == jc) ? scale * u[j] : su;
+        const __half hi = __float2half_rn(su);
+        const __half lo = __float2half_rn(su - __half2float(hi));
+        hv2[k] = part < 2 ? hi : part == 2 ? lo : __float2half_rn(0.f);
+      }
+      *reinterpret_cast<__half2*>(haug + (long long)w * 64 + 2 * lane) = __halves2half2(hv2[0], hv2[1]);
+    }
     if (lane == 0) {
       int tg = targets[w];
       if (tg < 0 || tg >= V) {
@@ -742,6 +817,30 @@ __global__ void lce_prep(const void* __restrict__ H, int dtype, int T, int Tpad,
       tok[tidx(w, R + 2, R)] = __int_as_float(tg);
       tok[tidx(w, R + 3, R)] = 0.f;
     }
+  }
+}
+
+// The vocabulary side of rank augmentation: waug[v] = [B_hi | B_lo | B_hi | 0]
+// (64 f16 per row, v < Vpad; rows >= V are zero like B).  One thread per
+// 8 columns of a row (16-byte stores).  Rebuilt at the start of every step
+// from the current B.
+template <int R>
+__global__ void lce_aug_b(const float* __restrict__ Bt, long long Vpad, __half* __restrict__ waug) {
+  static_assert(3 * R <= 64, "rank augmentation fits one 64-wide K-block");
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < Vpad * 8;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long v = i >> 3;
+    const int c0 = (int)(i & 7) * 8;
+    __align__(16) __half o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int c = c0 + e, part = c / R, j = c - part * R;
+      const float b = part < 3 ? Bt[bidx(v, j, R)] : 0.f;
+      const __half hi = __float2half_rn(b);
+      const __half lo = __float2half_rn(b - __half2float(hi));
+      o[e] = part == 1 ? lo : hi;  // part 3 (padding): b = 0, hi = 0
+    }
+    *reinterpret_cast<uint4*>(waug + v * 64 + c0) = *reinterpret_cast<const uint4*>(o);
   }
 }
 

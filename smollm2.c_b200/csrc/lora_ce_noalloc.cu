@@ -125,7 +125,8 @@ int setup_device(int dev, DeviceScratch** out) {
       return na_fail(LORA_CE_ECUDA, "cudaGetSymbolAddress failed for the scratch arrays");
     auto kern = lce_gemm_kernel<EpiLse<kNaRank>, true, 2>;
     const int kblocks_max = kNaMaxD / kBK;
-    const int smem = SmemLayout::bytes(kblocks_max, EpiLse<kNaRank>::kRec);
+    using Epi = EpiLse<kNaRank>;
+    const int smem = SmemLayout::bytes(kblocks_max, Epi::kRec * Epi::kRecBufs, Epi::kRing);
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
         cudaSuccess)
       return na_fail(LORA_CE_ECUDA, "cudaFuncSetAttribute failed");
@@ -232,9 +233,11 @@ extern "C" int lora_ce_token_loss_noalloc(const uint16_t* d_W, int32_t vocab, in
   if ((reinterpret_cast<uintptr_t>(d_H) & 15) != 0)
     return na_fail(LORA_CE_EINVAL, "hidden states must be 16-byte aligned");
   lce_prep<R><<<(int)std::min<long long>((Tpad + 7) / 8, 592), 256, (size_t)d * R * 4, st>>>(
-      d_H, h_dtype, T, (int)Tpad, d, s->params, scale, d_targets, V, s->h16, s->tok, s->err);
+      d_H, h_dtype, T, (int)Tpad, d, s->params, scale, d_targets, V, s->h16, s->tok, s->err,
+      nullptr);
   GemmArgs g{};
   g.kblocks = kblocks;
+  g.kmain = kblocks;
   g.T = T;
   g.V = V;
   g.R = R;
@@ -251,7 +254,8 @@ extern "C" int lora_ce_token_loss_noalloc(const uint16_t* d_W, int32_t vocab, in
   g.n_b = n_b1;
   g.Tcap = stride1;
   {
-    const int smem = SmemLayout::bytes(kblocks, EpiLse<R>::kRec);
+    using Epi = EpiLse<R>;
+    const int smem = SmemLayout::bytes(kblocks, Epi::kRec * Epi::kRecBufs, Epi::kRing);
     auto kern = lce_gemm_kernel<EpiLse<R>, true, 2>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
         cudaSuccess)
@@ -268,7 +272,7 @@ extern "C" int lora_ce_token_loss_noalloc(const uint16_t* d_W, int32_t vocab, in
     attr[0].val.clusterDim.z = 1;
     lc.attrs = attr;
     lc.numAttrs = 1;
-    if (cudaLaunchKernelEx(&lc, kern, mapH, mapW, g) != cudaSuccess)
+    if (cudaLaunchKernelEx(&lc, kern, mapH, mapW, mapH, mapW, g) != cudaSuccess)
       return na_fail(LORA_CE_ECUDA, "pass-1 launch failed");
   }
   lce_combine<R><<<(T + 7) / 8, 256, 0, st>>>(T, cp1, res_rows, n_b1, G1, stride1, s->pmax,
