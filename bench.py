@@ -82,6 +82,30 @@ def env_int(name, default):
         return default
 
 
+def bind_near_gpu(local: int):
+    """Run this process on the CPUs of the GPU's own NUMA node (from sysfs),
+    so the pinned host buffers of the end-to-end leg are allocated there and
+    host-device copies do not cross the socket link.  Returns the CPU list
+    or None when the topology is not visible."""
+    try:
+        import torch
+        p = torch.cuda.get_device_properties(local)
+        bus = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        with open(f"/sys/bus/pci/devices/{bus}/local_cpulist") as f:
+            spec = f.read().strip()
+        cpus = set()
+        for part in spec.split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        cpus &= os.sched_getaffinity(0)
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+            return spec
+    except (OSError, ValueError, AttributeError):
+        pass
+    return None
+
+
 def peaks():
     p = os.path.join(REPO, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -92,18 +116,58 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed
-    region."""
+    """SM clocks, power and throttle reasons during the timed region: an
+    NVML polling thread (every 2 ms, so that a region of a few tens of ms
+    still gets many samples), or nvidia-smi -lms 200 when NVML is not
+    importable."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+               "hw_thermal_slowdown": 0x40}
 
     def __init__(self, gpu: int):
         self.gpu = gpu
         self.proc = None
+        self.rows = []
+        self.thread = None
+        self.stop = False
+
+    def _poll(self, nv, hdl):
+        clk = nv.NVML_CLOCK_SM
+        fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        mx = nv.nvmlDeviceGetMaxClockInfo(hdl, clk)
+        while not self.stop:
+            try:
+                self.rows.append((float(nv.nvmlDeviceGetClockInfo(hdl, clk)), float(mx),
+                                  nv.nvmlDeviceGetPowerUsage(hdl) / 1000.0, int(fn(hdl))))
+            except Exception:  # noqa: BLE001 - a failed read only loses a sample
+                pass
+            time.sleep(0.002)
 
     def __enter__(self):
+        try:
+            import threading
+            import pynvml as nv
+            nv.nvmlInit()
+            busid = None
+            try:
+                import torch
+                p = torch.cuda.get_device_properties(self.gpu)
+                busid = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            except Exception:  # noqa: BLE001
+                pass
+            hdl = (nv.nvmlDeviceGetHandleByPciBusId(busid) if busid
+                   else nv.nvmlDeviceGetHandleByIndex(self.gpu))
+            self.thread = threading.Thread(target=self._poll, args=(nv, hdl), daemon=True)
+            self.thread.start()
+            time.sleep(0.01)
+            return self
+        except Exception:  # noqa: BLE001 - fall back to nvidia-smi
+            self.thread = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
@@ -116,6 +180,10 @@ class ClockSampler:
 
     def __exit__(self, *exc):
         self.out = ""
+        if self.thread is not None:
+            self.stop = True
+            self.thread.join(timeout=2)
+            return
         if self.proc:
             self.proc.terminate()
             try:
@@ -123,24 +191,26 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
                 self.out = ""
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for line in (self.out or "").strip().splitlines():
+                f = [x.strip() for x in line.split(",")]
+                if len(f) < 9:
+                    continue
+                try:
+                    bits = sum(self.REASONS[n] for n, v in zip(names, f[5:9]) if v.lower() == "active")
+                    self.rows.append((float(f[1]), float(f[2]), float(f[3]), bits))
+                except ValueError:
+                    continue
 
     def summary(self):
-        rows = []
-        for line in (self.out or "").strip().splitlines():
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                rows.append((float(f[1]), float(f[2]), float(f[3]), f[5:9]))
-            except ValueError:
-                continue
+        rows = self.rows
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, v in zip(names, r[3]) if v.lower() == "active"})
+        reasons = sorted({n for r in rows for n, b in self.REASONS.items() if r[3] & b})
         loaded = [r[0] for r in rows if r[2] > 200.0] or [r[0] for r in rows]
         return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows),
+                "source": "nvml" if self.thread is not None else "nvidia-smi"}
 
 
 # ----------------------------------------------------------------- CPU leg
@@ -491,6 +561,7 @@ def main():
         ref = CpuReference()
         cpu = ref.sample(15.0)
         ref.close()
+    numa_cpus = bind_near_gpu(local)  # after the CPU pool, which uses every core
 
     T = step_tokens(world) // world  # this rank's positions (strong scaling splits the total)
     h, tgt, A, B = wl.make_step_inputs(1000 + rank, T, V, D, R)
@@ -612,7 +683,11 @@ def main():
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": UNIT,
                     "h2d_bytes_per_step": int(hH.numel() * 2 + hT.numel() * 4),
-                    "d2h_bytes_per_step": 8},
+                    "d2h_bytes_per_step": 8,
+                    "host_cpus": numa_cpus,
+                    "ms_per_step": {"min": round(min(e2e_ms), 4),
+                                    "median": round(statistics.median(e2e_ms), 4),
+                                    "max": round(max(e2e_ms), 4)}},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk.summary(),
         }

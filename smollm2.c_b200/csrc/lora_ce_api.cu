@@ -124,6 +124,14 @@ int max_segments(int n_a, int n_b, int G) {
 
 }  // namespace
 
+namespace {
+// Chunks of a host-input step: pass 1 runs once per chunk of position blocks
+// so that the copy of the next chunk overlaps it.  Chunks of at least 8
+// blocks keep each launch's tile ranges long.
+constexpr int kMaxChunks = 4;
+int step_chunks(int n_a1) { return n_a1 >= 32 ? 4 : n_a1 >= 16 ? 2 : 1; }
+}  // namespace
+
 struct lora_ce_handle {
   lora_ce_config cfg{};
   // r: the adapter's rank; R: the rank the kernels run at, r rounded up to
@@ -136,6 +144,33 @@ struct lora_ce_handle {
   int pair = 2;             // 2: CTA-pair (cta_group::2) GEMM tiles; 1: single-CTA tiles
   int units1 = 0, units2 = 0;  // co-resident tile-range owners of pass 1 / pass 2
   cudaStream_t stream = nullptr;
+  // host-input steps copy h in chunks on `cstream` while the compute stream
+  // converts and runs pass 1 on the chunks that have arrived
+  cudaStream_t cstream = nullptr;
+  cudaEvent_t ev_start = nullptr;
+  cudaEvent_t ev_chunk[kMaxChunks] = {};
+  // CUDA graphs of whole steps, replayed while (T, dtype, input pointers)
+  // repeat; only Adam's bias corrections change between replays
+  struct StepGraph {
+    bool valid = false;
+    bool host = false;  // lora_ce_step (copies + read-back) or lora_ce_step_device
+    int T = 0, dtype = 0;
+    const void* H = nullptr;
+    const int32_t* tgt = nullptr;
+    float* d_loss = nullptr;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    cudaGraphNode_t adam = nullptr;
+    cudaKernelNodeParams adam_p{};
+    long long nparam = 0;
+    int launches = 0;
+    unsigned long long last_use = 0;
+  };
+  static constexpr int kGraphs = 4;
+  StepGraph graphs[kGraphs];
+  unsigned long long graph_clock = 0;
+  bool use_graphs = true;
+  float* res_host = nullptr;  // pinned [loss, error code] read back by lora_ce_step
   bool poisoned = false;
   bool have_weight = false;
   int32_t step = 0;
@@ -180,6 +215,8 @@ struct lora_ce_handle {
 
 namespace {
 
+void drop_graphs(lora_ce_handle* h);
+
 template <class T>
 int dalloc(T** p, size_t count) {
   if (cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T) + 16) != cudaSuccess)
@@ -187,6 +224,15 @@ int dalloc(T** p, size_t count) {
   if (cudaMemset(*p, 0, count * sizeof(T) + 16) != cudaSuccess)
     return fail(LORA_CE_ECUDA, "cudaMemset failed");
   return 0;
+}
+
+void free_streams(lora_ce_handle* h) {
+  if (h->res_host) cudaFreeHost(h->res_host);
+  for (cudaEvent_t e : h->ev_chunk)
+    if (e) cudaEventDestroy(e);
+  if (h->ev_start) cudaEventDestroy(h->ev_start);
+  if (h->cstream) cudaStreamDestroy(h->cstream);
+  if (h->stream) cudaStreamDestroy(h->stream);
 }
 
 void free_all(lora_ce_handle* h) {
@@ -219,6 +265,25 @@ using GemmKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensor
                            const CUtensorMap, const GemmArgs);
 
 // K-blocks of a GEMM tile: d / 64, plus one when the rank term is augmented.
+// Adam's arguments for step `step` (the bias corrections 1 - beta^step are
+// computed on the host with powf, as src/train.c:178-179 does).
+AdamArgs adam_args(const lora_ce_handle* h, long long nparam, int32_t step) {
+  AdamArgs aa{};
+  aa.n = nparam;
+  aa.lr = h->cfg.lr;
+  aa.b1 = h->cfg.beta1;
+  aa.b2 = h->cfg.beta2;
+  aa.c1 = 1.0f - h->cfg.beta1;
+  aa.c2 = 1.0f - h->cfg.beta2;
+  aa.eps = h->cfg.eps;
+  aa.wd = h->cfg.weight_decay;
+  aa.clip = h->cfg.clip_norm;
+  aa.b1t = 1.0f - powf(h->cfg.beta1, (float)step);
+  aa.b2t = 1.0f - powf(h->cfg.beta2, (float)step);
+  aa.n_norm_parts = aa.clip > 0.f ? 256 : 0;
+  return aa;
+}
+
 template <class Epi>
 int tile_kblocks(int d) {
   return d / kBK + (Epi::kAug ? 1 : 0);
@@ -289,7 +354,7 @@ inline void mark(lora_ce_handle* h, int phase) {
 
 template <int R>
 int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t* dtg,
-             float* d_loss_out) {
+             float* d_loss_out, int chunks, const cudaEvent_t* chunk_ready) {
   cudaStream_t st = h->stream;
   const int d = h->d, V = h->V;
   constexpr bool kAug = EpiLse<R>::kAug;
@@ -307,30 +372,17 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
                !make_map(&mapHa_str, h->h_aug, T, kBK, kBN)))
     return fail(LORA_CE_ECUDA, "cuTensorMapEncodeTiled failed for the rank augmentation");
 
-  // 1. convert h, U = h.A, per-position records
-  mark(h, kPhPrep);
-  {
-    const int threads = 256;  // 8 warps per block, grid-stride over positions
-    const int blocks = (int)std::min<long long>((Tpad + 7) / 8, 4LL * h->num_sms);
-    lce_prep<R><<<blocks, threads, (size_t)d * R * 4, st>>>(dH, dtype, T, (int)Tpad, d, h->params,
-                                                           h->cfg.scale, dtg, V, h->h16, h->tok,
-                                                           h->err, kAug ? h->h_aug : nullptr);
-    ++launches;
-  }
-  if constexpr (kAug) {  // [B_hi | B_lo | B_hi] rows from the current B
-    const int blocks = (int)std::min<long long>((h->Vpad * 8 + 255) / 256, 8LL * h->num_sms);
-    lce_aug_b<R><<<blocks, 256, 0, st>>>(h->params + (long long)d * R, h->Vpad, h->w_aug);
-    ++launches;
-  }
   const int pair = h->pair;
   const int res_rows = kBM * pair;
-  mark(h, kPhPass1);
-  // 2. pass 1: per-position max / sum / q over the vocabulary
   const int n_a1 = (T + res_rows - 1) / res_rows, n_b1 = (int)(h->Vpad / kBN);
-  const long long total1 = (long long)n_a1 * n_b1;
-  const int G1 = (int)std::min<long long>(h->units1, total1);
+  chunks = std::max(1, std::min(chunks, n_a1));
   const int cp1 = col_parts(EpiLse<R>::kWarps), cp2 = col_parts(EpiGrad<R>::kWarps);
-  const int seg1 = cp1 * max_segments(n_a1, n_b1, G1);
+  int seg1 = 0;
+  for (int c = 0; c < chunks; ++c) {
+    const int na = (int)(tile_start(c + 1, n_a1, chunks) - tile_start(c, n_a1, chunks));
+    const long long tot = (long long)na * n_b1;
+    seg1 = std::max(seg1, cp1 * max_segments(na, n_b1, (int)std::min<long long>(h->units1, tot)));
+  }
   const long long stride1 = (long long)n_a1 * res_rows;
   if ((long long)seg1 * stride1 > h->p1_cap)
     return fail(LORA_CE_ESTATE, "pass-1 partial buffer too small");
@@ -349,19 +401,46 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
   g.p_q = h->p_q;
   g.z_tgt = h->z_tgt;
   g.gBp = h->gBp;
-  g.n_a = n_a1;
-  g.n_b = n_b1;
   g.Tcap = stride1;
-  {
+
+  mark(h, kPhPrep);
+  if constexpr (kAug) {  // [B_hi | B_lo | B_hi] rows from the current B
+    const int blocks = (int)std::min<long long>((h->Vpad * 8 + 255) / 256, 8LL * h->num_sms);
+    lce_aug_b<R><<<blocks, 256, 0, st>>>(h->params + (long long)d * R, h->Vpad, h->w_aug);
+    ++launches;
+  }
+  // 1. per chunk of position blocks: convert h, U = h.A, per-position
+  //    records; 2. pass 1 on those positions (per-position max / sum / q)
+  for (int c = 0; c < chunks; ++c) {
+    const int a_lo = (int)tile_start(c, n_a1, chunks), a_hi = (int)tile_start(c + 1, n_a1, chunks);
+    const int t_lo = a_lo * res_rows;
+    const int t_hi = c + 1 == chunks ? (int)Tpad : a_hi * res_rows;  // last chunk pads to Tpad
+    if (chunk_ready) LCE_CUDA(cudaStreamWaitEvent(st, chunk_ready[c], 0));
+    {
+      const int threads = 256;  // 8 warps per block, grid-stride over positions
+      const int blocks = (int)std::min<long long>((t_hi - t_lo + 7) / 8, 4LL * h->num_sms);
+      lce_prep<R><<<blocks, threads, (size_t)d * R * 4, st>>>(
+          dH, dtype, t_lo, t_hi, T, d, h->params, h->cfg.scale, dtg, V, h->h16, h->tok, h->err,
+          kAug ? h->h_aug : nullptr);
+      ++launches;
+    }
+    if (c == 0) mark(h, kPhPass1);
+    g.a0 = a_lo;
+    g.n_a = a_hi - a_lo;
+    g.n_b = n_b1;
+    const long long tot = (long long)g.n_a * n_b1;
+    const int Gc = (int)std::min<long long>(h->units1, tot);
     int rc = launch_gemm<EpiLse<R>>(mapH_res, pair == 2 ? h->mapW_res : h->mapW_str, mapHa_res,
-                                    pair == 2 ? h->mapWa_res : h->mapWa_str, g, G1, pair, kblocks,
+                                    pair == 2 ? h->mapWa_res : h->mapWa_str, g, Gc, pair, kblocks,
                                     st);
     if (rc) return rc;
     ++launches;
   }
+  g.a0 = 0;
   // 3. merge partials -> M, 1/S, loss_t, dU
   mark(h, kPhCombine);
-  lce_combine<R><<<(T + 7) / 8, 256, 0, st>>>(T, cp1, res_rows, n_b1, G1, stride1, h->p_max,
+  lce_combine<R><<<(T + 7) / 8, 256, 0, st>>>(T, cp1, res_rows, n_b1, h->units1, chunks, stride1,
+                                                  h->p_max,
                                                   h->p_sum,
                                                   h->p_q, h->z_tgt, g.Bt, h->cfg.scale, h->tok,
                                                   h->dU, h->loss_tok);
@@ -406,23 +485,10 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
       return fail(LORA_CE_ENCCL, "ncclAllReduce failed");
   }
   // 8. clip norm (optional), 9. Adam
-  AdamArgs aa{};
-  aa.n = nparam;
-  aa.lr = h->cfg.lr;
-  aa.b1 = h->cfg.beta1;
-  aa.b2 = h->cfg.beta2;
-  aa.c1 = 1.0f - h->cfg.beta1;
-  aa.c2 = 1.0f - h->cfg.beta2;
-  aa.eps = h->cfg.eps;
-  aa.wd = h->cfg.weight_decay;
-  aa.clip = h->cfg.clip_norm;
   const int32_t next_step = h->step + 1;
-  aa.b1t = 1.0f - powf(h->cfg.beta1, (float)next_step);
-  aa.b2t = 1.0f - powf(h->cfg.beta2, (float)next_step);
-  aa.n_norm_parts = 0;
+  AdamArgs aa = adam_args(h, nparam, next_step);
   mark(h, kPhNorm);
   if (aa.clip > 0.f) {
-    aa.n_norm_parts = 256;
     lce_sqnorm<<<256, 256, 0, st>>>(nparam, h->Gbuf, h->norm_parts);
     ++launches;
   }
@@ -442,11 +508,11 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
 }
 
 int dispatch_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t* dtg,
-                  float* d_loss) {
+                  float* d_loss, int chunks = 1, const cudaEvent_t* chunk_ready = nullptr) {
   switch (h->R) {
-    case 4: return run_step<4>(h, dH, dtype, T, dtg, d_loss);
-    case 8: return run_step<8>(h, dH, dtype, T, dtg, d_loss);
-    case 16: return run_step<16>(h, dH, dtype, T, dtg, d_loss);
+    case 4: return run_step<4>(h, dH, dtype, T, dtg, d_loss, chunks, chunk_ready);
+    case 8: return run_step<8>(h, dH, dtype, T, dtg, d_loss, chunks, chunk_ready);
+    case 16: return run_step<16>(h, dH, dtype, T, dtg, d_loss, chunks, chunk_ready);
   }
   return fail(LORA_CE_EINVAL, "unsupported rank");
 }
@@ -479,6 +545,151 @@ int check_device_error(lora_ce_handle* h) {
     return fail(LORA_CE_EDEVICE, buf);
   }
   return 0;
+}
+
+}  // namespace
+
+namespace {
+
+void drop_graph(lora_ce_handle::StepGraph& gph) {
+  if (gph.exec) cudaGraphExecDestroy(gph.exec);
+  if (gph.graph) cudaGraphDestroy(gph.graph);
+  gph = lora_ce_handle::StepGraph{};
+}
+
+void drop_graphs(lora_ce_handle* h) {
+  for (auto& gph : h->graphs) drop_graph(gph);
+}
+
+// Everything one step enqueues on the handle's streams.  Host-input steps
+// (H, targets in host memory) copy them in (h in chunks on the copy stream,
+// see run_step) and read [loss, error code] back into res_host;
+// device-input steps write the loss to d_loss.
+int enqueue_step(lora_ce_handle* h, bool host, const void* H, int dtype, int T,
+                 const int32_t* targets, float* d_loss) {
+  if (!host) return dispatch_step(h, H, dtype, T, targets, d_loss);
+  LCE_CUDA(cudaMemcpyAsync(h->in_tgt, targets, (size_t)T * 4, cudaMemcpyHostToDevice, h->stream));
+  const int res_rows = kBM * h->pair;
+  const int n_a1 = (T + res_rows - 1) / res_rows;
+  const int chunks = h->prof ? 1 : step_chunks(n_a1);
+  const size_t row_bytes = (size_t)h->d * elt_size(dtype);
+  LCE_CUDA(cudaEventRecord(h->ev_start, h->stream));  // the previous step is done with in_H
+  LCE_CUDA(cudaStreamWaitEvent(h->cstream, h->ev_start, 0));
+  for (int c = 0; c < chunks; ++c) {
+    const long long t_lo = tile_start(c, n_a1, chunks) * res_rows;
+    const long long t_hi = std::min<long long>(T, tile_start(c + 1, n_a1, chunks) * res_rows);
+    LCE_CUDA(cudaMemcpyAsync(static_cast<char*>(h->in_H) + t_lo * row_bytes,
+                             static_cast<const char*>(H) + t_lo * row_bytes,
+                             (size_t)(t_hi - t_lo) * row_bytes, cudaMemcpyHostToDevice, h->cstream));
+    LCE_CUDA(cudaEventRecord(h->ev_chunk[c], h->cstream));
+  }
+  int rc = dispatch_step(h, h->in_H, dtype, T, h->in_tgt, h->d_loss, chunks, h->ev_chunk);
+  if (rc) return rc;
+  LCE_CUDA(cudaMemcpyAsync(h->d_loss + 1, h->err, 4, cudaMemcpyDeviceToDevice, h->stream));
+  LCE_CUDA(cudaMemcpyAsync(h->res_host, h->d_loss, 8, cudaMemcpyDeviceToHost, h->stream));
+  return 0;
+}
+
+// The cached graph for these arguments, captured on first use; nullptr when
+// capture is not possible (the caller then launches the step directly).
+lora_ce_handle::StepGraph* step_graph(lora_ce_handle* h, bool host, const void* H, int dtype,
+                                      int T, const int32_t* targets, float* d_loss) {
+  for (auto& gph : h->graphs)
+    if (gph.valid && gph.host == host && gph.T == T && gph.dtype == dtype && gph.H == H &&
+        gph.tgt == targets && gph.d_loss == d_loss) {
+      gph.last_use = ++h->graph_clock;
+      return &gph;
+    }
+  lora_ce_handle::StepGraph* slot = &h->graphs[0];
+  for (auto& gph : h->graphs)
+    if (!gph.valid || gph.last_use < slot->last_use) slot = &gph;
+  drop_graph(*slot);
+  // capturing enqueues nothing: restore the host-side step bookkeeping after
+  const int32_t step = h->step, launches = h->launches;
+  const int last_T = h->last_T;
+  if (cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeRelaxed) != cudaSuccess) return nullptr;
+  const int rc = enqueue_step(h, host, H, dtype, T, targets, d_loss);
+  const int new_launches = h->launches;
+  h->step = step;
+  h->launches = launches;
+  h->last_T = last_T;
+  cudaGraph_t graph = nullptr;
+  const cudaError_t ce = cudaStreamEndCapture(h->stream, &graph);
+  if (rc || ce != cudaSuccess || !graph) {
+    if (graph) cudaGraphDestroy(graph);
+    cudaGetLastError();
+    return nullptr;
+  }
+  cudaGraphExec_t exec = nullptr;
+  if (cudaGraphInstantiate(&exec, graph, 0) != cudaSuccess) {
+    cudaGraphDestroy(graph);
+    cudaGetLastError();
+    return nullptr;
+  }
+  // the Adam node, whose bias corrections change every step
+  size_t n = 0;
+  cudaGraphGetNodes(graph, nullptr, &n);
+  std::vector<cudaGraphNode_t> nodes(n);
+  cudaGraphGetNodes(graph, nodes.data(), &n);
+  cudaGraphNode_t adam = nullptr;
+  cudaKernelNodeParams ap{};
+  for (cudaGraphNode_t nd : nodes) {
+    cudaGraphNodeType ty;
+    if (cudaGraphNodeGetType(nd, &ty) != cudaSuccess || ty != cudaGraphNodeTypeKernel) continue;
+    cudaKernelNodeParams p{};
+    if (cudaGraphKernelNodeGetParams(nd, &p) == cudaSuccess &&
+        p.func == reinterpret_cast<void*>(lce_adam)) {
+      adam = nd;
+      ap = p;
+    }
+  }
+  if (!adam) {
+    cudaGraphExecDestroy(exec);
+    cudaGraphDestroy(graph);
+    return nullptr;
+  }
+  slot->valid = true;
+  slot->host = host;
+  slot->T = T;
+  slot->dtype = dtype;
+  slot->H = H;
+  slot->tgt = targets;
+  slot->d_loss = d_loss;
+  slot->graph = graph;
+  slot->exec = exec;
+  slot->adam = adam;
+  slot->adam_p = ap;
+  slot->nparam = (long long)h->d * h->R + h->Vpad * h->R;
+  slot->launches = new_launches;
+  slot->last_use = ++h->graph_clock;
+  return slot;
+}
+
+// Replay: set this step's Adam arguments, launch the graph.
+int launch_step_graph(lora_ce_handle* h, lora_ce_handle::StepGraph* gph, int T) {
+  AdamArgs aa = adam_args(h, gph->nparam, h->step + 1);
+  float* d_loss = gph->host ? h->d_loss : gph->d_loss;
+  void* args[] = {&aa, &h->params, &h->mom1, &h->mom2, &h->Gbuf, &h->gmean, &h->norm_parts,
+                  &d_loss};
+  cudaKernelNodeParams p = gph->adam_p;
+  p.kernelParams = args;
+  p.extra = nullptr;
+  LCE_CUDA(cudaGraphExecKernelNodeSetParams(gph->exec, gph->adam, &p));
+  LCE_CUDA(cudaGraphLaunch(gph->exec, h->stream));
+  h->step += 1;
+  h->launches = gph->launches;
+  h->last_T = T;
+  return 0;
+}
+
+int run_or_replay(lora_ce_handle* h, bool host, const void* H, int dtype, int T,
+                  const int32_t* targets, float* d_loss) {
+  if (h->use_graphs && !h->prof) {
+    lora_ce_handle::StepGraph* gph = step_graph(h, host, H, dtype, T, targets, d_loss);
+    if (gph) return launch_step_graph(h, gph, T);
+    h->use_graphs = false;  // capture failed: launch directly from now on
+  }
+  return enqueue_step(h, host, H, dtype, T, targets, d_loss);
 }
 
 }  // namespace
@@ -528,6 +739,8 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
   {
     const char* e = getenv("LORA_CE_CTA_PAIR");  // "1": single-CTA tiles (comparison runs)
     h->pair = (e && e[0] == '1') ? 1 : 2;
+    const char* gr = getenv("LORA_CE_GRAPHS");  // "0": launch every step directly
+    h->use_graphs = !(gr && gr[0] == '0');
   }
   const int R = h->R, d = h->d;
   const int res_rows = kBM * h->pair;
@@ -558,10 +771,18 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
   int s2 = 1;
   const int n_b1 = (int)(Vpad / kBN), n_a2 = (int)((V + res_rows - 1) / res_rows);
   for (int n_a1 = 1; (long long)n_a1 * res_rows < Tcap + res_rows; ++n_a1) {
-    const long long total = (long long)n_a1 * n_b1;
-    const int G = (int)std::min<long long>(h->units1, total);
-    p1 = std::max<long long>(p1, (long long)col_parts(16) * max_segments(n_a1, n_b1, G) * n_a1 *
-                                     res_rows);
+    // one pass-1 launch (device-input steps) or the chunked launches of a
+    // host-input step: slots per position are the most over the chunks
+    int seg = 0;
+    for (int chunks : {1, step_chunks(n_a1)}) {
+      for (int c = 0; c < chunks; ++c) {
+        const int na = (int)(tile_start(c + 1, n_a1, chunks) - tile_start(c, n_a1, chunks));
+        const long long total = (long long)na * n_b1;
+        const int G = (int)std::min<long long>(h->units1, total);
+        seg = std::max(seg, max_segments(na, n_b1, G));
+      }
+    }
+    p1 = std::max<long long>(p1, (long long)col_parts(16) * seg * n_a1 * res_rows);
   }
   for (int n_b2 = 1; (long long)n_b2 * kBN <= Tcap; ++n_b2) {
     const long long total = (long long)n_a2 * n_b2;
@@ -598,8 +819,16 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
   const bool aug = R >= LCE_AUG_MIN_RANK;
   if (!rc && aug) rc = dalloc(&h->w_aug, (size_t)Vpad * kBK);
   if (!rc && aug) rc = dalloc(&h->h_aug, (size_t)Tcap * kBK);
-  if (!rc && cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess)
+  if (!rc && (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess ||
+              cudaStreamCreateWithFlags(&h->cstream, cudaStreamNonBlocking) != cudaSuccess))
     rc = fail(LORA_CE_ECUDA, "cudaStreamCreate failed");
+  if (!rc && cudaMallocHost(reinterpret_cast<void**>(&h->res_host), 16) != cudaSuccess)
+    rc = fail(LORA_CE_ENOMEM, "cudaMallocHost failed");
+  if (!rc && cudaEventCreateWithFlags(&h->ev_start, cudaEventDisableTiming) != cudaSuccess)
+    rc = fail(LORA_CE_ECUDA, "cudaEventCreate failed");
+  for (int c = 0; c < kMaxChunks && !rc; ++c)
+    if (cudaEventCreateWithFlags(&h->ev_chunk[c], cudaEventDisableTiming) != cudaSuccess)
+      rc = fail(LORA_CE_ECUDA, "cudaEventCreate failed");
   if (!rc && !(make_map(&h->mapW_res, h->W, V, d, kBM) && make_map(&h->mapW_str, h->W, V, d, kBN)))
     rc = fail(LORA_CE_ECUDA, "cuTensorMapEncodeTiled failed for W");
   if (!rc && aug && !(make_map(&h->mapWa_res, h->w_aug, V, kBK, kBM) &&
@@ -611,7 +840,7 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
   }
   if (rc) {
     free_all(h);
-    if (h->stream) cudaStreamDestroy(h->stream);
+    free_streams(h);
     delete h;
     return rc;
   }
@@ -623,11 +852,13 @@ int lora_ce_destroy(lora_ce_handle* h) {
   if (!h) return 0;
   cudaSetDevice(h->cfg.device);
   if (h->stream) cudaStreamSynchronize(h->stream);
+  if (h->cstream) cudaStreamSynchronize(h->cstream);
+  drop_graphs(h);  // graphs holding NCCL calls go before the communicator
   if (h->comm) nccl().CommDestroy(h->comm);
   for (cudaEvent_t e : h->ev)
     if (e) cudaEventDestroy(e);
   free_all(h);
-  if (h->stream) cudaStreamDestroy(h->stream);
+  free_streams(h);
   delete h;
   return 0;
 }
@@ -688,6 +919,7 @@ int lora_ce_set_adapter(lora_ce_handle* h, const float* A, const float* B, int32
 
 int lora_ce_set_scale(lora_ce_handle* h, float scale) {
   if (!h || !std::isfinite(scale)) return fail(LORA_CE_EINVAL, "bad argument");
+  if (scale != h->cfg.scale) drop_graphs(h);  // captured steps carry the scale
   h->cfg.scale = scale;
   return 0;
 }
@@ -750,12 +982,13 @@ int lora_ce_get_token_loss(lora_ce_handle* h, float* loss_t, int32_t T) {
   return 0;
 }
 
+
 int lora_ce_step_device(lora_ce_handle* h, const void* dH, int32_t dtype, int32_t T,
                         const int32_t* dtg, float* d_loss) {
   int rc = check_step_args(h, dH, dtype, T, dtg);
   if (rc) return rc;
   LCE_CUDA(cudaSetDevice(h->cfg.device));
-  rc = dispatch_step(h, dH, dtype, T, dtg, d_loss ? d_loss : h->d_loss);
+  rc = run_or_replay(h, false, dH, dtype, T, dtg, d_loss ? d_loss : h->d_loss);
   if (rc) h->poisoned = true;
   return rc;
 }
@@ -765,18 +998,14 @@ int lora_ce_step(lora_ce_handle* h, const void* H, int32_t dtype, int32_t T,
   int rc = check_step_args(h, H, dtype, T, targets);
   if (rc) return rc;
   LCE_CUDA(cudaSetDevice(h->cfg.device));
-  LCE_CUDA(cudaMemcpyAsync(h->in_H, H, (size_t)T * h->d * elt_size(dtype), cudaMemcpyHostToDevice,
-                           h->stream));
-  LCE_CUDA(cudaMemcpyAsync(h->in_tgt, targets, (size_t)T * 4, cudaMemcpyHostToDevice, h->stream));
-  rc = dispatch_step(h, h->in_H, dtype, T, h->in_tgt, h->d_loss);
+  rc = run_or_replay(h, true, H, dtype, T, targets, nullptr);
   if (rc) {
     h->poisoned = true;
     return rc;
   }
-  LCE_CUDA(cudaMemcpyAsync(h->d_loss + 1, h->err, 4, cudaMemcpyDeviceToDevice, h->stream));
-  float res[2];
-  LCE_CUDA(cudaMemcpyAsync(res, h->d_loss, 8, cudaMemcpyDeviceToHost, h->stream));
   LCE_CUDA(cudaStreamSynchronize(h->stream));
+  float res[2];
+  memcpy(res, h->res_host, 8);
   int e;
   memcpy(&e, &res[1], 4);
   if (e != 0) {
@@ -813,6 +1042,7 @@ int lora_ce_comm_init(lora_ce_handle* h, int32_t nranks, int32_t rank, const voi
   if (!nccl().ok) return fail(LORA_CE_ENCCL, "libnccl.so.2 could not be loaded");
   ncclUniqueId id;
   memcpy(&id, id128, 128);
+  drop_graphs(h);  // steps captured without the all-reduce
   if (nccl().CommInitRank(&h->comm, nranks, id, rank) != ncclSuccess)
     return fail(LORA_CE_ENCCL, "ncclCommInitRank failed");
   h->nranks = nranks;

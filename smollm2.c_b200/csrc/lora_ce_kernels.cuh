@@ -104,6 +104,7 @@ struct GemmArgs {
   int n_a, n_b;      // resident-tile count, streamed-tile count
   int kblocks;       // K-blocks per tile: kmain, plus one rank block when augmented
   int kmain;         // d / 64 K-blocks of h / W
+  int a0;            // first resident block of this launch (pass 1 runs per chunk of positions)
   int T, V, R;
   long long Tcap;    // partial-buffer row stride (positions)
   long long Vpad;    // rows of Bt / gBp
@@ -523,7 +524,7 @@ __global__ void __launch_bounds__(block_threads(Epi::kWarps), 1)
           }
           if (leader)
             mbar_expect_tx(&bars[kBarAFull], (uint32_t)(kPair * g.kblocks * kAKBytes));
-          const int row0 = a * kResRows + (int)rank * kBM;
+          const int row0 = (g.a0 + a) * kResRows + (int)rank * kBM;
           for (int kb = 0; kb < g.kblocks; ++kb) {
             // K-blocks past kmain come from the rank-augmentation map, at x = 0
             const CUtensorMap* m = kb < g.kmain ? &map_res : &map_res_aug;
@@ -651,7 +652,7 @@ __global__ void __launch_bounds__(block_threads(Epi::kWarps), 1)
       if (a != cur_a) {
         if (cur_a >= 0 && !failed)
           epi.flush(g, kColParts * (unit - tile_owner((long long)cur_a * g.n_b, total, G)) + half);
-        epi.begin(g, a * kResRows + (int)rank * kBM + row);
+        epi.begin(g, (g.a0 + a) * kResRows + (int)rank * kBM + row);
         cur_a = a;
       }
       const int rbuf = (int)(li % kRB);
@@ -746,7 +747,7 @@ __global__ void __launch_bounds__(block_threads(Epi::kWarps), 1)
 // from shared memory are contiguous across lanes.  Positions in [T, Tpad)
 // get an all-zero record with target -1 so pass 2 can read whole tiles.
 template <int R>
-__global__ void lce_prep(const void* __restrict__ H, int dtype, int T, int Tpad, int d,
+__global__ void lce_prep(const void* __restrict__ H, int dtype, int t_lo, int t_hi, int T, int d,
                          const float* __restrict__ A, float scale,
                          const int32_t* __restrict__ targets, int V,
                          __half* __restrict__ h16, float* __restrict__ tok, int* err,
@@ -756,7 +757,7 @@ __global__ void lce_prep(const void* __restrict__ H, int dtype, int T, int Tpad,
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const int nw = (gridDim.x * blockDim.x) >> 5;
-  for (int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < Tpad; w += nw) {
+  for (int w = t_lo + ((blockIdx.x * blockDim.x + threadIdx.x) >> 5); w < t_hi; w += nw) {
     if (w >= T) {  // padding position: all fields zero, target -1
       for (int f = lane; f < tok_stride(R); f += 32)
         tok[tidx(w, f, R)] = f == R + 2 ? __int_as_float(-1) : 0.f;
@@ -850,7 +851,8 @@ __global__ void lce_aug_b(const float* __restrict__ Bt, long long Vpad, __half* 
 // (the reference's d_mid, src/train.c:161-168).  The record of t gets
 // M*log2(e) and 1/S for pass 2.
 template <int R>
-__global__ void lce_combine(int T, int cparts, int res_rows, int n_b1, int G1, long long Tcap,
+__global__ void lce_combine(int T, int cparts, int res_rows, int n_b1, int units1, int chunks,
+                            long long Tcap,
                             const float* __restrict__ p_max,
                             const float* __restrict__ p_sum, const float* __restrict__ p_q,
                             const float* __restrict__ z_tgt, const float* __restrict__ Bt,
@@ -860,8 +862,16 @@ __global__ void lce_combine(int T, int cparts, int res_rows, int n_b1, int G1, l
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
-  const int a = t / res_rows;
-  const long long total = (long long)((T + res_rows - 1) / res_rows) * n_b1;
+  // Pass 1 ran as `chunks` launches over even splits of the n_a position
+  // blocks (chunk c: blocks [start(c), start(c+1))), each with its own tile
+  // ranges over min(units1, tiles of the chunk) owners.
+  const int n_a = (T + res_rows - 1) / res_rows;
+  const int ab = t / res_rows;
+  const int c = tile_owner(ab, n_a, chunks);
+  const int a_lo = (int)tile_start(c, n_a, chunks), a_hi = (int)tile_start(c + 1, n_a, chunks);
+  const int a = ab - a_lo;
+  const long long total = (long long)(a_hi - a_lo) * n_b1;
+  const int G1 = (int)(total < units1 ? total : units1);
   const int s0 = tile_owner((long long)a * n_b1, total, G1);
   const int s1 = tile_owner((long long)a * n_b1 + n_b1 - 1, total, G1);
   const int nslot = cparts * (s1 - s0 + 1);

@@ -233,7 +233,7 @@ extern "C" int lora_ce_token_loss_noalloc(const uint16_t* d_W, int32_t vocab, in
   if ((reinterpret_cast<uintptr_t>(d_H) & 15) != 0)
     return na_fail(LORA_CE_EINVAL, "hidden states must be 16-byte aligned");
   lce_prep<R><<<(int)std::min<long long>((Tpad + 7) / 8, 592), 256, (size_t)d * R * 4, st>>>(
-      d_H, h_dtype, T, (int)Tpad, d, s->params, scale, d_targets, V, s->h16, s->tok, s->err,
+      d_H, h_dtype, 0, (int)Tpad, T, d, s->params, scale, d_targets, V, s->h16, s->tok, s->err,
       nullptr);
   GemmArgs g{};
   g.kblocks = kblocks;
@@ -275,7 +275,8 @@ extern "C" int lora_ce_token_loss_noalloc(const uint16_t* d_W, int32_t vocab, in
     if (cudaLaunchKernelEx(&lc, kern, mapH, mapW, mapH, mapW, g) != cudaSuccess)
       return na_fail(LORA_CE_ECUDA, "pass-1 launch failed");
   }
-  lce_combine<R><<<(T + 7) / 8, 256, 0, st>>>(T, cp1, res_rows, n_b1, G1, stride1, s->pmax,
+  lce_combine<R><<<(T + 7) / 8, 256, 0, st>>>(T, cp1, res_rows, n_b1, s->units, 1, stride1,
+                                                  s->pmax,
                                                   s->psum, s->pq, s->ztgt, Bp, scale, s->tok,
                                                   s->dU, d_loss);
   na_poison<<<(T + 255) / 256, 256, 0, st>>>(s->err, d_loss, T);

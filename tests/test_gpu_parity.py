@@ -291,3 +291,76 @@ def test_q4k_step_matches_oracle(oracle):
     for name, a, b in (("dA", gA, ref["gA"]), ("dB", gB, ref["gB"]), ("A", A1, ref["A"]),
                        ("B", B1, ref["B"])):
         assert rel(a, b) <= L2_RTOL, (name, rel(a, b))
+
+
+def test_chunked_host_step_matches_device_step():
+    """lora_ce_step copies h in chunks and runs pass 1 per chunk (T 8192: four
+    launches); lora_ce_step_device runs it as one launch.  The two differ
+    only in how the pass-1 partials are grouped: 1e-5 apart."""
+    import torch
+    V, d, r, T = 49152, 576, 4, 8192
+    W, H, _, tgt, A, B = make(V, d, r, T, 55)
+    outs = []
+    for mode in ("host", "device"):
+        m = lora_ce.LoraCE(lora_ce.default_config(d, V, r, T, scale=2.0, lr=1e-3))
+        m.set_weight(W)
+        m.set_adapter(A, B, 0)
+        if mode == "host":
+            loss = m.step(H, tgt)
+        else:
+            dH = torch.from_numpy(H.view(np.int16)).cuda()
+            dT = torch.from_numpy(tgt).cuda()
+            dL = torch.zeros(2, dtype=torch.float32, device="cuda")
+            m.step_device(dH.data_ptr(), lora_ce.BF16, T, dT.data_ptr(), dL.data_ptr())
+            m.sync()
+            loss = float(dL[0].item())
+        gA, gB, _, n = m.get_grads()
+        A1, B1, _ = m.get_adapter()
+        outs.append((loss, gA, gB, A1, B1))
+        m.close()
+    (l0, *a0), (l1, *a1) = outs
+    assert abs(l0 - l1) <= 1e-5 * abs(l1)
+    for x, y in zip(a0, a1):
+        assert rel(x, y) <= 1e-5
+
+
+def test_graph_replay_reads_current_inputs(oracle):
+    """Steps are CUDA-graph replays once (T, dtype, buffers) repeat: a replay
+    must copy the buffers' current contents and apply this step's Adam bias
+    corrections.  Three steps with new data in the same host buffers, with
+    graphs on and off."""
+    V, d, r, T = 8192, 576, 4, 512
+    W = wl.make_weight(70, V, d)
+    _, _, A, B = wl.make_step_inputs(70, T, V, d, r)
+    batches = [wl.make_step_inputs(71 + k, T, V, d, r)[:2] for k in range(3)]
+    results = []
+    for graphs in ("1", "0"):
+        os.environ["LORA_CE_GRAPHS"] = graphs
+        try:
+            m = lora_ce.LoraCE(lora_ce.default_config(d, V, r, T, scale=2.0, lr=1e-3))
+        finally:
+            os.environ.pop("LORA_CE_GRAPHS", None)
+        m.set_weight(W)
+        m.set_adapter(A, B, 0)
+        H = np.empty_like(batches[0][0])
+        tg = np.empty_like(batches[0][1])
+        losses = []
+        for h, t in batches:
+            H[...] = h
+            tg[...] = t
+            losses.append(m.step(H, tg))
+        A1, B1, step = m.get_adapter()
+        assert step == 3
+        results.append((losses, A1, B1))
+        m.close()
+    (l_g, A_g, B_g), (l_d, A_d, B_d) = results
+    np.testing.assert_array_equal(np.float32(l_g), np.float32(l_d))
+    np.testing.assert_array_equal(A_g, A_d)
+    np.testing.assert_array_equal(B_g, B_d)
+    # and the losses follow the oracle step by step
+    state, Ao, Bo = None, A, B
+    for (h, t), lg in zip(batches, l_g):
+        ref = oracle.step(W, Ao, Bo, wl.oracle_hidden(h), t, 2.0, 1e-3, nthreads=NTHREADS,
+                          state=state)
+        state, Ao, Bo = ref["state"], ref["A"], ref["B"]
+        assert abs(lg - ref["loss"]) <= LOSS_RTOL * ref["loss"]
