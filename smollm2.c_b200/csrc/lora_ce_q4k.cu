@@ -5,7 +5,7 @@
 //   y = (d * sc) * q - (dmin * m), each product and the difference rounded
 //   separately (ggml's scalar order without contraction)
 // HBM-bound: 144 bytes in and 512 (f16) or 1024 (f32) bytes out per block.
-// One warp per block; lane l produces weights 8l .. 8l+7 (run c = l / 8 of
+// Lane l of a block's warp produces weights 8l .. 8l+7 (run c = l / 8 of
 // 64, low nibbles for the first 32 of a run, high nibbles for the second)
 // from one 8-byte quant load and the block's 16-byte header, which all
 // lanes read (a broadcast), and writes them with 16- or 32-byte stores.
@@ -26,58 +26,79 @@ int q4k_fail(int code, const char* msg) {
   return code;
 }
 
-__device__ __forceinline__ uint32_t byte_of(const uint4& v, int i) {
-  const uint32_t w = i < 4 ? v.x : i < 8 ? v.y : i < 12 ? v.z : v.w;
-  return (w >> (8 * (i & 3))) & 0xffu;
-}
-
+// One warp per block; lane l makes weights 8l .. 8l+7 of the block.
+// * Decoding: each quant nibble q becomes the f32 with bits 0x4B0000qq,
+//   2^23 + q, by one byte permute, and subtracting 2^23 is exact. The
+//   6-bit (scale, min) pair of sub-block j comes from the three 32-bit
+//   words of scales[] with one shift by 8 * (j % 4).
+// * Arithmetic: (d * sc) * q - dmin * m, each step rounded separately, as
+//   written above.
 template <bool kF16>
 __global__ void __launch_bounds__(256) lce_q4k_dequant(const uint8_t* __restrict__ blocks,
                                                         long long n_blocks, void* __restrict__ out) {
   const int lane = threadIdx.x & 31;
   const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-  for (long long b = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); b < n_blocks;
-       b += warps) {
-    const uint8_t* blk = blocks + b * 144;
-    const uint4 hdr = *reinterpret_cast<const uint4*>(blk);  // d, dmin, scales[12]
-    const int c = lane >> 3;                   // run of 64
-    const int hi = (lane >> 2) & 1;            // high nibbles: second 32 of the run
-    const int o = (lane & 3) * 8;              // offset in the run's 32 quant bytes
-    const int j = 2 * c + hi;                  // sub-block
-    const uint2 qv = *reinterpret_cast<const uint2*>(blk + 16 + 32 * c + o);
-    // scales[k] is header byte 4 + k
-    int sc, m;
+  const int c = lane >> 3;          // run of 64
+  const int hi = (lane >> 2) & 1;   // high nibbles: second 32 of the run
+  const int o = (lane & 3) * 8;     // offset in the run's 32 quant bytes
+  const int j = 2 * c + hi;         // sub-block
+  const int sh = 8 * (j & 3);
+  // two blocks per iteration: both blocks' loads are in flight before either
+  // is decoded
+  auto decode = [&](long long b, const uint4& hdr, const uint2& qv) {
+    const uint32_t s0 = hdr.y >> sh, s1 = hdr.z >> sh, s2 = hdr.w >> sh;  // scales[k], [k+4], [k+8]
+    uint32_t sc, m;
     if (j < 4) {
-      sc = byte_of(hdr, 4 + j) & 63;
-      m = byte_of(hdr, 8 + j) & 63;
+      sc = s0 & 63u;
+      m = s1 & 63u;
     } else {
-      sc = (byte_of(hdr, 8 + j) & 15) | ((byte_of(hdr, j) >> 6) << 4);
-      m = (byte_of(hdr, 8 + j) >> 4) | ((byte_of(hdr, 4 + j) >> 6) << 4);
+      sc = (s2 & 15u) | ((s0 & 0xC0u) >> 2);
+      m = ((s2 >> 4) & 15u) | ((s1 & 0xC0u) >> 2);
     }
     const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xffffu)));
     const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
     const float dsc = __fmul_rn(d, (float)sc);
     const float mm = __fmul_rn(dmin, (float)m);
+    // the eight nibbles as bytes 0..7 of n0, n1
+    const uint32_t n0 = hi ? (qv.x >> 4) & 0x0F0F0F0Fu : qv.x & 0x0F0F0F0Fu;
+    const uint32_t n1 = hi ? (qv.y >> 4) & 0x0F0F0F0Fu : qv.y & 0x0F0F0F0Fu;
     float y[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      const uint32_t byte = ((e < 4 ? qv.x : qv.y) >> (8 * (e & 3))) & 0xffu;
-      const uint32_t q = hi ? (byte >> 4) : (byte & 15u);
-      y[e] = __fsub_rn(__fmul_rn(dsc, (float)q), mm);
+      // bits 0x4B0000qq: byte e%4 of the nibble word, then 00 00 4B
+      const uint32_t bits = __byte_perm(e < 4 ? n0 : n1, 0x4B000000u, (e & 3) | 0x7540u);
+      const float q = __fsub_rn(__uint_as_float(bits), 8388608.0f);  // exact
+      y[e] = __fsub_rn(__fmul_rn(dsc, q), mm);
     }
     const long long w0 = b * 256 + 64 * c + 32 * hi + o;
     if constexpr (kF16) {
       uint32_t p[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k)
-        p[k] = (uint32_t)__half_as_ushort(__float2half_rn(y[2 * k])) |
-               ((uint32_t)__half_as_ushort(__float2half_rn(y[2 * k + 1])) << 16);
+      for (int k = 0; k < 4; ++k) {  // two round-to-nearest conversions per instruction
+        const __half2 v = __float22half2_rn(make_float2(y[2 * k], y[2 * k + 1]));
+        p[k] = *reinterpret_cast<const uint32_t*>(&v);
+      }
       *reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + w0) = make_uint4(p[0], p[1], p[2], p[3]);
     } else {
       float4* dst = reinterpret_cast<float4*>(static_cast<float*>(out) + w0);
       dst[0] = make_float4(y[0], y[1], y[2], y[3]);
       dst[1] = make_float4(y[4], y[5], y[6], y[7]);
     }
+  };
+  auto qoff = [&](long long b) { return blocks + b * 144 + 16 + 32 * c + o; };
+  for (long long b = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); b < n_blocks;
+       b += 2 * warps) {
+    const long long b2 = b + warps;
+    const uint4 h1 = *reinterpret_cast<const uint4*>(blocks + b * 144);  // d, dmin | scales
+    const uint2 q1 = *reinterpret_cast<const uint2*>(qoff(b));
+    uint4 h2 = make_uint4(0, 0, 0, 0);
+    uint2 q2 = make_uint2(0, 0);
+    if (b2 < n_blocks) {
+      h2 = *reinterpret_cast<const uint4*>(blocks + b2 * 144);
+      q2 = *reinterpret_cast<const uint2*>(qoff(b2));
+    }
+    decode(b, h1, q1);
+    if (b2 < n_blocks) decode(b2, h2, q2);
   }
 }
 

@@ -79,6 +79,7 @@ def run_case(oracle, V, d, r, T, seed, dtype="bf16", steps=1, scale=2.0, lr=1e-3
         (3000, 128, 1, 77, "bf16"),     # ranks padded to the kernels' 4 / 8 / 16
         (3000, 192, 3, 40, "f16"),
         (2048, 576, 13, 100, "bf16"),
+        (49152, 576, 16, 700, "bf16"),  # rank augmentation at full vocabulary
     ],
 )
 def test_step_matches_oracle(oracle, V, d, r, T, dtype):
