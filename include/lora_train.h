@@ -22,8 +22,11 @@ extern "C" {
  * succeeded once. */
 int lora_train_set_lm_head(train_state* t, const uint16_t* w_f16);
 
-/* Same, taking token_embd.weight (F16, dims {dim, vocab}) from a loaded
- * model: the call cmd_train adds after train_create (src/studio.c:234). */
+/* Same, taking token_embd.weight (dims {dim, vocab}) from a loaded model:
+ * the call cmd_train adds after train_create (src/studio.c:234).  F16, or
+ * Q4_K (GGUF type 12, super-blocks over the flattened tensor) for QLoRA,
+ * which is dequantised once on the GPU; the reference itself refuses
+ * QLoRA (src/studio.c:187-191). */
 int lora_train_set_lm_head_gguf(train_state* t, const gguf_ctx* g);
 
 #ifdef __cplusplus

@@ -24,6 +24,11 @@
  *   LORA_CE_DEVICE        CUDA device ordinal (default 0)
  *   LORA_CE_WEIGHT_DECAY  decoupled weight decay (default 0: the reference's Adam)
  *   LORA_CE_CLIP_NORM     global gradient-norm clip (default 0: off)
+ *   LORA_TRAIN_PACK       "1": train_run packs train_params.batch samples into
+ *                         each step (one Adam update over all their predicted
+ *                         positions).  The reference parses --batch but trains
+ *                         one sample per step (src/train.c:340-351); that stays
+ *                         the default.
  */
 #include "train.h"
 #include "gguf.h"
@@ -54,9 +59,10 @@ struct train_state {
     float last_loss;
     lora_ce_handle* gpu;
     int have_weight;
-    int max_pred;     /* positions one step can hold: seq_max - 1 */
-    float* H;         /* [max_pred][dim] hidden rows of the current sample */
-    int32_t* targets; /* [max_pred] */
+    int max_pred;     /* positions of one sample: seq_max - 1 */
+    int pack;         /* samples per step in train_run (1 unless LORA_TRAIN_PACK) */
+    float* H;         /* [pack * max_pred][dim] hidden rows of the current step */
+    int32_t* targets; /* [pack * max_pred] */
     float* logits;    /* [vocab]: the body forward writes base logits here */
 };
 
@@ -97,9 +103,10 @@ train_state* train_create(forward_ctx* f, const train_params* p) {
     const int alpha = p->lora_alpha > 0 ? p->lora_alpha : 2 * t->rank;
     t->scale = (float)alpha / (float)t->rank;
     t->max_pred = p->seq_max > 1 ? p->seq_max - 1 : 1;
+    t->pack = (env_double("LORA_TRAIN_PACK", 0.0) != 0.0 && p->batch > 1) ? p->batch : 1;
 
     lora_ce_config cfg;
-    lora_ce_default_config(&cfg, t->dim, t->vocab, t->rank, t->max_pred);
+    lora_ce_default_config(&cfg, t->dim, t->vocab, t->rank, t->max_pred * t->pack);
     cfg.scale = t->scale;
     cfg.lr = p->lr;
     cfg.weight_decay = (float)env_double("LORA_CE_WEIGHT_DECAY", 0.0);
@@ -115,8 +122,8 @@ train_state* train_create(forward_ctx* f, const train_params* p) {
     const size_t na = (size_t)t->dim * t->rank, nb = (size_t)t->rank * t->vocab;
     float* A = malloc(na * sizeof(float));
     float* B = calloc(nb, sizeof(float));
-    t->H = malloc((size_t)t->max_pred * t->dim * sizeof(float));
-    t->targets = malloc((size_t)t->max_pred * sizeof(int32_t));
+    t->H = malloc((size_t)t->pack * t->max_pred * t->dim * sizeof(float));
+    t->targets = malloc((size_t)t->pack * t->max_pred * sizeof(int32_t));
     t->logits = malloc((size_t)t->vocab * sizeof(float));
     if (!A || !B || !t->H || !t->targets || !t->logits) {
         free(A);
@@ -159,50 +166,77 @@ int lora_train_set_lm_head(train_state* t, const uint16_t* w_f16) {
 int lora_train_set_lm_head_gguf(train_state* t, const gguf_ctx* g) {
     if (!t || !g) return -1;
     const gguf_tensor_info* ti = gguf_tensor_get(g, "token_embd.weight");
-    if (!ti || ti->dtype != GGUF_DT_F16 || (int)ti->dims[0] != t->dim ||
-        (int)ti->dims[1] != t->vocab) {
-        fprintf(stderr, "lora_train: no F16 token_embd.weight of [%d x %d] in the model\n",
+    const int shape_ok = ti && (int)ti->dims[0] == t->dim && (int)ti->dims[1] == t->vocab;
+    if (!shape_ok || (ti->dtype != GGUF_DT_F16 && ti->dtype != GGUF_DT_Q4_K)) {
+        fprintf(stderr,
+                "lora_train: no F16 or Q4_K token_embd.weight of [%d x %d] in the model\n",
                 t->vocab, t->dim);
         return -1;
     }
-    return lora_train_set_lm_head(t, (const uint16_t*)gguf_tensor_data(g, ti));
+    const void* data = gguf_tensor_data(g, ti);
+    if (ti->dtype == GGUF_DT_F16) return lora_train_set_lm_head(t, (const uint16_t*)data);
+    /* QLoRA: Q4_K super-blocks over the flattened tensor, dequantised once
+     * on the GPU into the f16 operand of the step */
+    const int rc = lora_ce_set_weight_q4k(t->gpu, data);
+    if (rc != LORA_CE_OK) {
+        report("lora_train_set_lm_head_gguf", rc);
+        return -1;
+    }
+    t->have_weight = 1;
+    return 0;
 }
 
-/* src/train.c:198-242: predicted positions 0 .. use_n-2 with
- * use_n = min(n_tokens, seq_max), position pos predicting tokens[pos+1];
- * the mean loss, or -1.0f on any failure. */
-float train_step(train_state* t, const int* tokens, int n_tokens) {
-    if (!t || !tokens || n_tokens < 2) return -1.0f;
+/* The predicted positions of one sample (src/train.c:198-229): positions
+ * 0 .. use_n-2 with use_n = min(n_tokens, seq_max), position pos predicting
+ * tokens[pos+1], hidden rows from one prefill and use_n-2 decodes of the
+ * body forward, stored from row `at` of the step buffers.  Returns the
+ * number of positions, or -1. */
+static int gather_sample(train_state* t, const int* tokens, int n_tokens, int at) {
+    if (!tokens || n_tokens < 2) return -1;
     const int use_n = n_tokens < t->p.seq_max ? n_tokens : t->p.seq_max;
-    if (use_n < 2) return -1.0f;
-    if (!t->have_weight) {
-        fprintf(stderr, "train_step: lm_head weight not set (lora_train_set_lm_head)\n");
-        return -1.0f;
-    }
+    if (use_n < 2) return -1;
     const int n_pred = use_n - 1;
     for (int pos = 0; pos < n_pred; pos++) {
         const int tgt = tokens[pos + 1];
-        if (tgt < 0 || tgt >= t->vocab) return -1.0f;
-        t->targets[pos] = tgt;
+        if (tgt < 0 || tgt >= t->vocab) return -1;
+        t->targets[at + pos] = tgt;
     }
     forward_reset(t->f);
-    if (forward_prefill(t->f, tokens, 1, t->logits) < 0) return -1.0f;
+    if (forward_prefill(t->f, tokens, 1, t->logits) < 0) return -1;
     for (int pos = 0; pos < n_pred; pos++) {
         const float* h = forward_last_hidden(t->f);
-        if (!h) return -1.0f;
-        memcpy(t->H + (size_t)pos * t->dim, h, (size_t)t->dim * sizeof(float));
+        if (!h) return -1;
+        memcpy(t->H + (size_t)(at + pos) * t->dim, h, (size_t)t->dim * sizeof(float));
         if (pos + 1 < n_pred && forward_decode(t->f, tokens[pos + 1], pos + 1, t->logits) < 0)
-            return -1.0f;
+            return -1;
     }
+    return n_pred;
+}
+
+/* One GPU step over the n gathered positions: the mean loss, or -1.0f. */
+static float step_positions(train_state* t, int n, const char* where) {
     float loss = -1.0f;
-    const int rc = lora_ce_step(t->gpu, t->H, LORA_CE_F32, n_pred, t->targets, &loss);
+    const int rc = lora_ce_step(t->gpu, t->H, LORA_CE_F32, n, t->targets, &loss);
     if (rc != LORA_CE_OK) {
-        report("train_step", rc);
+        report(where, rc);
         return -1.0f;
     }
     t->step++;
     t->last_loss = loss;
     return loss;
+}
+
+/* src/train.c:198-242: the mean loss over the sample's predicted positions,
+ * or -1.0f on any failure. */
+float train_step(train_state* t, const int* tokens, int n_tokens) {
+    if (!t || !tokens || n_tokens < 2) return -1.0f;
+    if (!t->have_weight) {
+        fprintf(stderr, "train_step: lm_head weight not set (lora_train_set_lm_head)\n");
+        return -1.0f;
+    }
+    const int n = gather_sample(t, tokens, n_tokens, 0);
+    if (n < 1) return -1.0f;
+    return step_positions(t, n, "train_step");
 }
 
 /* LORA0001 (src/train.c:244-258): magic, int32 {dim, vocab, rank, step},
@@ -356,15 +390,34 @@ int train_run(train_state* t, const char* packed_path, const train_params* p,
     char path[1024];
     int step = 0;
     float first_loss = -1.0f;
+    /* packing (LORA_TRAIN_PACK): samples gathered for the next step */
+    int packed = 0, packed_pos = 0, packed_first = 0;
+    const int last_epoch = p->epochs - 1;
     for (int epoch = 0; epoch < p->epochs && step < max_steps; epoch++) {
         for (int s = 0; s < ps.n && step < max_steps; s++) {
             const int n = packed_read(&ps, s, tokens, kSampleCap);
-            if (n < 2) continue;
-            const float loss = train_step(t, tokens, n);
+            const int final_sample = epoch == last_epoch && s == ps.n - 1;
+            float loss = -1.0f;
+            int sample = s;
+            if (t->pack == 1) {
+                if (n < 2) continue;
+                loss = train_step(t, tokens, n);
+            } else {
+                const int k = (n >= 2 && t->have_weight) ? gather_sample(t, tokens, n, packed_pos) : -1;
+                if (k > 0) {
+                    if (packed == 0) packed_first = s;
+                    packed_pos += k;
+                    ++packed;
+                }
+                if (packed == 0 || (packed < t->pack && !final_sample)) continue;
+                loss = step_positions(t, packed_pos, "train_run");
+                sample = packed_first;
+                packed = packed_pos = 0;
+            }
             if (loss < 0) continue;
             if (first_loss < 0) first_loss = loss;
             step++;
-            printf("step=%d epoch=%d sample=%d loss=%.4f\n", step, epoch, s, loss);
+            printf("step=%d epoch=%d sample=%d loss=%.4f\n", step, epoch, sample, loss);
             fflush(stdout);
 
             /* memory watchdog (src/train.c:354-368) */

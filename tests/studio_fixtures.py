@@ -138,6 +138,6 @@ class TrainerEnv:
 
 
 def params(rank=4, alpha=8, seq_max=256, lr=1e-3, epochs=1, checkpoint_every=0, max_steps=0,
-           seed=42, simulate_mem_kb=0) -> TrainParams:
-    return TrainParams(0, rank, alpha, seq_max, 1, lr, epochs, checkpoint_every, max_steps, seed,
-                       simulate_mem_kb)
+           seed=42, simulate_mem_kb=0, batch=1) -> TrainParams:
+    return TrainParams(0, rank, alpha, seq_max, batch, lr, epochs, checkpoint_every, max_steps,
+                       seed, simulate_mem_kb)

@@ -291,3 +291,70 @@ def test_lm_head_from_gguf(env, tmp_path):
     env.env.env_gguf_close(g)
     env.env.env_gguf_close(g2)
     env.env.env_forward_free(f)
+
+
+@pytest.mark.gpu
+def test_qlora_lm_head_from_gguf(env, oracle, tmp_path):
+    """A Q4_K token_embd.weight in the model file (QLoRA): dequantised on
+    the GPU, the step matches the oracle on the dequantised f16 weight."""
+    d, V, r, n = 576, 4096, 8, 64
+    blocks = wl.make_weight_q4k(13, V, d)
+    W16 = oracle.q4k_dequant(blocks).astype(np.float16).view(np.uint16).reshape(V, d)
+    h, tgt, _, _ = wl.make_step_inputs(13, n - 1, V, d, r)
+    H = np.ascontiguousarray(wl.oracle_hidden(h))
+    tokens = np.concatenate([[1], tgt]).astype(np.int32)
+    p = str(tmp_path / "q.gguf")
+    sf.write_gguf(p, [("token_embd.weight", [d, V], 12, blocks.tobytes())])
+    g = env.env.env_gguf_open(p.encode())
+    assert g
+    f = env.forward(H, V)
+    t = env.lib.train_create(f, sf.params(rank=r, alpha=16, seq_max=n, seed=42))
+    assert env.lib.lora_train_set_lm_head_gguf(t, g) == 0
+    loss = env.lib.train_step(t, tokens.ctypes.data, n)
+    A0 = oracle.kaiming_init(42, d, r)
+    ref = oracle.train_step_tokens(W16, A0, np.zeros((r, V), np.float32), H, tokens, n, 2.0, 1e-4)
+    assert abs(loss - ref["loss"]) <= 1e-4 * ref["loss"]
+    env.lib.train_free(t)
+    env.env.env_gguf_close(g)
+    env.env.env_forward_free(f)
+
+
+@pytest.mark.gpu
+def test_train_run_packs_samples_when_asked(env, oracle, tmp_path, capfd):
+    """LORA_TRAIN_PACK=1 with batch 3: train_run makes one step per three
+    usable samples (the last step takes what is left), each step one Adam
+    update over all their predicted positions, checked against the oracle
+    on the concatenated positions.  Without it, one sample per step."""
+    d, V = 128, 3000
+    W, H, samples = _run_inputs(d=d, V=V)  # lengths 64, 1, 40, 64, 30
+    packed = str(tmp_path / "data.bin")
+    sf.write_packed(packed, samples)
+    f = env.forward(H, V)
+    p = sf.params(rank=4, alpha=8, seq_max=64, lr=1e-3, batch=3, seed=42)
+    os.environ["LORA_TRAIN_PACK"] = "1"
+    try:
+        t = env.lib.train_create(f, p)
+    finally:
+        os.environ.pop("LORA_TRAIN_PACK", None)
+    assert env.lib.lora_train_set_lm_head(t, W.ctypes.data) == 0
+    out = str(tmp_path / "out")
+    assert env.lib.train_run(t, packed.encode(), p, out.encode()) == 0
+    env.flush()
+    lines = capfd.readouterr().out.strip().splitlines()
+    steps = [STEP_RE.match(x).groups() for x in lines if x.startswith("step=")]
+    assert [(int(a), int(c)) for a, _, c, _ in steps] == [(1, 0), (2, 4)]
+    # the oracle on the same positions: rows 0..n-2 of H for each sample
+    groups = [[0, 2, 3], [4]]
+    state, A, B = None, oracle.kaiming_init(42, d, 4), np.zeros((4, V), np.float32)
+    for (_, _, _, loss), grp in zip(steps, groups):
+        Hs = np.concatenate([H[:len(samples[i]) - 1] for i in grp])
+        tg = np.concatenate([np.asarray(samples[i][1:], np.int32) for i in grp])
+        ref = oracle.step(W, A, B, Hs, tg, 2.0, 1e-3, state=state)
+        state, A, B = ref["state"], ref["A"], ref["B"]
+        assert abs(float(loss) - ref["loss"]) <= 1e-4 * ref["loss"] + 1e-4
+    A1, B1, s1, _ = _read_adapter(os.path.join(out, "lora_final.bin"), d, V, 4)
+    assert s1 == 2
+    for a, b in ((A1, A), (B1, B)):
+        assert np.linalg.norm(a - b) <= 1e-3 * np.linalg.norm(b)
+    env.lib.train_free(t)
+    env.env.env_forward_free(f)
