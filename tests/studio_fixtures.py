@@ -26,7 +26,7 @@ ENV_SO = os.path.join(REPO, "oracle", "_ref", "libstudio_env.so")
 TRAIN_SO = os.path.join(REPO, "smollm2.c_b200", "liblora_train.so")
 
 GGUF_F32, GGUF_F16 = 0, 1
-GGUF_V_UINT32, GGUF_V_STRING = 4, 8
+GGUF_V_UINT32, GGUF_V_FLOAT32, GGUF_V_STRING, GGUF_V_ARRAY = 4, 6, 8, 9
 
 
 def _gguf_str(s: str) -> bytes:
@@ -36,12 +36,17 @@ def _gguf_str(s: str) -> bytes:
 
 def write_gguf(path: str, tensors, kv=()) -> None:
     """tensors: (name, dims (innermost first), dtype, raw bytes); kv:
-    (key, "u32" | "str", value)."""
+    (key, "u32" | "f32" | "str" | "str_arr", value)."""
     head = struct.pack("<IIQQ", 0x46554747, 3, len(tensors), len(kv))
     for key, typ, val in kv:
         head += _gguf_str(key)
         if typ == "u32":
             head += struct.pack("<II", GGUF_V_UINT32, val)
+        elif typ == "f32":
+            head += struct.pack("<If", GGUF_V_FLOAT32, val)
+        elif typ == "str_arr":
+            head += struct.pack("<IIQ", GGUF_V_ARRAY, GGUF_V_STRING, len(val))
+            head += b"".join(_gguf_str(x) for x in val)
         else:
             head += struct.pack("<I", GGUF_V_STRING) + _gguf_str(val)
     offs, off = [], 0
@@ -141,3 +146,45 @@ def params(rank=4, alpha=8, seq_max=256, lr=1e-3, epochs=1, checkpoint_every=0, 
            seed=42, simulate_mem_kb=0, batch=1) -> TrainParams:
     return TrainParams(0, rank, alpha, seq_max, batch, lr, epochs, checkpoint_every, max_steps,
                        seed, simulate_mem_kb)
+
+
+def write_smollm_gguf(path: str, seed: int, n_layers: int = 2, dim: int = 576, heads: int = 9,
+                      kv_heads: int = 3, ffn: int = 1536, vocab: int = 49152) -> np.ndarray:
+    """A SmolLM2-135M-shaped model file with random weights: the llama
+    metadata and tensor names the reference's forward_load reads
+    (src/forward.c:671-880), f16 matrices ~ N(0, 0.02) from a seed, f32
+    norms of 1.0, RMSNorm eps 1e-5, RoPE theta 1e5, tied embeddings, and a
+    token list of `vocab` placeholder strings.  `n_layers` is 30 in the
+    real model; fewer keep the CPU body quick.  Returns token_embd [V][d]
+    as f16 bits."""
+    rng = np.random.default_rng(seed)
+
+    def f16(*shape):
+        return (rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)).astype(np.float16)
+
+    kv_dim = dim // heads * kv_heads
+    embd = f16(vocab, dim)
+    ones = np.ones(dim, np.float32)
+    tensors = [("token_embd.weight", [dim, vocab], GGUF_F16, embd.tobytes()),
+               ("output_norm.weight", [dim], GGUF_F32, ones.tobytes())]
+    for L in range(n_layers):
+        b = f"blk.{L}."
+        tensors += [(b + "attn_norm.weight", [dim], GGUF_F32, ones.tobytes()),
+                    (b + "attn_q.weight", [dim, dim], GGUF_F16, f16(dim, dim).tobytes()),
+                    (b + "attn_k.weight", [dim, kv_dim], GGUF_F16, f16(kv_dim, dim).tobytes()),
+                    (b + "attn_v.weight", [dim, kv_dim], GGUF_F16, f16(kv_dim, dim).tobytes()),
+                    (b + "attn_output.weight", [dim, dim], GGUF_F16, f16(dim, dim).tobytes()),
+                    (b + "ffn_norm.weight", [dim], GGUF_F32, ones.tobytes()),
+                    (b + "ffn_gate.weight", [dim, ffn], GGUF_F16, f16(ffn, dim).tobytes()),
+                    (b + "ffn_up.weight", [dim, ffn], GGUF_F16, f16(ffn, dim).tobytes()),
+                    (b + "ffn_down.weight", [ffn, dim], GGUF_F16, f16(dim, ffn).tobytes())]
+    kv = [("general.architecture", "str", "llama"),
+          ("llama.embedding_length", "u32", dim), ("llama.block_count", "u32", n_layers),
+          ("llama.attention.head_count", "u32", heads),
+          ("llama.attention.head_count_kv", "u32", kv_heads),
+          ("llama.feed_forward_length", "u32", ffn),
+          ("llama.attention.layer_norm_rms_epsilon", "f32", 1e-5),
+          ("llama.rope.freq_base", "f32", 1e5),
+          ("tokenizer.ggml.tokens", "str_arr", [f"t{i}" for i in range(vocab)])]
+    write_gguf(path, tensors, kv)
+    return embd.view(np.uint16)
