@@ -38,8 +38,9 @@ T_PER_GPU = 8192
 LR, WD = 1e-3, 0.01
 METRIC = "LoRA lm_head CE fwd+bwd tokens/s"
 UNIT = "tokens/s"
-# The workloads (--config): 2 is the default bench line; 3 and 4 are the
-# rank-16 strong-scaling and the Q4_K (QLoRA) lm_head configurations.
+# The workloads (--config): 2 is the default bench line; 3, 4 and 5 are the
+# rank-16 strong-scaling, the Q4_K (QLoRA) lm_head and the rank-64
+# long-context configurations.
 CONFIGS = {
     2: dict(rank=4, alpha=8, tokens=8192, scaling="weak", q4k=False,
             desc="isolated fused LoRA lm_head CE fwd+bwd+AdamW step: h [8192x576] bf16 per GPU, "
@@ -47,6 +48,9 @@ CONFIGS = {
     3: dict(rank=16, alpha=32, tokens=65536, scaling="strong", q4k=False,
             desc="rank 16, 65536 positions split evenly over the GPUs, W [49152x576] f16, "
                  "alpha 32, dA/dB all-reduce before AdamW"),
+    5: dict(rank=64, alpha=128, tokens=65536, scaling="weak", q4k=False, clip=1.0,
+            desc="long-context batch: 32 x 2048 positions per GPU, r 64, alpha 128, W "
+                 "[49152x576] f16, AdamW with grad-clip 1.0"),
     4: dict(rank=8, alpha=16, tokens=32768, scaling="weak", q4k=True,
             desc="QLoRA lm_head: W [49152x576] as Q4_K super-blocks (dequantised once into the "
                  "f16 GEMM operand), r 8, alpha 16, h [32768x576] bf16 per GPU"),
@@ -589,7 +593,7 @@ def main():
     h, tgt, A, B = wl.make_step_inputs(1000 + rank, T, V, D, R)
     _, _, A, B = wl.make_step_inputs(1000, 8, V, D, R)  # same adapter on every rank
     cfg = lora_ce.default_config(D, V, R, T, scale=ALPHA / R, lr=LR, weight_decay=WD,
-                                 device=local)
+                                 clip_norm=CONFIG.get("clip", 0.0), device=local)
     m = lora_ce.LoraCE(cfg)
     if CONFIG["q4k"]:
         m.set_weight_q4k(wl.make_weight_q4k(1, V, D))

@@ -50,8 +50,8 @@ extern "C" {
 typedef struct lora_ce_config {
     int32_t dim;        /* d: hidden size, multiple of 64, <= 640 (576) */
     int32_t vocab;      /* V: vocabulary size (49152) */
-    int32_t rank;       /* r: 1..16 (run at 4, 8 or 16 with zero padding,
-                           which leaves every result unchanged) */
+    int32_t rank;       /* r: 1..64 (run at 4, 8, 16, 32 or 64 with zero
+                           padding, which leaves every result unchanged) */
     float scale;        /* alpha / r (train_create: src/train.c:62-63) */
     float lr;           /* learning rate */
     float beta1;        /* 0.9   (ADAM_B1, src/train.c:23) */

@@ -12,6 +12,7 @@
 #include <cstdio>
 #include <cstring>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 #include "lora_ce.h"
@@ -135,7 +136,7 @@ int step_chunks(int n_a1) { return n_a1 >= 32 ? 4 : n_a1 >= 16 ? 2 : 1; }
 struct lora_ce_handle {
   lora_ce_config cfg{};
   // r: the adapter's rank; R: the rank the kernels run at, r rounded up to
-  // 4, 8 or 16.  The extra columns of A and rows of B are zero and stay
+  // 4, 8, 16, 32 or 64.  The extra columns of A and rows of B are zero and stay
   // zero (their U, dU, dA and dB terms are exactly 0, so Adam leaves them at
   // 0), which makes a rank-r step identical to the reference's.
   int r = 0, R = 0, d = 0, V = 0;
@@ -205,6 +206,10 @@ struct lora_ce_handle {
   // rank augmentation (R >= 8): waug [Vpad][64], haug [Tcap][64] f16
   __half* w_aug = nullptr;
   __half* h_aug = nullptr;
+  // ranks 32, 64: per 16-rank chunk, pass 1's column records (B, rank-16
+  // layout) and pass 2's position records (sU, -M log2 e, 1/S)
+  float* Bc = nullptr;
+  float* tokc = nullptr;
   CUtensorMap mapWa_res{}, mapWa_str{};
   ncclComm_t comm = nullptr;
   int nranks = 1, rank = 0;
@@ -239,9 +244,18 @@ void free_all(lora_ce_handle* h) {
   void* ptrs[] = {h->W,     h->h16,   h->tok,      h->params, h->mom1,  h->mom2,
                   h->Gbuf,  h->gmean, h->p_max,    h->p_sum,  h->p_q,   h->z_tgt,
                   h->loss_tok, h->dU, h->gAp,      h->gBp,    h->norm_parts, h->err, h->corr_fx,
-                  h->d_loss, h->in_H, h->in_tgt, h->w_aug, h->h_aug};
+                  h->d_loss, h->in_H, h->in_tgt, h->w_aug, h->h_aug, h->Bc, h->tokc};
   for (void* p : ptrs)
     if (p) cudaFree(p);
+}
+
+// The rank the kernels run at: the adapter's rank rounded up.
+int kernel_rank(int r) { return r <= 4 ? 4 : r <= 8 ? 8 : r <= 16 ? 16 : r <= 32 ? 32 : 64; }
+
+// The same decisions at run time, for sizing a handle's buffers.
+int aug_width_of(int R) {
+  if (R < LCE_AUG_MIN_RANK) return 0;
+  return R <= 16 ? 64 : (2 * R + 63) / 64 * 64;
 }
 
 int check_cfg(const lora_ce_config* c) {
@@ -249,10 +263,9 @@ int check_cfg(const lora_ce_config* c) {
   if (c->dim < 64 || c->dim % 64 != 0 || c->dim > 64 * kMaxKBlocks)
     return fail(LORA_CE_EINVAL, "dim must be a multiple of 64 in [64, 640]");
   if (c->vocab < 1) return fail(LORA_CE_EINVAL, "vocab must be positive");
-  if (c->rank < 1 || c->rank > 16) return fail(LORA_CE_EINVAL, "rank must be in [1, 16]");
-  const int r_kernel = c->rank <= 4 ? 4 : c->rank <= 8 ? 8 : 16;
-  if (r_kernel >= LCE_AUG_MIN_RANK && c->dim / 64 + 1 > kMaxKBlocks)
-    return fail(LORA_CE_EINVAL, "this rank needs dim <= 576 (one K-block for the rank term)");
+  if (c->rank < 1 || c->rank > 64) return fail(LORA_CE_EINVAL, "rank must be in [1, 64]");
+  if (c->dim / 64 + aug_width_of(kernel_rank(c->rank)) / 64 > kMaxKBlocks)
+    return fail(LORA_CE_EINVAL, "dim too large for this rank (resident K-blocks)");
   if (c->max_tokens < 1) return fail(LORA_CE_EINVAL, "max_tokens must be positive");
   if (!(c->lr >= 0.f) || !(c->eps > 0.f) || !(c->beta1 >= 0.f && c->beta1 < 1.f) ||
       !(c->beta2 >= 0.f && c->beta2 < 1.f) || !(c->weight_decay >= 0.f) ||
@@ -264,7 +277,6 @@ int check_cfg(const lora_ce_config* c) {
 using GemmKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap,
                            const CUtensorMap, const GemmArgs);
 
-// K-blocks of a GEMM tile: d / 64, plus one when the rank term is augmented.
 // Adam's arguments for step `step` (the bias corrections 1 - beta^step are
 // computed on the host with powf, as src/train.c:178-179 does).
 AdamArgs adam_args(const lora_ce_handle* h, long long nparam, int32_t step) {
@@ -284,20 +296,60 @@ AdamArgs adam_args(const lora_ce_handle* h, long long nparam, int32_t step) {
   return aa;
 }
 
-template <class Epi>
-int tile_kblocks(int d) {
-  return d / kBK + (Epi::kAug ? 1 : 0);
-}
+
+// Everything a kernel rank decides.  Ranks up to 16 run each pass once;
+// ranks 32 and 64 run each pass once per chunk of 16 ranks (the epilogue's
+// accumulators for 16 ranks are what fits in registers), with the full-rank
+// logit term in the MMA either way.
+//   augmentation layout 0: none (rank 4: the term is epilogue FMAs)
+//   layout 1: one 64-wide block, [sU_hi | sU_hi | sU_lo] . [B_hi | B_lo | B_hi]
+//   layout 2: [sU_hi | sU_lo] . [B_hi | B_lo], 2R columns, K-steps pairing
+//             hi.hi, hi.lo and lo.hi slices
+template <int R>
+struct RankPlan {
+  static constexpr bool kChunked = R > 16;
+  static constexpr int kRC = kChunked ? 16 : R;  // ranks per pass
+  using EL = std::conditional_t<kChunked, EpiLse<16, true, true>, EpiLse<R>>;
+  using EG = std::conditional_t<kChunked, EpiGrad<16, true, true>, EpiGrad<R>>;
+  static constexpr bool kAug = EL::kAug;
+  static constexpr int kLayout = !kAug ? 0 : kChunked ? 2 : 1;
+  static constexpr int kAugWidth = kLayout == 2 ? (2 * R + 63) / 64 * 64 : kLayout == 1 ? 64 : 0;
+  static constexpr int kAugBlocks = kAugWidth / 64;
+  static_assert(EG::kAug == kAug, "both passes augment the rank term or neither");
+  static void schedule(GemmArgs& g) {
+    g.n_aug = 0;
+    if constexpr (kLayout == 1) {
+      for (int s = 0; s < (3 * R + 15) / 16; ++s) {
+        g.aug_a[g.n_aug] = (uint8_t)s;
+        g.aug_b[g.n_aug++] = (uint8_t)s;
+      }
+    } else if constexpr (kLayout == 2) {
+      constexpr int q = R / 16;
+      for (int k = 0; k < q; ++k) {
+        const uint8_t pa[3] = {(uint8_t)k, (uint8_t)k, (uint8_t)(q + k)};
+        const uint8_t pb[3] = {(uint8_t)k, (uint8_t)(q + k), (uint8_t)k};
+        for (int m = 0; m < 3; ++m) {
+          g.aug_a[g.n_aug] = pa[m];
+          g.aug_b[g.n_aug++] = pb[m];
+        }
+      }
+    }
+  }
+};
 
 template <class Epi>
 GemmKernel gemm_kernel(int pair, int kblocks, int* smem_out) {
   const int smem_staged = SmemLayout::bytes(kblocks, Epi::kRec * Epi::kRecBufs,
                                             pair == 2 ? Epi::kRing : kRingBytes);
   const bool staged = smem_staged <= kMaxDynSmem;
-  *smem_out = staged ? smem_staged : SmemLayout::bytes(kblocks, 0, kRingBytes);
+  *smem_out = staged ? smem_staged
+                     : SmemLayout::bytes(kblocks, 0, pair == 2 ? Epi::kRing : kRingBytes);
   if (pair == 2) return staged ? lce_gemm_kernel<Epi, true, 2> : lce_gemm_kernel<Epi, false, 2>;
   return staged ? lce_gemm_kernel<Epi, true, 1> : lce_gemm_kernel<Epi, false, 1>;
 }
+
+template <int R>
+void plan_units(lora_ce_handle* h, int* u1, int* u2);
 
 // How many tile-range owners (CTAs, or 2-CTA clusters) of this GEMM pass
 // can be resident at once: the persistent split assumes all of them are.
@@ -322,6 +374,21 @@ int resident_units(int pair, int kblocks, int num_sms) {
   int n = 0;
   if (cudaOccupancyMaxActiveClusters(&n, kern, &lc) != cudaSuccess) return 0;
   return n;
+}
+
+// Co-resident units of a rank's two passes; also lets lce_prep of large
+// ranks use its d*R floats of dynamic shared memory.
+template <int R>
+void plan_units(lora_ce_handle* h, int* u1, int* u2) {
+  using Plan = RankPlan<R>;
+  const int kb = h->d / kBK + Plan::kAugBlocks;
+  *u1 = resident_units<typename Plan::EL>(h->pair, kb, h->num_sms);
+  *u2 = resident_units<typename Plan::EG>(h->pair, kb, h->num_sms);
+  const int prep_smem = h->d * R * 4;
+  if (prep_smem > 48 * 1024 &&
+      cudaFuncSetAttribute(lce_prep<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem) !=
+          cudaSuccess)
+    *u1 = 0;
 }
 
 // Launch one GEMM pass: `units` tile-range owners (CTAs, or 2-CTA clusters).
@@ -355,28 +422,32 @@ inline void mark(lora_ce_handle* h, int phase) {
 template <int R>
 int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t* dtg,
              float* d_loss_out, int chunks, const cudaEvent_t* chunk_ready) {
+  using Plan = RankPlan<R>;
+  using EL = typename Plan::EL;
+  using EG = typename Plan::EG;
+  constexpr bool kAug = Plan::kAug;
+  constexpr int kRC = Plan::kRC;
   cudaStream_t st = h->stream;
   const int d = h->d, V = h->V;
-  constexpr bool kAug = EpiLse<R>::kAug;
-  static_assert(EpiGrad<R>::kAug == kAug, "both passes augment the rank term or neither");
   const int kmain = d / kBK;
-  const int kblocks = tile_kblocks<EpiLse<R>>(d);
+  const int kblocks = kmain + Plan::kAugBlocks;  // resident and streamed K-blocks alike
   const long long Tpad = round_up(T, kBN);
   int launches = 0;
+  if (Plan::kChunked) chunks = 1;  // rank chunks: one launch per chunk of ranks instead
 
   CUtensorMap mapH_res, mapH_str;
   if (!make_map(&mapH_res, h->h16, T, d, kBM) || !make_map(&mapH_str, h->h16, T, d, kBN))
     return fail(LORA_CE_ECUDA, "cuTensorMapEncodeTiled failed for h");
   CUtensorMap mapHa_res = mapH_res, mapHa_str = mapH_str;  // unused unless kAug
-  if (kAug && (!make_map(&mapHa_res, h->h_aug, T, kBK, kBM) ||
-               !make_map(&mapHa_str, h->h_aug, T, kBK, kBN)))
+  if (kAug && (!make_map(&mapHa_res, h->h_aug, T, Plan::kAugWidth, kBM) ||
+               !make_map(&mapHa_str, h->h_aug, T, Plan::kAugWidth, kBN)))
     return fail(LORA_CE_ECUDA, "cuTensorMapEncodeTiled failed for the rank augmentation");
 
   const int pair = h->pair;
   const int res_rows = kBM * pair;
   const int n_a1 = (T + res_rows - 1) / res_rows, n_b1 = (int)(h->Vpad / kBN);
   chunks = std::max(1, std::min(chunks, n_a1));
-  const int cp1 = col_parts(EpiLse<R>::kWarps), cp2 = col_parts(EpiGrad<R>::kWarps);
+  const int cp1 = col_parts(EL::kWarps), cp2 = col_parts(EG::kWarps);
   int seg1 = 0;
   for (int c = 0; c < chunks; ++c) {
     const int na = (int)(tile_start(c + 1, n_a1, chunks) - tile_start(c, n_a1, chunks));
@@ -388,10 +459,14 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
     return fail(LORA_CE_ESTATE, "pass-1 partial buffer too small");
   GemmArgs g{};
   g.kblocks = kblocks;
+  g.kstr = kblocks;
   g.kmain = kmain;
+  Plan::schedule(g);
+  g.rank_total = R;
+  g.rank_off = 0;
   g.T = T;
   g.V = V;
-  g.R = R;
+  g.R = kRC;
   g.Vpad = h->Vpad;
   g.err = h->err;
   g.tok = h->tok;
@@ -404,9 +479,13 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
   g.Tcap = stride1;
 
   mark(h, kPhPrep);
-  if constexpr (kAug) {  // [B_hi | B_lo | B_hi] rows from the current B
-    const int blocks = (int)std::min<long long>((h->Vpad * 8 + 255) / 256, 8LL * h->num_sms);
-    lce_aug_b<R><<<blocks, 256, 0, st>>>(h->params + (long long)d * R, h->Vpad, h->w_aug);
+  float* const Bfull = h->params + (long long)d * R;
+  const long long tokc_stride = h->Tcap * tok_stride(16), Bc_stride = h->Vpad * 16;
+  if constexpr (kAug) {  // the vocabulary side of the augmentation, from the current B
+    const int groups = Plan::kAugWidth / 8;
+    const int blocks = (int)std::min<long long>((h->Vpad * groups + 255) / 256, 8LL * h->num_sms);
+    lce_aug_b<R><<<blocks, 256, 0, st>>>(Bfull, h->Vpad, h->w_aug, Plan::kLayout, Plan::kAugWidth,
+                                         Plan::kChunked ? h->Bc : nullptr, Bc_stride);
     ++launches;
   }
   // 1. per chunk of position blocks: convert h, U = h.A, per-position
@@ -421,7 +500,8 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
       const int blocks = (int)std::min<long long>((t_hi - t_lo + 7) / 8, 4LL * h->num_sms);
       lce_prep<R><<<blocks, threads, (size_t)d * R * 4, st>>>(
           dH, dtype, t_lo, t_hi, T, d, h->params, h->cfg.scale, dtg, V, h->h16, h->tok, h->err,
-          kAug ? h->h_aug : nullptr);
+          kAug ? h->h_aug : nullptr, Plan::kLayout, Plan::kAugWidth,
+          Plan::kChunked ? h->tokc : nullptr, tokc_stride);
       ++launches;
     }
     if (c == 0) mark(h, kPhPass1);
@@ -430,20 +510,26 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
     g.n_b = n_b1;
     const long long tot = (long long)g.n_a * n_b1;
     const int Gc = (int)std::min<long long>(h->units1, tot);
-    int rc = launch_gemm<EpiLse<R>>(mapH_res, pair == 2 ? h->mapW_res : h->mapW_str, mapHa_res,
-                                    pair == 2 ? h->mapWa_res : h->mapWa_str, g, Gc, pair, kblocks,
-                                    st);
-    if (rc) return rc;
-    ++launches;
+    for (int rc0 = 0; rc0 < R; rc0 += kRC) {  // rank chunks (one pass below rank 32)
+      g.rank_off = rc0;
+      g.Bt = Plan::kChunked ? h->Bc + (rc0 / 16) * Bc_stride : Bfull;
+      int rc = launch_gemm<EL>(mapH_res, pair == 2 ? h->mapW_res : h->mapW_str, mapHa_res,
+                               pair == 2 ? h->mapWa_res : h->mapWa_str, g, Gc, pair, kblocks, st);
+      if (rc) return rc;
+      ++launches;
+    }
   }
   g.a0 = 0;
+  g.rank_off = 0;
+  g.Bt = Bfull;
   // 3. merge partials -> M, 1/S, loss_t, dU
   mark(h, kPhCombine);
   lce_combine<R><<<(T + 7) / 8, 256, 0, st>>>(T, cp1, res_rows, n_b1, h->units1, chunks, stride1,
                                                   h->p_max,
                                                   h->p_sum,
-                                                  h->p_q, h->z_tgt, g.Bt, h->cfg.scale, h->tok,
-                                                  h->dU, h->loss_tok);
+                                                  h->p_q, h->z_tgt, Bfull, h->cfg.scale, h->tok,
+                                                  h->dU, h->loss_tok,
+                                                  Plan::kChunked ? h->tokc : nullptr, tokc_stride);
   ++launches;
   // onehot part of dB (order-independent fixed-point sums)
   lce_onehot<R><<<(T + 63) / 64, 64, 0, st>>>(T, h->tok, h->corr_fx, h->err);
@@ -455,20 +541,25 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
   if (cp2 * max_segments(n_a2, n_b2, G2) > h->gbp_segs)
     return fail(LORA_CE_ESTATE, "pass-2 partial buffer too small");
   mark(h, kPhPass2);
-  {
-    g.n_a = n_a2;
-    g.n_b = n_b2;
-    int rc = launch_gemm<EpiGrad<R>>(h->mapW_res, pair == 2 ? mapH_res : mapH_str, h->mapWa_res,
-                                     pair == 2 ? mapHa_res : mapHa_str, g, G2, pair, kblocks, st);
+  g.n_a = n_a2;
+  g.n_b = n_b2;
+  for (int rc0 = 0; rc0 < R; rc0 += kRC) {  // rank chunks: their own position records
+    g.rank_off = rc0;
+    g.tok = Plan::kChunked ? h->tokc + (rc0 / 16) * tokc_stride : h->tok;
+    int rc = launch_gemm<EG>(h->mapW_res, pair == 2 ? mapH_res : mapH_str, h->mapWa_res,
+                             pair == 2 ? mapHa_res : mapHa_str, g, G2, pair, kblocks, st);
     if (rc) return rc;
     ++launches;
   }
+  g.tok = h->tok;
   // 5. dA partials, 6. pack gradient sums
   const int n_chunks = (T + kDAChunk - 1) / kDAChunk;
   mark(h, kPhDA);
-  lce_dA_partial<R><<<dim3(n_chunks, (d + 63) / 64), dim3(32, da_rows(R)), 0, st>>>(
-      T, d, h->h16, h->dU, h->gAp);
-  ++launches;
+  for (int rc0 = 0; rc0 < R; rc0 += kRC) {
+    lce_dA_partial<kRC><<<dim3(n_chunks, (d + 63) / 64), dim3(32, da_rows(kRC)), 0, st>>>(
+        T, d, h->h16, h->dU, h->gAp, R, rc0);
+    ++launches;
+  }
   const long long nparam = (long long)d * R + h->Vpad * R;
   mark(h, kPhFinalize);
   {
@@ -513,6 +604,8 @@ int dispatch_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int
     case 4: return run_step<4>(h, dH, dtype, T, dtg, d_loss, chunks, chunk_ready);
     case 8: return run_step<8>(h, dH, dtype, T, dtg, d_loss, chunks, chunk_ready);
     case 16: return run_step<16>(h, dH, dtype, T, dtg, d_loss, chunks, chunk_ready);
+    case 32: return run_step<32>(h, dH, dtype, T, dtg, d_loss, chunks, chunk_ready);
+    case 64: return run_step<64>(h, dH, dtype, T, dtg, d_loss, chunks, chunk_ready);
   }
   return fail(LORA_CE_EINVAL, "unsupported rank");
 }
@@ -730,7 +823,7 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
   if (!h) return fail(LORA_CE_ENOMEM, "host allocation failed");
   h->cfg = *cfg;
   h->r = cfg->rank;
-  h->R = cfg->rank <= 4 ? 4 : cfg->rank <= 8 ? 8 : 16;
+  h->R = kernel_rank(cfg->rank);
   h->d = cfg->dim;
   h->V = cfg->vocab;
   h->Vpad = round_up(cfg->vocab, kBN);
@@ -747,16 +840,11 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
   {
     int u1 = 0, u2 = 0;
     switch (R) {
-      case 4: u1 = resident_units<EpiLse<4>>(h->pair, tile_kblocks<EpiLse<4>>(d), h->num_sms);
-              u2 = resident_units<EpiGrad<4>>(h->pair, tile_kblocks<EpiGrad<4>>(d), h->num_sms);
-              break;
-      case 8: u1 = resident_units<EpiLse<8>>(h->pair, tile_kblocks<EpiLse<8>>(d), h->num_sms);
-              u2 = resident_units<EpiGrad<8>>(h->pair, tile_kblocks<EpiGrad<8>>(d), h->num_sms);
-              break;
-      default: u1 = resident_units<EpiLse<16>>(h->pair, tile_kblocks<EpiLse<16>>(d), h->num_sms);
-               u2 = resident_units<EpiGrad<16>>(h->pair, tile_kblocks<EpiGrad<16>>(d),
-                                                h->num_sms);
-               break;
+      case 4: plan_units<4>(h, &u1, &u2); break;
+      case 8: plan_units<8>(h, &u1, &u2); break;
+      case 16: plan_units<16>(h, &u1, &u2); break;
+      case 32: plan_units<32>(h, &u1, &u2); break;
+      default: plan_units<64>(h, &u1, &u2); break;
     }
     if (u1 < 1 || u2 < 1) {
       delete h;
@@ -816,9 +904,12 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
   if (!rc) rc = dalloc(&h->d_loss, 2);
   if (!rc) rc = dalloc(reinterpret_cast<char**>(&h->in_H), (size_t)Tcap * d * 4);
   if (!rc) rc = dalloc(&h->in_tgt, (size_t)Tcap);
-  const bool aug = R >= LCE_AUG_MIN_RANK;
-  if (!rc && aug) rc = dalloc(&h->w_aug, (size_t)Vpad * kBK);
-  if (!rc && aug) rc = dalloc(&h->h_aug, (size_t)Tcap * kBK);
+  const int aug_width = aug_width_of(R);
+  const bool aug = aug_width > 0;
+  if (!rc && aug) rc = dalloc(&h->w_aug, (size_t)Vpad * aug_width);
+  if (!rc && aug) rc = dalloc(&h->h_aug, (size_t)Tcap * aug_width);
+  if (!rc && R > 16) rc = dalloc(&h->Bc, (size_t)(R / 16) * Vpad * 16);
+  if (!rc && R > 16) rc = dalloc(&h->tokc, (size_t)(R / 16) * Tcap * tok_stride(16));
   if (!rc && (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess ||
               cudaStreamCreateWithFlags(&h->cstream, cudaStreamNonBlocking) != cudaSuccess))
     rc = fail(LORA_CE_ECUDA, "cudaStreamCreate failed");
@@ -831,8 +922,8 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
       rc = fail(LORA_CE_ECUDA, "cudaEventCreate failed");
   if (!rc && !(make_map(&h->mapW_res, h->W, V, d, kBM) && make_map(&h->mapW_str, h->W, V, d, kBN)))
     rc = fail(LORA_CE_ECUDA, "cuTensorMapEncodeTiled failed for W");
-  if (!rc && aug && !(make_map(&h->mapWa_res, h->w_aug, V, kBK, kBM) &&
-                       make_map(&h->mapWa_str, h->w_aug, V, kBK, kBN)))
+  if (!rc && aug && !(make_map(&h->mapWa_res, h->w_aug, V, aug_width, kBM) &&
+                       make_map(&h->mapWa_str, h->w_aug, V, aug_width, kBN)))
     rc = fail(LORA_CE_ECUDA, "cuTensorMapEncodeTiled failed for the rank augmentation");
   if (!aug) {  // never read without augmentation; any valid map fills the kernel parameter
     h->mapWa_res = h->mapW_res;

@@ -54,12 +54,12 @@ constexpr int kAKBytes = kBM * kBK * 2;   // 16 KB per resident K-block
 __host__ __device__ constexpr int str_rows(int pair) { return kBN / pair; }
 __host__ __device__ constexpr int stage_bytes(int pair) { return str_rows(pair) * kBK * 2; }
 __host__ __device__ constexpr int num_stages(int pair) { return kRingBytes / stage_bytes(pair); }
-// A pass whose column records are staged in shared memory may run a smaller
-// ring (Epi::kRing, at least three 16 KB stages in a CTA pair) to make room
-// for them next to the resident tile; otherwise the ring is kRingBytes.
+// In CTA pairs a pass runs the ring of its epilogue (Epi::kRing, at least
+// two 16 KB stages), smaller beside many resident K-blocks to leave room for
+// staged records; single CTAs use kRingBytes.
 template <class Epi, bool kStage, int kPair>
 __host__ __device__ constexpr int ring_bytes() {
-  return (kStage && kPair == 2) ? Epi::kRing : kRingBytes;
+  return kPair == 2 ? Epi::kRing : kRingBytes;
 }
 // Warp roles: warp 0 TMA producer, warp 1 MMA issuer, then kEpiWarps
 // epilogue warps (4 or 2 per TMEM lane quarter, set per epilogue by its
@@ -69,7 +69,7 @@ __host__ __device__ constexpr int col_parts(int epi_warps) { return epi_warps / 
 __host__ __device__ constexpr int block_threads(int epi_warps) { return 32 * (epi_warps + 3); }
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kTmemCols = 512;    // two 256-column fp32 accumulators
-constexpr int kMaxKBlocks = 10;        // d <= 640
+constexpr int kMaxKBlocks = 12;        // resident K-blocks: d/64 plus rank augmentation
 // Smallest rank whose LoRA term joins the MMA as an extra K-block.
 #ifndef LCE_AUG_MIN_RANK
 #define LCE_AUG_MIN_RANK 8
@@ -102,9 +102,19 @@ __host__ __device__ inline int tile_owner(long long x, long long total, int G) {
 
 struct GemmArgs {
   int n_a, n_b;      // resident-tile count, streamed-tile count
-  int kblocks;       // K-blocks per tile: kmain, plus one rank block when augmented
+  int kblocks;       // resident K-blocks: kmain, plus the rank-augmentation blocks
+  int kstr;          // streamed K-blocks per tile: kmain, plus the rank-augmentation blocks
   int kmain;         // d / 64 K-blocks of h / W
   int a0;            // first resident block of this launch (pass 1 runs per chunk of positions)
+  // Rank augmentation: after the kmain K-blocks, MMA K-step s (16 wide)
+  // pairs column slice aug_a[s] of the resident augmentation blocks with
+  // slice aug_b[s] of the streamed ones (slice i = block i/4, columns
+  // 16*(i%4) ..), so that hi/lo products can be formed from any layout.
+  int n_aug;
+  uint8_t aug_a[16], aug_b[16];
+  // Ranks: the epilogue handles ranks [rank_off, rank_off + R) of a rank
+  // of rank_total (larger ranks run as chunks of 16, one launch each).
+  int rank_total, rank_off;
   int T, V, R;
   long long Tcap;    // partial-buffer row stride (positions)
   long long Vpad;    // rows of Bt / gBp
@@ -200,14 +210,16 @@ __device__ __forceinline__ float2 f2(float x, float y) { return make_float2(x, y
 
 // Pass 1: the thread owns position t; columns are vocab ids; the records of
 // a column pair are B[:, v], B[:, v+1] interleaved (2R floats).
-template <int R, bool kAug_ = (R >= LCE_AUG_MIN_RANK)>
+template <int R, bool kAug_ = (R >= LCE_AUG_MIN_RANK), bool kChunk = false>
 struct EpiLse {
   static constexpr bool kAug = kAug_;  // rank term in the accumulator
   static constexpr int kRec = R;  // floats per column
-  // ring when records are staged: 3 stages beside 10 resident K-blocks at
-  // rank 8, 2 at rank 16 (which then fits its 32 KB of records)
-  static constexpr int kRing = !kAug ? kRingBytes : R >= 16 ? 32768 : 49152;
-  static constexpr int kRecBufs = 2;  // staged record buffers (tile i+1 loads during tile i)
+  // ring (CTA pairs): 3 stages beside 10 resident K-blocks at rank 8, 2 at
+  // rank 16 and in rank chunks (up to 11 resident K-blocks)
+  static constexpr int kRing = !kAug ? kRingBytes : (R >= 16 || kChunk) ? 32768 : 49152;
+  // staged record buffers (tile i+1 loads during tile i); a rank chunk
+  // beside 11 resident K-blocks has room for one
+  static constexpr int kRecBufs = kChunk ? 1 : 2;
   static constexpr int kWarps = R == 4 ? 16 : 8;  // 16 at rank 8 would spill
   static constexpr int kCW = (R >= 16 || kWarps == 16) ? 8 : 16;
   static constexpr float kLazy = 8.0f;   // move the reference max only past this
@@ -236,7 +248,7 @@ struct EpiLse {
         sU2[j] = f2(u, u);
       }
     }
-    tgt = valid ? __float_as_int(g.tok[tidx(tt, R + 2, R)]) : -1;
+    tgt = valid ? __float_as_int(g.tok[tidx(tt, g.rank_total + 2, g.rank_total)]) : -1;
     m = -INFINITY;
     mL = -INFINITY;
     s2 = f2(0.f, 0.f);
@@ -329,7 +341,7 @@ struct EpiLse {
     g.p_max[o] = m;
     g.p_sum[o] = s2.x + s2.y;
 #pragma unroll
-    for (int j = 0; j < R; ++j) g.p_q[o * R + j] = q2[j].x + q2[j].y;
+    for (int j = 0; j < R; ++j) g.p_q[o * g.rank_total + g.rank_off + j] = q2[j].x + q2[j].y;
   }
 };
 
@@ -337,15 +349,15 @@ struct EpiLse {
 // of a position pair are tok[] fields interleaved (2(R+4) floats).  This
 // pass accumulates the p part of dl = p - onehot; lce_onehot adds the
 // onehot part.
-template <int R, bool kAug_ = (R >= LCE_AUG_MIN_RANK)>
+template <int R, bool kAug_ = (R >= LCE_AUG_MIN_RANK), bool kChunk = false>
 struct EpiGrad {
   static constexpr bool kAug = kAug_;  // rank term in the accumulator
   static constexpr int kRec = R + 4;
-  // 2 stages beside 10 resident K-blocks when staging (rank 8 fits, rank 16
-  // does not and reads its records from global memory with the full ring)
+  // 2 stages beside 10 or 11 resident K-blocks
   static constexpr int kRing = !kAug ? kRingBytes : 32768;
-  // rank 16 stages one record buffer (its 2 x 20 KB do not fit beside 10
-  // resident K-blocks); the loader then waits for the previous tile's release
+  // rank 16 (and rank chunks) stage one record buffer: 2 x 20 KB do not fit
+  // beside 10 resident K-blocks; the loader then waits for the previous
+  // tile's release
   static constexpr int kRecBufs = (kAug && R >= 16) ? 1 : 2;
   static constexpr int kWarps = R <= 8 ? 16 : 8;
   static constexpr int kCW = (R >= 16 || kWarps == 16) ? 8 : 16;
@@ -399,9 +411,10 @@ struct EpiGrad {
 
   __device__ void flush(const GemmArgs& g, int slot) {
     if (!valid) return;
-    float* o = g.gBp + (long long)slot * g.Vpad * R;
+    const int rt = g.rank_total;
+    float* o = g.gBp + (long long)slot * g.Vpad * rt;
 #pragma unroll
-    for (int j = 0; j < R; ++j) o[bidx(v, j, R)] = g2[j].x + g2[j].y;
+    for (int j = 0; j < R; ++j) o[bidx(v, g.rank_off + j, rt)] = g2[j].x + g2[j].y;
   }
 };
 
@@ -539,7 +552,7 @@ __global__ void __launch_bounds__(block_threads(Epi::kWarps), 1)
           ++a_uses;
         }
         const int srow0 = b * kBN + (int)rank * kStRows;
-        for (int kb = 0; kb < g.kblocks; ++kb) {
+        for (int kb = 0; kb < g.kstr; ++kb) {
           if (!mbar_wait(&bars[kBarEmpty + stage], phase ^ 1, g.err, kErrWaitProducer)) {
             ok = false;
             break;
@@ -591,7 +604,15 @@ __global__ void __launch_bounds__(block_threads(Epi::kWarps), 1)
         if (!mbar_wait(&bars[kBarAccEmpty + buf], (use & 1) ^ 1, g.err, kErrWaitMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(buf * kBN);
-        for (int kb = 0; kb < g.kblocks; ++kb) {
+        auto mma = [&](uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+          if constexpr (kPair == 2) umma_f16_pair(d_tmem, adesc, bdesc, kIdesc, accumulate);
+          else umma_f16(d_tmem, adesc, bdesc, kIdesc, accumulate);
+        };
+        auto release = [&](int st_) {
+          if constexpr (kPair == 2) umma_commit_pair(&bars[kBarEmpty + st_], 0x3);
+          else umma_commit(&bars[kBarEmpty + st_]);
+        };
+        for (int kb = 0; kb < g.kmain; ++kb) {
           if (!mbar_wait(&bars[kBarFull + stage], phase, g.err, kErrWaitMma)) {
             ok = false;
             break;
@@ -600,20 +621,44 @@ __global__ void __launch_bounds__(block_threads(Epi::kWarps), 1)
           const uint64_t adesc = sw128_kmajor_desc(smem_u32(sA + kb * kAKBytes));
           const uint64_t bdesc = sw128_kmajor_desc(smem_u32(sB + stage * kStBytes));
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            if constexpr (kPair == 2)
-              umma_f16_pair(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), kIdesc,
-                            (kb | k) != 0 ? 1u : 0u);
-            else
-              umma_f16(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), kIdesc,
-                       (kb | k) != 0 ? 1u : 0u);
-          }
-          if constexpr (kPair == 2) umma_commit_pair(&bars[kBarEmpty + stage], 0x3);
-          else umma_commit(&bars[kBarEmpty + stage]);
+          for (int k = 0; k < kBK / 16; ++k)
+            mma(adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), (kb | k) != 0 ? 1u : 0u);
+          release(stage);
           if (++stage == kSt) {
             stage = 0;
             phase ^= 1;
           }
+        }
+        // rank augmentation: all of this tile's streamed augmentation stages
+        // (one or two; the ring has at least two) in the ring at once, then
+        // the scheduled K-steps, then their release
+        const int n_str_aug = g.kstr - g.kmain;
+        int aug_stage[2] = {0, 0};
+        for (int i = 0; i < n_str_aug && ok; ++i) {
+          if (!mbar_wait(&bars[kBarFull + stage], phase, g.err, kErrWaitMma)) {
+            ok = false;
+            break;
+          }
+          aug_stage[i] = stage;
+          if (++stage == kSt) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        if (n_str_aug > 0) {
+          tc_fence_after();
+          for (int sidx = 0; sidx < g.n_aug; ++sidx) {
+            const int ia = g.aug_a[sidx], ib = g.aug_b[sidx];
+            const uint64_t adesc =
+                sw128_kmajor_desc(smem_u32(sA + (g.kmain + (ia >> 2)) * kAKBytes)) +
+                (uint64_t)(2 * (ia & 3));
+            const uint64_t bdesc =
+                sw128_kmajor_desc(smem_u32(sB + aug_stage[ib >> 2] * kStBytes)) +
+                (uint64_t)(2 * (ib & 3));
+            mma(adesc, bdesc, 1u);
+          }
+          for (int i = 0; i < n_str_aug; ++i) release(aug_stage[i]);
         }
         if (!ok) break;
         const bool last_of_a = x + 1 == x_end || (int)((x + 1) / g.n_b) != a;
@@ -751,7 +796,8 @@ __global__ void lce_prep(const void* __restrict__ H, int dtype, int t_lo, int t_
                          const float* __restrict__ A, float scale,
                          const int32_t* __restrict__ targets, int V,
                          __half* __restrict__ h16, float* __restrict__ tok, int* err,
-                         __half* __restrict__ haug) {
+                         __half* __restrict__ haug, int aug_layout, int aug_width,
+                         float* __restrict__ tokc, long long tokc_stride) {
   extern __shared__ __align__(16) float sA[];  // [d][R]
   for (int k = threadIdx.x; k < d * R; k += blockDim.x) sA[k] = A[k];
   __syncthreads();
@@ -761,8 +807,13 @@ __global__ void lce_prep(const void* __restrict__ H, int dtype, int t_lo, int t_
     if (w >= T) {  // padding position: all fields zero, target -1
       for (int f = lane; f < tok_stride(R); f += 32)
         tok[tidx(w, f, R)] = f == R + 2 ? __int_as_float(-1) : 0.f;
-      if (haug) *reinterpret_cast<__half2*>(haug + (long long)w * 64 + 2 * lane) =
-          __floats2half2_rn(0.f, 0.f);
+      if (haug)
+        for (int cc = 2 * lane; cc < aug_width; cc += 64)
+          *reinterpret_cast<__half2*>(haug + (long long)w * aug_width + cc) =
+              __floats2half2_rn(0.f, 0.f);
+      if (tokc)  // chunk records of a padding position: all zero
+        for (int c = 0; c < R / 16; ++c)
+          for (int f = lane; f < tok_stride(16); f += 32) tokc[c * tokc_stride + tidx(w, f, 16)] = 0.f;
       continue;
     }
     float u[R];
@@ -791,19 +842,36 @@ __global__ void lce_prep(const void* __restrict__ H, int dtype, int t_lo, int t_
       for (int off = 16; off > 0; off >>= 1) u[j] += __shfl_xor_sync(0xffffffffu, u[j], off);
     }
     if (haug) {
-      // lane l writes augmentation columns 2l, 2l+1: [sU_hi | sU_hi | sU_lo | 0]
-      __half hv2[2];
+      // columns of the augmentation row: layout 1 [sU_hi | sU_hi | sU_lo | 0]
+      // (ranks <= 21, one 64-wide block), layout 2 [sU_hi | sU_lo] (ranks 32,
+      // 64); lane l writes columns 2l, 2l+1 of each 64-column block
+      for (int cb = 0; cb < aug_width; cb += 64) {
+        __half hv2[2];
 #pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const int c = 2 * lane + k, part = c / R, jc = c - part * R;
-        float su = 0.f;
+        for (int k = 0; k < 2; ++k) {
+          const int c = cb + 2 * lane + k, part = c / R, jc = c - part * R;
+          float su = 0.f;
 #pragma unroll
-        for (int j = 0; j < R; ++j) su = (j == jc) ? scale * u[j] : su;
-        const __half hi = __float2half_rn(su);
-        const __half lo = __float2half_rn(su - __half2float(hi));
-        hv2[k] = part < 2 ? hi : part == 2 ? lo : __float2half_rn(0.f);
+          for (int j = 0; j < R; ++j) su = (j == jc) ? scale * u[j] : su;
+          const __half hi = __float2half_rn(su);
+          const __half lo = __float2half_rn(su - __half2float(hi));
+          const bool is_lo = aug_layout == 1 ? part == 2 : part == 1;
+          const bool used = aug_layout == 1 ? part < 3 : part < 2;
+          hv2[k] = !used ? __float2half_rn(0.f) : is_lo ? lo : hi;
+        }
+        *reinterpret_cast<__half2*>(haug + (long long)w * aug_width + cb + 2 * lane) =
+            __halves2half2(hv2[0], hv2[1]);
       }
-      *reinterpret_cast<__half2*>(haug + (long long)w * 64 + 2 * lane) = __halves2half2(hv2[0], hv2[1]);
+    }
+    if (tokc) {
+      // rank chunks of 16: sU of the chunk; M, 1/S come from lce_combine
+      for (int c = 0; c < R / 16; ++c)
+        for (int f = lane; f < tok_stride(16); f += 32) {
+          float val = 0.f;
+#pragma unroll
+          for (int j = 0; j < R; ++j) val = (f < 16 && j == 16 * c + f) ? scale * u[j] : val;
+          tokc[c * tokc_stride + tidx(w, f, 16)] = val;
+        }
     }
     if (lane == 0) {
       int tg = targets[w];
@@ -821,27 +889,42 @@ __global__ void lce_prep(const void* __restrict__ H, int dtype, int t_lo, int t_
   }
 }
 
-// The vocabulary side of rank augmentation: waug[v] = [B_hi | B_lo | B_hi | 0]
-// (64 f16 per row, v < Vpad; rows >= V are zero like B).  One thread per
-// 8 columns of a row (16-byte stores).  Rebuilt at the start of every step
-// from the current B.
+// The vocabulary side of rank augmentation, rebuilt at the start of every
+// step from the current B (rows >= V are zero like B): layout 1
+// waug[v] = [B_hi | B_lo | B_hi | 0] (ranks <= 21, one 64-wide block),
+// layout 2 waug[v] = [B_hi | B_lo] (ranks 32, 64).  One thread per 8
+// columns of a row (16-byte stores).  With Bc, also B's rank chunks of 16,
+// each in the pair-interleaved layout of rank 16 (pass 1's column records).
 template <int R>
-__global__ void lce_aug_b(const float* __restrict__ Bt, long long Vpad, __half* __restrict__ waug) {
-  static_assert(3 * R <= 64, "rank augmentation fits one 64-wide K-block");
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < Vpad * 8;
+__global__ void lce_aug_b(const float* __restrict__ Bt, long long Vpad, __half* __restrict__ waug,
+                          int aug_layout, int aug_width, float* __restrict__ Bc,
+                          long long Bc_stride) {
+  static_assert(3 * R <= 64 || R % 16 == 0, "layout 1 fits one block; larger ranks use layout 2");
+  const int groups = aug_width / 8;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < Vpad * groups;
        i += (long long)gridDim.x * blockDim.x) {
-    const long long v = i >> 3;
-    const int c0 = (int)(i & 7) * 8;
+    const long long v = i / groups;
+    const int c0 = (int)(i - v * groups) * 8;
     __align__(16) __half o[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       const int c = c0 + e, part = c / R, j = c - part * R;
-      const float b = part < 3 ? Bt[bidx(v, j, R)] : 0.f;
+      const bool used = aug_layout == 1 ? part < 3 : part < 2;
+      const bool is_lo = part == 1;  // [hi | lo | hi] and [hi | lo] alike
+      const float b = used ? Bt[bidx(v, j, R)] : 0.f;
       const __half hi = __float2half_rn(b);
       const __half lo = __float2half_rn(b - __half2float(hi));
-      o[e] = part == 1 ? lo : hi;  // part 3 (padding): b = 0, hi = 0
+      o[e] = is_lo ? lo : hi;  // unused columns: b = 0, hi = 0
     }
-    *reinterpret_cast<uint4*>(waug + v * 64 + c0) = *reinterpret_cast<const uint4*>(o);
+    *reinterpret_cast<uint4*>(waug + v * aug_width + c0) = *reinterpret_cast<const uint4*>(o);
+  }
+  if (Bc) {  // rank chunks of 16 in their own pair-interleaved arrays
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < Vpad * R;
+         i += (long long)gridDim.x * blockDim.x) {
+      const long long v = i / R;
+      const int j = (int)(i - v * R);
+      Bc[(j / 16) * Bc_stride + bidx(v, j % 16, 16)] = Bt[bidx(v, j, R)];
+    }
   }
 }
 
@@ -857,7 +940,8 @@ __global__ void lce_combine(int T, int cparts, int res_rows, int n_b1, int units
                             const float* __restrict__ p_sum, const float* __restrict__ p_q,
                             const float* __restrict__ z_tgt, const float* __restrict__ Bt,
                             float scale, float* __restrict__ tok, float* __restrict__ dU,
-                            float* __restrict__ loss_tok) {
+                            float* __restrict__ loss_tok, float* __restrict__ tokc,
+                            long long tokc_stride) {
   // one warp per position; lane k merges slots k, k+32, ... (fixed order)
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -904,6 +988,11 @@ __global__ void lce_combine(int T, int cparts, int res_rows, int n_b1, int units
   loss_tok[t] = -logf(pt + 1e-12f);
   tok[tidx(t, R, R)] = -(M * kLog2e);
   tok[tidx(t, R + 1, R)] = inv;
+  if (tokc)  // the rank chunks' records of position t (pass 2 of each chunk)
+    for (int c = 0; c < R / 16; ++c) {
+      tokc[c * tokc_stride + tidx(t, 16, 16)] = -(M * kLog2e);
+      tokc[c * tokc_stride + tidx(t, 17, 16)] = inv;
+    }
 #pragma unroll
   for (int j = 0; j < R; ++j) dU[(long long)t * R + j] = scale * (Q[j] * inv - Bt[bidx(tg, j, R)]);
 }
@@ -963,7 +1052,8 @@ template <int R>
 __global__ void __launch_bounds__(32 * da_rows(R)) lce_dA_partial(int T, int d,
                                                                   const __half* __restrict__ h16,
                                                                   const float* __restrict__ dU,
-                                                                  float* __restrict__ gAp) {
+                                                                  float* __restrict__ gAp,
+                                                                  int rank_total, int rank_off) {
   constexpr int Y = da_rows(R);
   constexpr int NT = 32 * Y;
   __shared__ __align__(16) float sdU[kDAChunk * R];
@@ -972,7 +1062,8 @@ __global__ void __launch_bounds__(32 * da_rows(R)) lce_dA_partial(int T, int d,
   const int t0 = c * kDAChunk;
   const int nt = min(kDAChunk, T - t0);
   const int tid = threadIdx.y * 32 + threadIdx.x;
-  for (int k = tid; k < nt * R; k += NT) sdU[k] = dU[(long long)t0 * R + k];
+  for (int k = tid; k < nt * R; k += NT)
+    sdU[k] = dU[(long long)(t0 + k / R) * rank_total + rank_off + k % R];
   __syncthreads();
   const int i = blockIdx.y * 64 + 2 * threadIdx.x;
   float a0[R], a1[R];
@@ -1001,7 +1092,7 @@ __global__ void __launch_bounds__(32 * da_rows(R)) lce_dA_partial(int T, int d,
 #pragma unroll
     for (int y = 0; y < Y; ++y) v += sred[y][k];
     const int ii = blockIdx.y * 64 + k / R;
-    if (ii < d) gAp[((long long)c * d + ii) * R + (k % R)] = v;
+    if (ii < d) gAp[((long long)c * d + ii) * rank_total + rank_off + (k % R)] = v;
   }
 }
 

@@ -234,10 +234,13 @@ extern "C" int lora_ce_token_loss_noalloc(const uint16_t* d_W, int32_t vocab, in
     return na_fail(LORA_CE_EINVAL, "hidden states must be 16-byte aligned");
   lce_prep<R><<<(int)std::min<long long>((Tpad + 7) / 8, 592), 256, (size_t)d * R * 4, st>>>(
       d_H, h_dtype, 0, (int)Tpad, T, d, s->params, scale, d_targets, V, s->h16, s->tok, s->err,
-      nullptr);
+      nullptr, 0, 0, nullptr, 0);
   GemmArgs g{};
   g.kblocks = kblocks;
+  g.kstr = kblocks;
   g.kmain = kblocks;
+  g.rank_total = R;
+  g.rank_off = 0;
   g.T = T;
   g.V = V;
   g.R = R;
@@ -278,7 +281,7 @@ extern "C" int lora_ce_token_loss_noalloc(const uint16_t* d_W, int32_t vocab, in
   lce_combine<R><<<(T + 7) / 8, 256, 0, st>>>(T, cp1, res_rows, n_b1, s->units, 1, stride1,
                                                   s->pmax,
                                                   s->psum, s->pq, s->ztgt, Bp, scale, s->tok,
-                                                  s->dU, d_loss);
+                                                  s->dU, d_loss, nullptr, 0);
   na_poison<<<(T + 255) / 256, 256, 0, st>>>(s->err, d_loss, T);
   if (cudaGetLastError() != cudaSuccess) return na_fail(LORA_CE_ECUDA, "kernel launch failed");
   return 0;

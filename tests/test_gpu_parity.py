@@ -80,6 +80,10 @@ def run_case(oracle, V, d, r, T, seed, dtype="bf16", steps=1, scale=2.0, lr=1e-3
         (3000, 192, 3, 40, "f16"),
         (2048, 576, 13, 100, "bf16"),
         (49152, 576, 16, 700, "bf16"),  # rank augmentation at full vocabulary
+        (4099, 128, 32, 100, "bf16"),   # rank chunks: 2 x 16, augmentation layout 2
+        (3000, 192, 20, 77, "f16"),     # padded to 32
+        (2048, 576, 40, 260, "bf16"),   # padded to 64
+        (49152, 576, 64, 300, "bf16"),  # rank 64 at full vocabulary (11 resident K-blocks)
     ],
 )
 def test_step_matches_oracle(oracle, V, d, r, T, dtype):
