@@ -27,15 +27,21 @@
 // Neither epilogue needs a reduction across threads, and the T x V logits
 // never leave TMEM/registers.
 //
-// Rank augmentation (ranks 8 and 16): the LoRA term of the logits,
-// s*U[t].B[:,v], joins the tensor-core product as one more 64-wide K-block,
-//   haug[t] = [sU_hi | sU_hi | sU_lo | 0],  waug[v] = [B_hi | B_lo | B_hi | 0]
-// (x_hi = f16(x), x_lo = f16(x - x_hi)), so the accumulator holds
-// h.W + sU_hi.B_hi + sU_hi.B_lo + sU_lo.B_hi: the rank term to about 2^-22
-// relative (only the lo.lo product is dropped), and the epilogues skip r
-// multiply-adds per logit.  At rank 4 the extra K-block (11% more MMA
-// work) costs more than the four multiply-adds it saves, so rank 4 keeps
-// the term in the epilogue.
+// Rank augmentation (ranks 8 to 64): the LoRA term of the logits,
+// s*U[t].B[:,v], joins the tensor-core product as extra K-blocks, with
+// x_hi = f16(x), x_lo = f16(x - x_hi):
+//   layout 1 (ranks 8, 16; one 64-wide block)
+//     haug[t] = [sU_hi | sU_hi | sU_lo | 0],  waug[v] = [B_hi | B_lo | B_hi | 0]
+//   layout 2 (ranks 32, 64; 2R columns)
+//     haug[t] = [sU_hi | sU_lo],  waug[v] = [B_hi | B_lo]
+//     with K-steps pairing the hi.hi, hi.lo and lo.hi column slices
+//     (GemmArgs::aug_a / aug_b).
+// Either way the accumulator holds h.W + sU_hi.B_hi + sU_hi.B_lo +
+// sU_lo.B_hi: the rank term to about 2^-22 relative (only lo.lo is dropped),
+// and the epilogues skip r multiply-adds per logit.  At rank 4 the extra
+// K-block (11% more MMA work) costs more than the four multiply-adds it
+// saves, so rank 4 keeps the term in the epilogue.  Ranks 32 and 64 run each
+// pass once per 16-rank chunk of the epilogue sums (GemmArgs::rank_off).
 #pragma once
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>

@@ -369,3 +369,32 @@ def test_graph_replay_reads_current_inputs(oracle):
                           state=state)
         state, Ao, Bo = ref["state"], ref["A"], ref["B"]
         assert abs(lg - ref["loss"]) <= LOSS_RTOL * ref["loss"]
+
+
+def test_rank64_adamw_clip_and_graph_replay(oracle):
+    """Rank 64 (16-rank chunks, augmentation layout 2) with weight decay and
+    an active clip over three steps (graph replays after the first), and
+    bit-identical results on a second handle."""
+    V, d, r, T = 8192, 576, 64, 384
+    W, H, Hor, tgt, A, B = make(V, d, r, T, 64)
+    runs = []
+    for _ in range(2):
+        m = lora_ce.LoraCE(lora_ce.default_config(d, V, r, T, scale=2.0, lr=1e-3,
+                                                  weight_decay=0.01, clip_norm=1e-3))
+        m.set_weight(W)
+        m.set_adapter(A, B, 0)
+        losses = [m.step(H, tgt) for _ in range(3)]
+        A1, B1, step = m.get_adapter()
+        assert step == 3
+        runs.append((losses, A1, B1))
+        m.close()
+    np.testing.assert_array_equal(np.float32(runs[0][0]), np.float32(runs[1][0]))
+    np.testing.assert_array_equal(runs[0][1], runs[1][1])
+    np.testing.assert_array_equal(runs[0][2], runs[1][2])
+    state, Ao, Bo = None, A, B
+    for k in range(3):
+        ref = oracle.step(W, Ao, Bo, Hor, tgt, 2.0, 1e-3, wd=0.01, clip=1e-3, nthreads=NTHREADS,
+                          state=state)
+        state, Ao, Bo = ref["state"], ref["A"], ref["B"]
+        assert abs(runs[0][0][k] - ref["loss"]) <= LOSS_RTOL * ref["loss"]
+    assert rel(runs[0][1], Ao) <= L2_RTOL and rel(runs[0][2], Bo) <= L2_RTOL
