@@ -480,7 +480,7 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
 
   mark(h, kPhPrep);
   float* const Bfull = h->params + (long long)d * R;
-  const long long tokc_stride = h->Tcap * tok_stride(16), Bc_stride = h->Vpad * 16;
+  const long long tokc_stride = h->Tcap * kChunkRec, Bc_stride = h->Vpad * 16;
   if constexpr (kAug) {  // the vocabulary side of the augmentation, from the current B
     const int groups = Plan::kAugWidth / 8;
     const int blocks = (int)std::min<long long>((h->Vpad * groups + 255) / 256, 8LL * h->num_sms);
@@ -632,9 +632,10 @@ int check_device_error(lora_ce_handle* h) {
     h->poisoned = true;
     char buf[96];
     snprintf(buf, sizeof buf, "device error %d (%s)", e,
-             e == kErrTarget  ? "target id out of range"
-             : e == kErrRange ? "s*U out of the supported range"
-                              : "bounded wait expired");
+             e == kErrTarget      ? "target id out of range"
+             : e == kErrRange     ? "s*U out of the supported range"
+             : e == kErrSmemAlign ? "shared memory base not 1024-byte aligned"
+                                  : "bounded wait expired");
     return fail(LORA_CE_EDEVICE, buf);
   }
   return 0;
@@ -909,7 +910,7 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
   if (!rc && aug) rc = dalloc(&h->w_aug, (size_t)Vpad * aug_width);
   if (!rc && aug) rc = dalloc(&h->h_aug, (size_t)Tcap * aug_width);
   if (!rc && R > 16) rc = dalloc(&h->Bc, (size_t)(R / 16) * Vpad * 16);
-  if (!rc && R > 16) rc = dalloc(&h->tokc, (size_t)(R / 16) * Tcap * tok_stride(16));
+  if (!rc && R > 16) rc = dalloc(&h->tokc, (size_t)(R / 16) * Tcap * kChunkRec);
   if (!rc && (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess ||
               cudaStreamCreateWithFlags(&h->cstream, cudaStreamNonBlocking) != cudaSuccess))
     rc = fail(LORA_CE_ECUDA, "cudaStreamCreate failed");
@@ -1101,9 +1102,10 @@ int lora_ce_step(lora_ce_handle* h, const void* H, int32_t dtype, int32_t T,
   memcpy(&e, &res[1], 4);
   if (e != 0) {
     h->poisoned = true;
-    return fail(LORA_CE_EDEVICE, e == kErrTarget  ? "target id out of range"
-                                 : e == kErrRange ? "s*U out of the supported range"
-                                                  : "device pipeline error (bounded wait expired)");
+    return fail(LORA_CE_EDEVICE, e == kErrTarget      ? "target id out of range"
+                                 : e == kErrRange     ? "s*U out of the supported range"
+                                 : e == kErrSmemAlign ? "shared memory base not 1024-byte aligned"
+                                                      : "device pipeline error (bounded wait expired)");
   }
   if (loss_out) *loss_out = res[0];
   return 0;

@@ -89,6 +89,12 @@ constexpr int kMaxKBlocks = 12;        // resident K-blocks: d/64 plus rank augm
 //        0..R-1 s*U[t][:], R: -M*log2(e), R+1: 1/S, R+2: target (int bits), R+3: 0
 // A whole 256-column tile is one contiguous block in either layout.
 __host__ __device__ constexpr int tok_stride(int R) { return R + 4; }
+// A rank chunk's pass-2 record of position t: fields 0..15 sU of the
+// chunk's 16 ranks, 16: -M*log2(e), 17: 1/S, pair-interleaved like tidx.
+constexpr int kChunkRec = 18;
+__host__ __device__ inline long long crec_idx(long long t, int f) {
+  return (t >> 1) * 2 * kChunkRec + 2 * f + (t & 1);
+}
 __host__ __device__ inline long long bidx(long long v, int j, int R) {
   return (v >> 1) * 2 * R + 2 * j + (v & 1);
 }
@@ -151,8 +157,10 @@ struct SmemLayout {
   static __host__ __device__ constexpr int bar_off(int kblocks, int rec_floats, int ring) {
     return rec_off(kblocks, ring) + rec_bytes(rec_floats);
   }
+  // The dynamic shared array is declared 1024-byte aligned, so no slack is
+  // reserved for aligning it; the kernel checks the alignment it got.
   static __host__ __device__ constexpr int bytes(int kblocks, int rec_floats, int ring) {
-    return 1024 /*align slack*/ + bar_off(kblocks, rec_floats, ring) + 256;
+    return bar_off(kblocks, rec_floats, ring) + 256;
   }
 };
 constexpr int kMaxDynSmem = 232448;  // 227 KB opt-in per CTA on sm_100
@@ -358,7 +366,9 @@ struct EpiLse {
 template <int R, bool kAug_ = (R >= LCE_AUG_MIN_RANK), bool kChunk = false>
 struct EpiGrad {
   static constexpr bool kAug = kAug_;  // rank term in the accumulator
-  static constexpr int kRec = R + 4;
+  // rank chunks read their own records {sU[0..16), -M log2 e, 1/S}
+  // (crec_idx), the others the position records tok[] (tidx)
+  static constexpr int kRec = kChunk ? R + 2 : R + 4;
   // 2 stages beside 10 or 11 resident K-blocks
   static constexpr int kRing = !kAug ? kRingBytes : 32768;
   // rank 16 (and rank chunks) stage one record buffer: 2 x 20 KB do not fit
@@ -463,10 +473,22 @@ __global__ void __launch_bounds__(block_threads(Epi::kWarps), 1)
   static_assert(kSt >= 2 && kSt <= kMaxStages, "ring stages");
   constexpr int kStRows = str_rows(kPair);
   constexpr int kResRows = kBM * kPair;
-  extern __shared__ uint8_t smem_raw[];
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment by index arithmetic on the shared array, so that
-  // pointers derived from it stay in the shared address space.
-  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  // pointers derived from it stay in the shared address space.  The array is
+  // declared aligned and the layout reserves no slack: a base that arrived
+  // misaligned by more than the launch's spare bytes is reported, not used
+  // (both CTAs of a pair see the same base and return together).
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  {
+    uint32_t dyn_bytes;
+    asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn_bytes));
+    if (pad + (uint32_t)SmemLayout::bytes(g.kblocks, kRecF, kRingB) > dyn_bytes) {
+      if (threadIdx.x == 0) atomicCAS(g.err, 0, kErrSmemAlign);
+      return;
+    }
+  }
+  uint8_t* smem = smem_raw + pad;
   uint8_t* sA = smem + SmemLayout::a_off();
   uint8_t* sB = smem + SmemLayout::b_off(g.kblocks);
   float* srec = reinterpret_cast<float*>(smem + SmemLayout::rec_off(g.kblocks, kRingB));
@@ -729,10 +751,24 @@ __global__ void __launch_bounds__(block_threads(Epi::kWarps), 1)
         // the masked chunk variant.
         const bool tail = gcol + kBN / kColParts > Epi::limit(g);
         float ca[CW], cb[CW];
+        // Records read from global memory (not staged): the lanes prefetch
+        // into L1 the lines of chunk c+2's records while chunk c runs.
+        constexpr int kRecLine = 32;  // floats per 128-byte line
+        constexpr int kChunkLines = (CW * Epi::kRec + kRecLine - 1) / kRecLine;
+        auto prefetch_recs = [&](int c) {
+          if constexpr (!kStage) {
+            if (c < NCH && lane < kChunkLines)
+              asm volatile("prefetch.L1 [%0];" ::"l"(rb + c * CW * Epi::kRec + lane * kRecLine));
+          }
+        };
+        prefetch_recs(0);
+        prefetch_recs(1);
         tmem_ld<CW>(base, ca);
         tmem_ld_wait<CW>(ca);
 #pragma unroll 1
         for (int c = 0; c < NCH; c += 2) {
+          prefetch_recs(c + 2);
+          prefetch_recs(c + 3);
           tmem_ld<CW>(base + (uint32_t)((c + 1) * CW), cb);
           run_chunk<Epi>(epi, g, tail, gcol + c * CW, ca, rb + c * CW * Epi::kRec);
           tmem_ld_wait<CW>(cb);
@@ -819,7 +855,7 @@ __global__ void lce_prep(const void* __restrict__ H, int dtype, int t_lo, int t_
               __floats2half2_rn(0.f, 0.f);
       if (tokc)  // chunk records of a padding position: all zero
         for (int c = 0; c < R / 16; ++c)
-          for (int f = lane; f < tok_stride(16); f += 32) tokc[c * tokc_stride + tidx(w, f, 16)] = 0.f;
+          for (int f = lane; f < kChunkRec; f += 32) tokc[c * tokc_stride + crec_idx(w, f)] = 0.f;
       continue;
     }
     float u[R];
@@ -872,11 +908,11 @@ __global__ void lce_prep(const void* __restrict__ H, int dtype, int t_lo, int t_
     if (tokc) {
       // rank chunks of 16: sU of the chunk; M, 1/S come from lce_combine
       for (int c = 0; c < R / 16; ++c)
-        for (int f = lane; f < tok_stride(16); f += 32) {
+        for (int f = lane; f < kChunkRec; f += 32) {
           float val = 0.f;
 #pragma unroll
           for (int j = 0; j < R; ++j) val = (f < 16 && j == 16 * c + f) ? scale * u[j] : val;
-          tokc[c * tokc_stride + tidx(w, f, 16)] = val;
+          tokc[c * tokc_stride + crec_idx(w, f)] = val;
         }
     }
     if (lane == 0) {
@@ -996,8 +1032,8 @@ __global__ void lce_combine(int T, int cparts, int res_rows, int n_b1, int units
   tok[tidx(t, R + 1, R)] = inv;
   if (tokc)  // the rank chunks' records of position t (pass 2 of each chunk)
     for (int c = 0; c < R / 16; ++c) {
-      tokc[c * tokc_stride + tidx(t, 16, 16)] = -(M * kLog2e);
-      tokc[c * tokc_stride + tidx(t, 17, 16)] = inv;
+      tokc[c * tokc_stride + crec_idx(t, 16)] = -(M * kLog2e);
+      tokc[c * tokc_stride + crec_idx(t, 17)] = inv;
     }
 #pragma unroll
   for (int j = 0; j < R; ++j) dU[(long long)t * R + j] = scale * (Q[j] * inv - Bt[bidx(tg, j, R)]);

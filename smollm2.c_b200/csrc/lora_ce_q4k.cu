@@ -43,8 +43,6 @@ __global__ void __launch_bounds__(256) lce_q4k_dequant(const uint8_t* __restrict
   const int o = (lane & 3) * 8;     // offset in the run's 32 quant bytes
   const int j = 2 * c + hi;         // sub-block
   const int sh = 8 * (j & 3);
-  // two blocks per iteration: both blocks' loads are in flight before either
-  // is decoded
   auto decode = [&](long long b, const uint4& hdr, const uint2& qv) {
     const uint32_t s0 = hdr.y >> sh, s1 = hdr.z >> sh, s2 = hdr.w >> sh;  // scales[k], [k+4], [k+8]
     uint32_t sc, m;
@@ -86,19 +84,26 @@ __global__ void __launch_bounds__(256) lce_q4k_dequant(const uint8_t* __restrict
     }
   };
   auto qoff = [&](long long b) { return blocks + b * 144 + 16 + 32 * c + o; };
+  // kInFlight blocks per iteration: all their loads are issued before any
+  // is decoded, so a warp keeps several global loads outstanding
+  constexpr int kInFlight = 4;
   for (long long b = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); b < n_blocks;
-       b += 2 * warps) {
-    const long long b2 = b + warps;
-    const uint4 h1 = *reinterpret_cast<const uint4*>(blocks + b * 144);  // d, dmin | scales
-    const uint2 q1 = *reinterpret_cast<const uint2*>(qoff(b));
-    uint4 h2 = make_uint4(0, 0, 0, 0);
-    uint2 q2 = make_uint2(0, 0);
-    if (b2 < n_blocks) {
-      h2 = *reinterpret_cast<const uint4*>(blocks + b2 * 144);
-      q2 = *reinterpret_cast<const uint2*>(qoff(b2));
+       b += kInFlight * warps) {
+    uint4 hd[kInFlight];
+    uint2 qd[kInFlight];
+#pragma unroll
+    for (int u = 0; u < kInFlight; ++u) {
+      const long long bu = b + u * warps;
+      hd[u] = make_uint4(0, 0, 0, 0);
+      qd[u] = make_uint2(0, 0);
+      if (bu < n_blocks) {
+        hd[u] = *reinterpret_cast<const uint4*>(blocks + bu * 144);  // d, dmin | scales
+        qd[u] = *reinterpret_cast<const uint2*>(qoff(bu));
+      }
     }
-    decode(b, h1, q1);
-    if (b2 < n_blocks) decode(b2, h2, q2);
+#pragma unroll
+    for (int u = 0; u < kInFlight; ++u)
+      if (b + u * warps < n_blocks) decode(b + u * warps, hd[u], qd[u]);
   }
 }
 

@@ -20,6 +20,7 @@ enum DeviceError : int {
   kErrTarget = 4,
   kErrDrain = 5,
   kErrRange = 6,
+  kErrSmemAlign = 7,  // dynamic shared memory not 1024-byte aligned (layout would not fit)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
