@@ -17,6 +17,7 @@
 
 #include "lora_ce.h"
 #include "lora_ce_kernels.cuh"
+#include "lora_ce_tc.cuh"
 
 using namespace lce;
 
@@ -67,6 +68,22 @@ bool make_map(CUtensorMap* m, const void* base, long long rows, int d, int box_r
   if (!fn) return false;
   cuuint64_t dims[2] = {(cuuint64_t)d, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)d * 2};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+// [rows][width] f16 with a row stride of ld elements (ld % 8 == 0), read in
+// boxes of 64 x box_rows with 128 B swizzle; columns past width read as 0.
+bool make_map_ld(CUtensorMap* m, const void* base, long long rows, long long width, long long ld,
+                 int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)width, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
   cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
@@ -144,6 +161,10 @@ struct lora_ce_handle {
   int num_sms = 0;
   int pair = 2;             // 2: CTA-pair (cta_group::2) GEMM tiles; 1: single-CTA tiles
   int units1 = 0, units2 = 0;  // co-resident tile-range owners of pass 1 / pass 2
+  // ranks 8..64 in CTA pairs: both passes with their rank sums on the tensor
+  // cores (lce_gemm_tc, 192-column streamed tiles)
+  bool tc = false;
+  int units1t = 0, units2t = 0;
   cudaStream_t stream = nullptr;
   // host-input steps copy h in chunks on `cstream` while the compute stream
   // converts and runs pass 1 on the chunks that have arrived
@@ -211,6 +232,12 @@ struct lora_ce_handle {
   float* Bc = nullptr;
   float* tokc = nullptr;
   CUtensorMap mapWa_res{}, mapWa_str{};
+  // tensor-core rank sums: pass 1's B^T [hi ; lo] (2R x Vpad), pass 2's
+  // (s*U)^T [hi ; lo] (2R x Tcap) and per-position exponent offsets
+  __half* xv = nullptr;
+  __half* xt = nullptr;
+  float* nml = nullptr;
+  CUtensorMap mapW_strT{}, mapWa_strT{}, mapXv{};
   ncclComm_t comm = nullptr;
   int nranks = 1, rank = 0;
   // optional per-phase timing (events on the handle's stream)
@@ -244,7 +271,8 @@ void free_all(lora_ce_handle* h) {
   void* ptrs[] = {h->W,     h->h16,   h->tok,      h->params, h->mom1,  h->mom2,
                   h->Gbuf,  h->gmean, h->p_max,    h->p_sum,  h->p_q,   h->z_tgt,
                   h->loss_tok, h->dU, h->gAp,      h->gBp,    h->norm_parts, h->err, h->corr_fx,
-                  h->d_loss, h->in_H, h->in_tgt, h->w_aug, h->h_aug, h->Bc, h->tokc};
+                  h->d_loss, h->in_H, h->in_tgt, h->w_aug, h->h_aug, h->Bc, h->tokc,
+                  h->xv, h->xt, h->nml};
   for (void* p : ptrs)
     if (p) cudaFree(p);
 }
@@ -376,6 +404,58 @@ int resident_units(int pair, int kblocks, int num_sms) {
   return n;
 }
 
+// The tensor-core rank-sum passes (CTA pairs, ranks 8..64).
+template <int kPass, int R>
+int tc_smem(int kblocks) {
+  return TcLayout::bytes(kblocks, TcLayout::stages(kblocks, R), R);
+}
+
+template <int kPass, int R>
+int resident_units_tc(int kblocks, int num_sms) {
+  const int smem = tc_smem<kPass, R>(kblocks);
+  if (TcLayout::stages(kblocks, R) < 2 || smem > kMaxDynSmem) return 0;
+  auto kern = lce_gemm_tc<kPass, R>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return 0;
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3((unsigned)num_sms);
+  lc.blockDim = dim3(kThreadsT);
+  lc.dynamicSmemBytes = (size_t)smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &lc) != cudaSuccess) return 0;
+  return n;
+}
+
+template <int kPass, int R>
+int launch_gemm_tc(const CUtensorMap& map_res, const CUtensorMap& map_str,
+                   const CUtensorMap& map_res_aug, const CUtensorMap& map_str_aug,
+                   const CUtensorMap& map_x, const GemmArgs& g, int units, cudaStream_t st) {
+  const int smem = tc_smem<kPass, R>(g.kblocks);
+  auto kern = lce_gemm_tc<kPass, R>;
+  LCE_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3((unsigned)(units * 2));
+  lc.blockDim = dim3(kThreadsT);
+  lc.dynamicSmemBytes = (size_t)smem;
+  lc.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  LCE_CUDA(cudaLaunchKernelEx(&lc, kern, map_res, map_str, map_res_aug, map_str_aug, map_x, g));
+  return 0;
+}
+
 // Co-resident units of a rank's two passes; also lets lce_prep of large
 // ranks use its d*R floats of dynamic shared memory.
 template <int R>
@@ -384,6 +464,13 @@ void plan_units(lora_ce_handle* h, int* u1, int* u2) {
   const int kb = h->d / kBK + Plan::kAugBlocks;
   *u1 = resident_units<typename Plan::EL>(h->pair, kb, h->num_sms);
   *u2 = resident_units<typename Plan::EG>(h->pair, kb, h->num_sms);
+  if constexpr (R >= 8) {
+    if (h->tc) {
+      h->units1t = resident_units_tc<1, R>(kb, h->num_sms);
+      h->units2t = resident_units_tc<2, R>(kb, h->num_sms);
+      if (h->units1t < 1 || h->units2t < 1) h->tc = false;  // the per-logit epilogues instead
+    }
+  }
   const int prep_smem = h->d * R * 4;
   if (prep_smem > 48 * 1024 &&
       cudaFuncSetAttribute(lce_prep<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem) !=
@@ -433,7 +520,10 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
   const int kblocks = kmain + Plan::kAugBlocks;  // resident and streamed K-blocks alike
   const long long Tpad = round_up(T, kBN);
   int launches = 0;
-  if (Plan::kChunked) chunks = 1;  // rank chunks: one launch per chunk of ranks instead
+  // ranks 8..64: rank sums on the tensor cores (one launch per pass at every rank)
+  const bool tc = R >= 8 && h->tc;
+  const bool rank_chunks = Plan::kChunked && !tc;
+  if (rank_chunks) chunks = 1;  // rank chunks: one launch per chunk of ranks instead
 
   CUtensorMap mapH_res, mapH_str;
   if (!make_map(&mapH_res, h->h16, T, d, kBM) || !make_map(&mapH_str, h->h16, T, d, kBN))
@@ -445,14 +535,17 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
 
   const int pair = h->pair;
   const int res_rows = kBM * pair;
-  const int n_a1 = (T + res_rows - 1) / res_rows, n_b1 = (int)(h->Vpad / kBN);
+  const int n_a1 = (T + res_rows - 1) / res_rows;
+  const int n_b1 = tc ? (V + kBNT - 1) / kBNT : (int)(h->Vpad / kBN);
+  const int units1 = tc ? h->units1t : h->units1;
   chunks = std::max(1, std::min(chunks, n_a1));
-  const int cp1 = col_parts(EL::kWarps), cp2 = col_parts(EG::kWarps);
+  const int cp1 = tc ? col_parts(kEpiWarpsT) : col_parts(EL::kWarps);
+  const int cp2 = tc ? 1 : col_parts(EG::kWarps);
   int seg1 = 0;
   for (int c = 0; c < chunks; ++c) {
     const int na = (int)(tile_start(c + 1, n_a1, chunks) - tile_start(c, n_a1, chunks));
     const long long tot = (long long)na * n_b1;
-    seg1 = std::max(seg1, cp1 * max_segments(na, n_b1, (int)std::min<long long>(h->units1, tot)));
+    seg1 = std::max(seg1, cp1 * max_segments(na, n_b1, (int)std::min<long long>(units1, tot)));
   }
   const long long stride1 = (long long)n_a1 * res_rows;
   if ((long long)seg1 * stride1 > h->p1_cap)
@@ -477,6 +570,8 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
   g.z_tgt = h->z_tgt;
   g.gBp = h->gBp;
   g.Tcap = stride1;
+  g.stages = tc ? TcLayout::stages(kblocks, R) : 0;
+  g.nml = h->nml;
 
   mark(h, kPhPrep);
   float* const Bfull = h->params + (long long)d * R;
@@ -485,8 +580,15 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
     const int groups = Plan::kAugWidth / 8;
     const int blocks = (int)std::min<long long>((h->Vpad * groups + 255) / 256, 8LL * h->num_sms);
     lce_aug_b<R><<<blocks, 256, 0, st>>>(Bfull, h->Vpad, h->w_aug, Plan::kLayout, Plan::kAugWidth,
-                                         Plan::kChunked ? h->Bc : nullptr, Bc_stride);
+                                         rank_chunks ? h->Bc : nullptr, Bc_stride);
     ++launches;
+  }
+  if constexpr (R >= 8) {
+    if (tc) {  // pass 1's rank operand B^T [hi ; lo]
+      const int blocks = (int)std::min<long long>(((long long)V * R + 255) / 256, 8LL * h->num_sms);
+      lce_xt_vocab<R><<<blocks, 256, 0, st>>>(V, h->Vpad, Bfull, h->xv);
+      ++launches;
+    }
   }
   // 1. per chunk of position blocks: convert h, U = h.A, per-position
   //    records; 2. pass 1 on those positions (per-position max / sum / q)
@@ -501,7 +603,7 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
       lce_prep<R><<<blocks, threads, (size_t)d * R * 4, st>>>(
           dH, dtype, t_lo, t_hi, T, d, h->params, h->cfg.scale, dtg, V, h->h16, h->tok, h->err,
           kAug ? h->h_aug : nullptr, Plan::kLayout, Plan::kAugWidth,
-          Plan::kChunked ? h->tokc : nullptr, tokc_stride);
+          rank_chunks ? h->tokc : nullptr, tokc_stride);
       ++launches;
     }
     if (c == 0) mark(h, kPhPass1);
@@ -509,7 +611,16 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
     g.n_a = a_hi - a_lo;
     g.n_b = n_b1;
     const long long tot = (long long)g.n_a * n_b1;
-    const int Gc = (int)std::min<long long>(h->units1, tot);
+    const int Gc = (int)std::min<long long>(units1, tot);
+    if constexpr (R >= 8) {
+      if (tc) {
+        int rc = launch_gemm_tc<1, R>(mapH_res, h->mapW_strT, mapHa_res, h->mapWa_strT, h->mapXv,
+                                      g, Gc, st);
+        if (rc) return rc;
+        ++launches;
+        continue;
+      }
+    }
     for (int rc0 = 0; rc0 < R; rc0 += kRC) {  // rank chunks (one pass below rank 32)
       g.rank_off = rc0;
       g.Bt = Plan::kChunked ? h->Bc + (rc0 / 16) * Bc_stride : Bfull;
@@ -524,28 +635,49 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
   g.Bt = Bfull;
   // 3. merge partials -> M, 1/S, loss_t, dU
   mark(h, kPhCombine);
-  lce_combine<R><<<(T + 7) / 8, 256, 0, st>>>(T, cp1, res_rows, n_b1, h->units1, chunks, stride1,
+  lce_combine<R><<<(T + 7) / 8, 256, 0, st>>>(T, cp1, res_rows, n_b1, units1, chunks, stride1,
                                                   h->p_max,
                                                   h->p_sum,
                                                   h->p_q, h->z_tgt, Bfull, h->cfg.scale, h->tok,
                                                   h->dU, h->loss_tok,
-                                                  Plan::kChunked ? h->tokc : nullptr, tokc_stride);
+                                                  rank_chunks ? h->tokc : nullptr, tokc_stride);
   ++launches;
   // onehot part of dB (order-independent fixed-point sums)
   lce_onehot<R><<<(T + 63) / 64, 64, 0, st>>>(T, h->tok, h->corr_fx, h->err);
   ++launches;
   // 4. pass 2: dB per vocab row
-  const int n_a2 = (V + res_rows - 1) / res_rows, n_b2 = (int)(Tpad / kBN);
+  const int n_a2 = (V + res_rows - 1) / res_rows;
+  const int n_b2 = tc ? (T + kBNT - 1) / kBNT : (int)(Tpad / kBN);
   const long long total2 = (long long)n_a2 * n_b2;
-  const int G2 = (int)std::min<long long>(h->units2, total2);
+  const int G2 = (int)std::min<long long>(tc ? h->units2t : h->units2, total2);
   if (cp2 * max_segments(n_a2, n_b2, G2) > h->gbp_segs)
     return fail(LORA_CE_ESTATE, "pass-2 partial buffer too small");
+  if constexpr (R >= 8) {
+    if (tc) {  // pass 2's rank operand (s*U)^T [hi ; lo] and exponent offsets
+      const int blocks = (int)std::min<long long>(((long long)T * R + 255) / 256, 8LL * h->num_sms);
+      lce_xt_pos<R><<<blocks, 256, 0, st>>>(T, h->Tcap, h->tok, h->xt, h->nml);
+      ++launches;
+    }
+  }
   mark(h, kPhPass2);
   g.n_a = n_a2;
   g.n_b = n_b2;
-  for (int rc0 = 0; rc0 < R; rc0 += kRC) {  // rank chunks: their own position records
+  if constexpr (R >= 8) {
+    if (tc) {
+      CUtensorMap mapH_strT, mapHa_strT, mapXt;
+      if (!make_map(&mapH_strT, h->h16, T, d, kStRowsT) ||
+          !make_map(&mapHa_strT, h->h_aug, T, Plan::kAugWidth, kStRowsT) ||
+          !make_map_ld(&mapXt, h->xt, 2 * R, T, h->Tcap, R))
+        return fail(LORA_CE_ECUDA, "cuTensorMapEncodeTiled failed for pass 2");
+      int rc = launch_gemm_tc<2, R>(h->mapW_res, mapH_strT, h->mapWa_res, mapHa_strT, mapXt, g,
+                                    G2, st);
+      if (rc) return rc;
+      ++launches;
+    }
+  }
+  for (int rc0 = 0; rc0 < R && !tc; rc0 += kRC) {  // rank chunks: their own position records
     g.rank_off = rc0;
-    g.tok = Plan::kChunked ? h->tokc + (rc0 / 16) * tokc_stride : h->tok;
+    g.tok = rank_chunks ? h->tokc + (rc0 / 16) * tokc_stride : h->tok;
     int rc = launch_gemm<EG>(h->mapW_res, pair == 2 ? mapH_res : mapH_str, h->mapWa_res,
                              pair == 2 ? mapHa_res : mapHa_str, g, G2, pair, kblocks, st);
     if (rc) return rc;
@@ -835,6 +967,12 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
     h->pair = (e && e[0] == '1') ? 1 : 2;
     const char* gr = getenv("LORA_CE_GRAPHS");  // "0": launch every step directly
     h->use_graphs = !(gr && gr[0] == '0');
+    // Tensor-core rank sums from rank LCE_TC_MIN_RANK up (below it the
+    // per-logit epilogues are faster); LORA_CE_TC=0 turns them off, =1
+    // turns them on from rank 8 (comparison and parity runs).
+    const char* tc = getenv("LORA_CE_TC");
+    const int tc_min = tc && tc[0] == '1' ? 8 : LCE_TC_MIN_RANK;
+    h->tc = h->pair == 2 && h->R >= tc_min && !(tc && tc[0] == '0');
   }
   const int R = h->R, d = h->d;
   const int res_rows = kBM * h->pair;
@@ -872,11 +1010,31 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
       }
     }
     p1 = std::max<long long>(p1, (long long)col_parts(16) * seg * n_a1 * res_rows);
+    if (h->tc) {  // 192-column vocab tiles
+      const int n_b1t = (int)((V + kBNT - 1) / kBNT);
+      int segt = 0;
+      for (int chunks : {1, step_chunks(n_a1)}) {
+        for (int c = 0; c < chunks; ++c) {
+          const int na = (int)(tile_start(c + 1, n_a1, chunks) - tile_start(c, n_a1, chunks));
+          const long long total = (long long)na * n_b1t;
+          const int G = (int)std::min<long long>(h->units1t, total);
+          segt = std::max(segt, max_segments(na, n_b1t, G));
+        }
+      }
+      p1 = std::max<long long>(p1, (long long)col_parts(kEpiWarpsT) * segt * n_a1 * res_rows);
+    }
   }
   for (int n_b2 = 1; (long long)n_b2 * kBN <= Tcap; ++n_b2) {
     const long long total = (long long)n_a2 * n_b2;
     const int G = (int)std::min<long long>(h->units2, total);
     s2 = std::max(s2, col_parts(16) * max_segments(n_a2, n_b2, G));
+  }
+  if (h->tc) {  // 192-column position tiles, one slot per segment
+    for (int n_b2 = 1; (long long)(n_b2 - 1) * kBNT < Tcap; ++n_b2) {
+      const long long total = (long long)n_a2 * n_b2;
+      const int G = (int)std::min<long long>(h->units2t, total);
+      s2 = std::max(s2, max_segments(n_a2, n_b2, G));
+    }
   }
   h->p1_cap = p1;
   h->gbp_segs = s2;
@@ -909,8 +1067,11 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
   const bool aug = aug_width > 0;
   if (!rc && aug) rc = dalloc(&h->w_aug, (size_t)Vpad * aug_width);
   if (!rc && aug) rc = dalloc(&h->h_aug, (size_t)Tcap * aug_width);
-  if (!rc && R > 16) rc = dalloc(&h->Bc, (size_t)(R / 16) * Vpad * 16);
-  if (!rc && R > 16) rc = dalloc(&h->tokc, (size_t)(R / 16) * Tcap * kChunkRec);
+  if (!rc && R > 16 && !h->tc) rc = dalloc(&h->Bc, (size_t)(R / 16) * Vpad * 16);
+  if (!rc && R > 16 && !h->tc) rc = dalloc(&h->tokc, (size_t)(R / 16) * Tcap * kChunkRec);
+  if (!rc && h->tc) rc = dalloc(&h->xv, (size_t)2 * R * Vpad);
+  if (!rc && h->tc) rc = dalloc(&h->xt, (size_t)2 * R * Tcap);
+  if (!rc && h->tc) rc = dalloc(&h->nml, (size_t)Tcap + kBNT);
   if (!rc && (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess ||
               cudaStreamCreateWithFlags(&h->cstream, cudaStreamNonBlocking) != cudaSuccess))
     rc = fail(LORA_CE_ECUDA, "cudaStreamCreate failed");
@@ -926,6 +1087,11 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
   if (!rc && aug && !(make_map(&h->mapWa_res, h->w_aug, V, aug_width, kBM) &&
                        make_map(&h->mapWa_str, h->w_aug, V, aug_width, kBN)))
     rc = fail(LORA_CE_ECUDA, "cuTensorMapEncodeTiled failed for the rank augmentation");
+  if (!rc && h->tc &&
+      !(make_map(&h->mapW_strT, h->W, V, d, kStRowsT) &&
+        make_map(&h->mapWa_strT, h->w_aug, V, aug_width, kStRowsT) &&
+        make_map_ld(&h->mapXv, h->xv, 2 * R, V, Vpad, R)))
+    rc = fail(LORA_CE_ECUDA, "cuTensorMapEncodeTiled failed for the tensor-core rank sums");
   if (!aug) {  // never read without augmentation; any valid map fills the kernel parameter
     h->mapWa_res = h->mapW_res;
     h->mapWa_str = h->mapW_str;

@@ -140,6 +140,9 @@ struct GemmArgs {
   float* z_tgt;       // [Tcap]
   // pass 2
   float* gBp;         // [seg][Vpad][R]
+  // tensor-core rank sums (lce_gemm_tc)
+  int stages;         // streamed-operand ring stages
+  const float* nml;   // pass 2: per position -M*log2(e) + log2(1/S) + 14
 };
 
 // Dynamic shared memory: [resident K-blocks | streamed ring (ring bytes) | staged

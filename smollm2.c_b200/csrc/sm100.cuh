@@ -82,6 +82,35 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   }
 }
 
+// mbar_wait with cluster-scope acquire: for phases completed by the peer
+// CTA's release arrivals (mbar_arrive_cluster_release).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err,
+                                                  int code) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((i & 31) == 0) {
+      if (*(volatile int*)err != 0) return false;
+      if (globaltimer() - t0 > kWaitTimeoutNs) {
+        atomicCAS(err, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
 // Cluster helpers (CTA pairs for the 2-SM MMA).
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -104,6 +133,14 @@ __device__ __forceinline__ void cluster_sync() {
 // tcgen05.wait::ld + tcgen05.fence::before_thread_sync provide.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+
+// Release at cluster scope: this thread's earlier writes (and, after
+// tcgen05.wait::st + tcgen05.fence::before_thread_sync, its TMEM stores) are
+// visible to a thread of either CTA that observes the phase.
+__device__ __forceinline__ void mbar_arrive_cluster_release(uint32_t caddr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr)
+               : "memory");
 }
 
 // ---------------------------------------------------------------- TMA
@@ -197,6 +234,17 @@ __device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t adesc, u
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
+// 2-SM MMA with A in tensor memory: D[tmem] (+)= A[tmem] . B[smem]^T.  A's
+// 128 rows per CTA are the TMEM lanes at a_tmem (same address in both CTAs),
+// two f16 K-elements per 32-bit column, the lower K index in the low half.
+__device__ __forceinline__ void umma_f16_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
 // Arrive on the mbarrier at the same offset in every CTA of `cta_mask` once
 // the leader's previously issued MMAs have completed (a commit, not a load).
 __device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
@@ -282,6 +330,31 @@ __device__ __forceinline__ void tmem_ld_wait(float (&v)[N]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < N; ++i) asm volatile("" : "+f"(v[i]));
+}
+
+// 32 lanes x N consecutive 32-bit columns from registers (N = 8 or 16);
+// complete (visible to later tcgen05 operations) after tmem_st_wait().
+template <int N>
+__device__ __forceinline__ void tmem_st(uint32_t taddr, const uint32_t (&r)[N]) {
+  if constexpr (N == 8) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(
+            taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+        : "memory");
+  } else {
+    static_assert(N == 16, "tmem_st width");
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+        "r"(r[15])
+        : "memory");
+  }
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {

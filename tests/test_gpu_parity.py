@@ -90,6 +90,26 @@ def test_step_matches_oracle(oracle, V, d, r, T, dtype):
     run_case(oracle, V, d, r, T, seed=V + T + r, dtype=dtype, steps=2)
 
 
+@pytest.mark.parametrize("tc", ["0", "1"])
+@pytest.mark.parametrize(
+    "V,d,r,T,dtype",
+    [
+        (1000, 64, 8, 300, "f32"),
+        (2048, 576, 13, 100, "bf16"),
+        (2048, 576, 16, 513, "bf16"),
+        (4099, 128, 32, 300, "bf16"),   # vocabulary and positions off both tile grids
+        (3000, 192, 20, 77, "f16"),
+        (49152, 576, 64, 300, "bf16"),
+    ],
+)
+def test_step_matches_oracle_both_rank_paths(oracle, monkeypatch, tc, V, d, r, T, dtype):
+    """Ranks 8..64 down both paths: the tensor-core rank sums (LORA_CE_TC=1
+    uses them from rank 8) and the per-logit epilogues with rank chunks
+    above 16 (LORA_CE_TC=0)."""
+    monkeypatch.setenv("LORA_CE_TC", tc)
+    run_case(oracle, V, d, r, T, seed=V + T + r + 1, dtype=dtype, steps=2)
+
+
 def test_adamw_and_clip_extensions(oracle):
     run_case(oracle, 49152, 576, 4, 300, seed=77, wd=0.01, clip=1.0, steps=2)
     run_case(oracle, 3000, 128, 4, 50, seed=78, wd=0.01, clip=1e-4, steps=1)  # clip active
