@@ -476,6 +476,11 @@ void plan_units(lora_ce_handle* h, int* u1, int* u2) {
       cudaFuncSetAttribute(lce_prep<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem) !=
           cudaSuccess)
     *u1 = 0;
+  if constexpr (R >= 16) {
+    if (cudaFuncSetAttribute(lce_prep_wide<R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             prep_wide_smem(R, h->d)) != cudaSuccess)
+      *u1 = 0;
+  }
 }
 
 // Launch one GEMM pass: `units` tile-range owners (CTAs, or 2-CTA clusters).
@@ -597,7 +602,16 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
     const int t_lo = a_lo * res_rows;
     const int t_hi = c + 1 == chunks ? (int)Tpad : a_hi * res_rows;  // last chunk pads to Tpad
     if (chunk_ready) LCE_CUDA(cudaStreamWaitEvent(st, chunk_ready[c], 0));
-    {
+    if constexpr (R >= 16) {  // lanes over ranks, one block per SM
+      const int per_block = kPrepWarps * prep_wide_rows(R);
+      const int blocks = (int)std::min<long long>((t_hi - t_lo + per_block - 1) / per_block,
+                                                  h->num_sms);
+      lce_prep_wide<R><<<blocks, 32 * kPrepWarps, (size_t)prep_wide_smem(R, d), st>>>(
+          dH, dtype, t_lo, t_hi, T, d, h->params, h->cfg.scale, dtg, V, h->h16, h->tok, h->err,
+          kAug ? h->h_aug : nullptr, Plan::kLayout, Plan::kAugWidth,
+          rank_chunks ? h->tokc : nullptr, tokc_stride);
+      ++launches;
+    } else {
       const int threads = 256;  // 8 warps per block, grid-stride over positions
       const int blocks = (int)std::min<long long>((t_hi - t_lo + 7) / 8, 4LL * h->num_sms);
       lce_prep<R><<<blocks, threads, (size_t)d * R * 4, st>>>(

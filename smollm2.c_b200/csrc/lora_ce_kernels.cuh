@@ -934,6 +934,138 @@ __global__ void lce_prep(const void* __restrict__ H, int dtype, int t_lo, int t_
   }
 }
 
+// lce_prep for ranks 16..64: the same outputs, computed with lanes over
+// ranks instead of over d (the d-strided reads of A rows conflict on
+// every shared-memory bank once a row is 64 B or more, and the warp-wide
+// reduction of R sums costs 5R shuffles).  A warp takes kPrepQ * 64/R
+// positions at a time: it converts their h rows (f16 out, the f16 values
+// kept as f32 in shared memory), then lane (g, jp) accumulates
+// U[g*kPrepQ + q][2jp, 2jp+1] for its kPrepQ positions, reading A[i][2jp..]
+// (consecutive across lanes) and h[.][i..i+3] (one row per lane group).
+constexpr int kPrepQ = 4;
+constexpr int kPrepWarps = 4;
+__host__ __device__ constexpr int prep_wide_rows(int R) { return kPrepQ * 64 / R; }
+__host__ __device__ constexpr int prep_wide_smem(int R, int d) {
+  return d * R * 4 + kPrepWarps * prep_wide_rows(R) * (d + 4) * 4;
+}
+template <int R>
+__global__ void __launch_bounds__(32 * kPrepWarps)
+    lce_prep_wide(const void* __restrict__ H, int dtype, int t_lo, int t_hi, int T, int d,
+                  const float* __restrict__ A, float scale, const int32_t* __restrict__ targets,
+                  int V, __half* __restrict__ h16, float* __restrict__ tok, int* err,
+                  __half* __restrict__ haug, int aug_layout, int aug_width,
+                  float* __restrict__ tokc, long long tokc_stride) {
+  static_assert(R >= 16 && R <= 64, "wide prep: ranks 16..64");
+  constexpr int NP = prep_wide_rows(R);  // positions per warp batch
+  constexpr int kLanesPer = R / 2;       // lanes per position group
+  extern __shared__ __align__(16) float smem_f[];
+  float* sA = smem_f;  // [d][R]
+  const int ldh = d + 4;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* sh = smem_f + d * R + warp * NP * ldh;  // [NP][d + 4]
+  for (int k = threadIdx.x; k < d * R; k += blockDim.x) sA[k] = A[k];
+  __syncthreads();
+  const int g = lane / kLanesPer, jp = lane % kLanesPer;
+  const int nwarps = gridDim.x * kPrepWarps;
+  for (int w0 = t_lo + (blockIdx.x * kPrepWarps + warp) * NP; w0 < t_hi; w0 += nwarps * NP) {
+    // convert this batch's rows (positions >= T read as zero rows)
+    for (int p = 0; p < NP; ++p) {
+      const int w = w0 + p;
+      for (int i = 2 * lane; i < d; i += 64) {
+        float2 hf = make_float2(0.f, 0.f);
+        if (w < T && w < t_hi) {
+          const long long o = (long long)w * d + i;
+          float2 x;
+          if (dtype == 0) x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(
+                              reinterpret_cast<const __nv_bfloat16*>(H) + o));
+          else if (dtype == 1) x = __half22float2(*reinterpret_cast<const __half2*>(
+                                   reinterpret_cast<const __half*>(H) + o));
+          else x = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(H) + o);
+          const __half2 hv = __floats2half2_rn(x.x, x.y);
+          *reinterpret_cast<__half2*>(h16 + o) = hv;
+          hf = __half22float2(hv);
+        }
+        *reinterpret_cast<float2*>(sh + p * ldh + i) = hf;
+      }
+    }
+    __syncwarp();
+    float2 acc[kPrepQ];
+#pragma unroll
+    for (int q = 0; q < kPrepQ; ++q) acc[q] = make_float2(0.f, 0.f);
+    const float* hrow = sh + g * kPrepQ * ldh;
+#pragma unroll 2
+    for (int i = 0; i < d; i += 4) {
+      float2 a[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) a[k] = *reinterpret_cast<const float2*>(sA + (i + k) * R + 2 * jp);
+#pragma unroll
+      for (int q = 0; q < kPrepQ; ++q) {
+        const float4 hv = *reinterpret_cast<const float4*>(hrow + q * ldh + i);
+        acc[q].x = fmaf(hv.x, a[0].x, acc[q].x);
+        acc[q].y = fmaf(hv.x, a[0].y, acc[q].y);
+        acc[q].x = fmaf(hv.y, a[1].x, acc[q].x);
+        acc[q].y = fmaf(hv.y, a[1].y, acc[q].y);
+        acc[q].x = fmaf(hv.z, a[2].x, acc[q].x);
+        acc[q].y = fmaf(hv.z, a[2].y, acc[q].y);
+        acc[q].x = fmaf(hv.w, a[3].x, acc[q].x);
+        acc[q].y = fmaf(hv.w, a[3].y, acc[q].y);
+      }
+    }
+    __syncwarp();  // the batch's rows are read before the next batch overwrites them
+#pragma unroll
+    for (int q = 0; q < kPrepQ; ++q) {
+      const int w = w0 + g * kPrepQ + q;
+      if (w >= t_hi) continue;
+      const bool pad = w >= T;
+      const int j0 = 2 * jp;
+      const float su0 = pad ? 0.f : scale * acc[q].x, su1 = pad ? 0.f : scale * acc[q].y;
+      tok[tidx(w, j0, R)] = su0;
+      tok[tidx(w, j0 + 1, R)] = su1;
+      if (jp == 0) {
+        int tg = -1;
+        if (!pad) {
+          tg = targets[w];
+          if (tg < 0 || tg >= V) {
+            atomicCAS(err, 0, kErrTarget);
+            tg = 0;
+          }
+        }
+        tok[tidx(w, R, R)] = 0.f;
+        tok[tidx(w, R + 1, R)] = 0.f;
+        tok[tidx(w, R + 2, R)] = __int_as_float(tg);
+        tok[tidx(w, R + 3, R)] = 0.f;
+      }
+      if (haug) {
+        const __half h0 = __float2half_rn(su0), h1 = __float2half_rn(su1);
+        const __half2 hi = __halves2half2(h0, h1);
+        const __half2 lo = __floats2half2_rn(su0 - __half2float(h0), su1 - __half2float(h1));
+        __half* row = haug + (long long)w * aug_width;
+        if (aug_layout == 1) {  // [sU_hi | sU_hi | sU_lo | 0]
+          *reinterpret_cast<__half2*>(row + j0) = hi;
+          *reinterpret_cast<__half2*>(row + R + j0) = hi;
+          *reinterpret_cast<__half2*>(row + 2 * R + j0) = lo;
+          for (int c = 3 * R + j0; c < aug_width; c += R)
+            *reinterpret_cast<__half2*>(row + c) = __floats2half2_rn(0.f, 0.f);
+        } else {  // [sU_hi | sU_lo | 0]
+          *reinterpret_cast<__half2*>(row + j0) = hi;
+          *reinterpret_cast<__half2*>(row + R + j0) = lo;
+          for (int c = 2 * R + j0; c < aug_width; c += R)
+            *reinterpret_cast<__half2*>(row + c) = __floats2half2_rn(0.f, 0.f);
+        }
+      }
+      if (tokc) {  // rank chunks of 16: sU of the chunk; M, 1/S come from lce_combine
+        const int c = j0 / 16, f = j0 % 16;
+        tokc[c * tokc_stride + crec_idx(w, f)] = su0;
+        tokc[c * tokc_stride + crec_idx(w, f + 1)] = su1;
+        if (jp < R / 16) {
+          tokc[jp * tokc_stride + crec_idx(w, 16)] = 0.f;
+          tokc[jp * tokc_stride + crec_idx(w, 17)] = 0.f;
+        }
+      }
+    }
+  }
+}
+
 // The vocabulary side of rank augmentation, rebuilt at the start of every
 // step from the current B (rows >= V are zero like B): layout 1
 // waug[v] = [B_hi | B_lo | B_hi | 0] (ranks <= 21, one 64-wide block),
