@@ -943,13 +943,19 @@ __global__ void lce_prep(const void* __restrict__ H, int dtype, int t_lo, int t_
 // U[g*kPrepQ + q][2jp, 2jp+1] for its kPrepQ positions, reading A[i][2jp..]
 // (consecutive across lanes) and h[.][i..i+3] (one row per lane group).
 constexpr int kPrepQ = 4;
-constexpr int kPrepWarps = 4;
+constexpr int kPrepMaxWarps = 8;
 __host__ __device__ constexpr int prep_wide_rows(int R) { return kPrepQ * 64 / R; }
+// Warps per block: as many as fit beside A in shared memory, up to 8.
+__host__ __device__ constexpr int prep_wide_warps(int R, int d) {
+  return (kMaxDynSmem - d * R * 4) / (prep_wide_rows(R) * (d + 4) * 4) < kPrepMaxWarps
+             ? (kMaxDynSmem - d * R * 4) / (prep_wide_rows(R) * (d + 4) * 4)
+             : kPrepMaxWarps;
+}
 __host__ __device__ constexpr int prep_wide_smem(int R, int d) {
-  return d * R * 4 + kPrepWarps * prep_wide_rows(R) * (d + 4) * 4;
+  return d * R * 4 + prep_wide_warps(R, d) * prep_wide_rows(R) * (d + 4) * 4;
 }
 template <int R>
-__global__ void __launch_bounds__(32 * kPrepWarps)
+__global__ void __launch_bounds__(32 * kPrepMaxWarps)
     lce_prep_wide(const void* __restrict__ H, int dtype, int t_lo, int t_hi, int T, int d,
                   const float* __restrict__ A, float scale, const int32_t* __restrict__ targets,
                   int V, __half* __restrict__ h16, float* __restrict__ tok, int* err,
@@ -966,26 +972,33 @@ __global__ void __launch_bounds__(32 * kPrepWarps)
   for (int k = threadIdx.x; k < d * R; k += blockDim.x) sA[k] = A[k];
   __syncthreads();
   const int g = lane / kLanesPer, jp = lane % kLanesPer;
-  const int nwarps = gridDim.x * kPrepWarps;
-  for (int w0 = t_lo + (blockIdx.x * kPrepWarps + warp) * NP; w0 < t_hi; w0 += nwarps * NP) {
-    // convert this batch's rows (positions >= T read as zero rows)
-    for (int p = 0; p < NP; ++p) {
-      const int w = w0 + p;
-      for (int i = 2 * lane; i < d; i += 64) {
-        float2 hf = make_float2(0.f, 0.f);
+  const int warps_blk = blockDim.x >> 5;
+  const int nwarps = gridDim.x * warps_blk;
+  for (int w0 = t_lo + (blockIdx.x * warps_blk + warp) * NP; w0 < t_hi; w0 += nwarps * NP) {
+    // convert this batch's rows (positions >= T read as zero rows); the NP
+    // rows' loads of one column pair are issued together
+    for (int i = 2 * lane; i < d; i += 64) {
+      float2 x[NP];
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        const int w = w0 + p;
+        x[p] = make_float2(0.f, 0.f);
         if (w < T && w < t_hi) {
           const long long o = (long long)w * d + i;
-          float2 x;
-          if (dtype == 0) x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(
+          if (dtype == 0) x[p] = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(
                               reinterpret_cast<const __nv_bfloat16*>(H) + o));
-          else if (dtype == 1) x = __half22float2(*reinterpret_cast<const __half2*>(
+          else if (dtype == 1) x[p] = __half22float2(*reinterpret_cast<const __half2*>(
                                    reinterpret_cast<const __half*>(H) + o));
-          else x = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(H) + o);
-          const __half2 hv = __floats2half2_rn(x.x, x.y);
-          *reinterpret_cast<__half2*>(h16 + o) = hv;
-          hf = __half22float2(hv);
+          else x[p] = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(H) + o);
         }
-        *reinterpret_cast<float2*>(sh + p * ldh + i) = hf;
+      }
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        const int w = w0 + p;
+        const __half2 hv = __floats2half2_rn(x[p].x, x[p].y);
+        if (w < T && w < t_hi)
+          *reinterpret_cast<__half2*>(h16 + (long long)w * d + i) = hv;
+        *reinterpret_cast<float2*>(sh + p * ldh + i) = __half22float2(hv);
       }
     }
     __syncwarp();

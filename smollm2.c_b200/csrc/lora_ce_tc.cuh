@@ -41,7 +41,7 @@ namespace lce {
 
 constexpr int kBNT = 128;                      // streamed rows per tile
 constexpr int kStRowsT = kBNT / 2;             // per CTA of the pair
-constexpr int kBlkBytesT = kStRowsT * kBK * 2; // 8 KB: one streamed K-block per CTA
+constexpr int kStBytesT = kStRowsT * kBK * 2;  // 8 KB ring stage
 constexpr int kMaxStT = 8;
 constexpr int kXBlocksT = kBNT / kBK;          // K-blocks of the rank product per tile
 constexpr int kEpiWarpsT = 8;                  // two per TMEM lane quarter
@@ -77,23 +77,18 @@ enum : int {
 // buffers x 2 K-blocks of R rows) | max exchange (2 x 2 x 128 floats) |
 // barriers | TMEM slot].  Rank 64 keeps one rank-operand buffer, so that
 // its ring still has 4 stages beside 11 resident K-blocks.
-// A ring stage holds kps K-blocks (2 below rank 64, so that every stage
-// carries 8 MMAs of work against its barrier round trip; rank 64 keeps
-// 1-block stages, the only way to have 4 of them).
 struct TcLayout {
   static __host__ __device__ constexpr int xbufs(int R) { return R >= 64 ? 1 : 2; }
-  static __host__ __device__ constexpr int kps(int R) { return R >= 64 ? 1 : 2; }
-  static __host__ __device__ constexpr int stage_bytes(int R) { return kps(R) * kBlkBytesT; }
   static __host__ __device__ constexpr int ring_off(int kblocks) { return kblocks * kAKBytes; }
-  static __host__ __device__ constexpr int x_off(int kblocks, int stages, int R) {
-    return ring_off(kblocks) + stages * stage_bytes(R);
+  static __host__ __device__ constexpr int x_off(int kblocks, int stages) {
+    return ring_off(kblocks) + stages * kStBytesT;
   }
   static __host__ __device__ constexpr int x_kblock_bytes(int R) { return R * 128; }
   static __host__ __device__ constexpr int x_buf_bytes(int R) {
     return kXBlocksT * x_kblock_bytes(R);
   }
   static __host__ __device__ constexpr int xch_off(int kblocks, int stages, int R) {
-    return x_off(kblocks, stages, R) + xbufs(R) * x_buf_bytes(R);
+    return x_off(kblocks, stages) + xbufs(R) * x_buf_bytes(R);
   }
   static __host__ __device__ constexpr int bar_off(int kblocks, int stages, int R) {
     return xch_off(kblocks, stages, R) + 2 * 2 * kBM * 4;
@@ -103,8 +98,8 @@ struct TcLayout {
   }
   // the most ring stages that fit beside the rest
   static __host__ __device__ constexpr int stages(int kblocks, int R) {
-    return (kMaxDynSmem - bytes(kblocks, 0, R)) / stage_bytes(R) < kMaxStT
-               ? (kMaxDynSmem - bytes(kblocks, 0, R)) / stage_bytes(R)
+    return (kMaxDynSmem - bytes(kblocks, 0, R)) / kStBytesT < kMaxStT
+               ? (kMaxDynSmem - bytes(kblocks, 0, R)) / kStBytesT
                : kMaxStT;
   }
 };
@@ -160,8 +155,6 @@ __global__ void __launch_bounds__(kThreadsT, 1)
   constexpr int kXKB = TcLayout::x_kblock_bytes(R);
   constexpr int kXBuf = TcLayout::x_buf_bytes(R);
   constexpr int kXN = TcLayout::xbufs(R);
-  constexpr int kKPS = TcLayout::kps(R);
-  constexpr int kSB = TcLayout::stage_bytes(R);
   constexpr int kResRows = 2 * kBM;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const int kSt = g.stages;
@@ -178,7 +171,7 @@ __global__ void __launch_bounds__(kThreadsT, 1)
   uint8_t* smem = smem_raw + pad;
   uint8_t* sA = smem;
   uint8_t* sB = smem + TcLayout::ring_off(g.kblocks);
-  uint8_t* sX = smem + TcLayout::x_off(g.kblocks, kSt, R);
+  uint8_t* sX = smem + TcLayout::x_off(g.kblocks, kSt);
   float* xch = reinterpret_cast<float*>(smem + TcLayout::xch_off(g.kblocks, kSt, R));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TcLayout::bar_off(g.kblocks, kSt, R));
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kTNumBars);
@@ -260,20 +253,16 @@ __global__ void __launch_bounds__(kThreadsT, 1)
           ++a_uses;
         }
         const int srow0 = b * kBNT + (int)rank * kStRowsT;
-        for (int kb0 = 0; kb0 < g.kstr; kb0 += kKPS) {
+        for (int kb = 0; kb < g.kstr; ++kb) {
           if (!mbar_wait(&bars[kTEmpty + stage], phase ^ 1, g.err, kErrWaitProducer)) {
             ok = false;
             break;
           }
-          const int nblk = g.kstr - kb0 < kKPS ? g.kstr - kb0 : kKPS;
-          if (leader) mbar_expect_tx(&bars[kTFull + stage], (uint32_t)(2 * nblk * kBlkBytesT));
-          for (int j = 0; j < nblk; ++j) {
-            const int kb = kb0 + j;
-            const CUtensorMap* m = kb < g.kmain ? &map_str : &map_str_aug;
-            const int kx = (kb < g.kmain ? kb : kb - g.kmain) * kBK;
-            tma_load_2d_pair(sB + stage * kSB + j * kBlkBytesT, m,
-                             mapa_shared(smem_u32(&bars[kTFull + stage]), 0), kx, srow0);
-          }
+          if (leader) mbar_expect_tx(&bars[kTFull + stage], (uint32_t)(2 * kStBytesT));
+          const CUtensorMap* m = kb < g.kmain ? &map_str : &map_str_aug;
+          const int kx = (kb < g.kmain ? kb : kb - g.kmain) * kBK;
+          tma_load_2d_pair(sB + stage * kStBytesT, m,
+                           mapa_shared(smem_u32(&bars[kTFull + stage]), 0), kx, srow0);
           issued_parity[stage] = (int)phase;
           if (++stage == kSt) {
             stage = 0;
@@ -344,54 +333,51 @@ __global__ void __launch_bounds__(kThreadsT, 1)
         const int buf = (int)(li & 1);
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(buf * kBNT);
-        // Stages of kKPS K-blocks: the h.W blocks are multiplied as their
-        // stage lands; the stages holding rank-augmentation blocks (one or
-        // two, at the end of the tile) stay held until the scheduled
-        // augmentation K-steps have been issued.
-        uint32_t aug_addr[2] = {0u, 0u};
-        int held[2] = {0, 0};
-        int n_held = 0;
-        for (int kb0 = 0; kb0 < g.kstr; kb0 += kKPS) {
+        for (int kb = 0; kb < g.kmain; ++kb) {
           if (!mbar_wait(&bars[kTFull + stage], phase, g.err, kErrWaitMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const int nblk = g.kstr - kb0 < kKPS ? g.kstr - kb0 : kKPS;
-          bool has_aug = false;
-          for (int j = 0; j < nblk; ++j) {
-            const int kb = kb0 + j;
-            const uint32_t baddr = smem_u32(sB + stage * kSB + j * kBlkBytesT);
-            if (kb < g.kmain) {
-              const uint64_t adesc = sw128_kmajor_desc(smem_u32(sA + kb * kAKBytes));
-              const uint64_t bdesc = sw128_kmajor_desc(baddr);
+          const uint64_t adesc = sw128_kmajor_desc(smem_u32(sA + kb * kAKBytes));
+          const uint64_t bdesc = sw128_kmajor_desc(smem_u32(sB + stage * kStBytesT));
 #pragma unroll
-              for (int k = 0; k < kBK / 16; ++k)
-                umma_f16_pair(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k),
-                              kIdesc, (kb | k) != 0 ? 1u : 0u);
-            } else {
-              aug_addr[kb - g.kmain] = baddr;
-              has_aug = true;
-            }
+          for (int k = 0; k < kBK / 16; ++k)
+            umma_f16_pair(d_tmem, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), kIdesc,
+                          (kb | k) != 0 ? 1u : 0u);
+          umma_commit_pair(&bars[kTEmpty + stage], 0x3);
+          if (++stage == kSt) {
+            stage = 0;
+            phase ^= 1;
           }
-          if (has_aug) held[n_held++] = stage;
-          else umma_commit_pair(&bars[kTEmpty + stage], 0x3);
+        }
+        const int n_str_aug = g.kstr - g.kmain;
+        int aug_stage[2] = {0, 0};
+        for (int i = 0; i < n_str_aug && ok; ++i) {
+          if (!mbar_wait(&bars[kTFull + stage], phase, g.err, kErrWaitMma)) {
+            ok = false;
+            break;
+          }
+          aug_stage[i] = stage;
           if (++stage == kSt) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        if (g.kstr > g.kmain) {
+        if (n_str_aug > 0) {
+          tc_fence_after();
           for (int sidx = 0; sidx < g.n_aug; ++sidx) {
             const int ia = g.aug_a[sidx], ib = g.aug_b[sidx];
             const uint64_t adesc =
                 sw128_kmajor_desc(smem_u32(sA + (g.kmain + (ia >> 2)) * kAKBytes)) +
                 (uint64_t)(2 * (ia & 3));
-            const uint64_t bdesc = sw128_kmajor_desc(aug_addr[ib >> 2]) + (uint64_t)(2 * (ib & 3));
+            const uint64_t bdesc =
+                sw128_kmajor_desc(smem_u32(sB + aug_stage[ib >> 2] * kStBytesT)) +
+                (uint64_t)(2 * (ib & 3));
             umma_f16_pair(d_tmem, adesc, bdesc, kIdesc, 1u);
           }
-          for (int i = 0; i < n_held; ++i) umma_commit_pair(&bars[kTEmpty + held[i]], 0x3);
+          for (int i = 0; i < n_str_aug; ++i) umma_commit_pair(&bars[kTEmpty + aug_stage[i]], 0x3);
         }
         const bool last_of_a = x + 1 == x_end || (int)((x + 1) / g.n_b) != a;
         umma_commit_pair(&bars[kTZFull + buf], 0x3);
