@@ -671,8 +671,8 @@ def main():
     traffic = None
     tp = os.path.join(REPO, "profiles", "traffic.json")
     if os.path.exists(tp):
-        with open(tp) as f:
-            traffic = json.load(f).get(dom)
+        with open(tp) as f:  # per workload: the GEMM passes' DRAM bytes per launch
+            traffic = json.load(f).get(f"config{args.config}", {}).get(dom)
 
     # end to end through the public API with pinned host buffers
     hH = torch.from_numpy(h.view(np.int16)).pin_memory()
