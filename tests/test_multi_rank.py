@@ -29,9 +29,9 @@ def free_port() -> int:
         return s.getsockname()[1]
 
 
-def inputs():
+def inputs(r=R):
     W = wl.make_weight(61, V, D)
-    h, tgt, A, B = wl.make_step_inputs(61, T_TOTAL, V, D, R)
+    h, tgt, A, B = wl.make_step_inputs(61, T_TOTAL, V, D, r)
     return W, h, tgt, A, B
 
 
@@ -88,11 +88,11 @@ def test_gloo_two_ranks_reproduce_single_process_step(oracle):
         np.testing.assert_array_equal(out[0][k], out[1][k])
 
 
-def _gpu_rank(rank, world, uid_path, out):
+def _gpu_rank(rank, world, uid_path, out, r):
     import time
     import lora_ce
-    W, h, tgt, A, B = inputs()
-    m = lora_ce.LoraCE(lora_ce.default_config(D, V, R, T_TOTAL, scale=SCALE, lr=LR,
+    W, h, tgt, A, B = inputs(r)
+    m = lora_ce.LoraCE(lora_ce.default_config(D, V, r, T_TOTAL, scale=SCALE, lr=LR,
                                               device=rank))
     m.set_weight(W)
     m.set_adapter(A, B, 0)
@@ -118,7 +118,8 @@ def _gpu_rank(rank, world, uid_path, out):
 
 
 @pytest.mark.gpu
-def test_two_gpus_match_oracle(oracle, tmp_path):
+@pytest.mark.parametrize("r", [4, 64])  # rank 64: the tensor-core rank-sum passes
+def test_two_gpus_match_oracle(oracle, tmp_path, r):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
@@ -126,8 +127,8 @@ def test_two_gpus_match_oracle(oracle, tmp_path):
     world = 2
     mgr = mp.Manager()
     out = mgr.dict()
-    mp.spawn(_gpu_rank, args=(world, str(tmp_path / "uid"), out), nprocs=world, join=True)
-    W, h, tgt, A, B = inputs()
+    mp.spawn(_gpu_rank, args=(world, str(tmp_path / "uid"), out, r), nprocs=world, join=True)
+    W, h, tgt, A, B = inputs(r)
     ref = oracle.step(W, A, B, wl.oracle_hidden(h), tgt, SCALE, LR)
     for rank in range(world):
         r = out[rank]
