@@ -541,7 +541,7 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
   const int pair = h->pair;
   const int res_rows = kBM * pair;
   const int n_a1 = (T + res_rows - 1) / res_rows;
-  const int n_b1 = tc ? (V + kBNT - 1) / kBNT : (int)(h->Vpad / kBN);
+  const int n_b1 = tc ? (V + tc_bn(R) - 1) / tc_bn(R) : (int)(h->Vpad / kBN);
   const int units1 = tc ? h->units1t : h->units1;
   chunks = std::max(1, std::min(chunks, n_a1));
   const int cp1 = tc ? col_parts(kEpiWarpsT) : col_parts(EL::kWarps);
@@ -662,7 +662,7 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
   ++launches;
   // 4. pass 2: dB per vocab row
   const int n_a2 = (V + res_rows - 1) / res_rows;
-  const int n_b2 = tc ? (T + kBNT - 1) / kBNT : (int)(Tpad / kBN);
+  const int n_b2 = tc ? (T + tc_bn(R) - 1) / tc_bn(R) : (int)(Tpad / kBN);
   const long long total2 = (long long)n_a2 * n_b2;
   const int G2 = (int)std::min<long long>(tc ? h->units2t : h->units2, total2);
   if (cp2 * max_segments(n_a2, n_b2, G2) > h->gbp_segs)
@@ -680,8 +680,8 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
   if constexpr (R >= 8) {
     if (tc) {
       CUtensorMap mapH_strT, mapHa_strT, mapXt;
-      if (!make_map(&mapH_strT, h->h16, T, d, kStRowsT) ||
-          !make_map(&mapHa_strT, h->h_aug, T, Plan::kAugWidth, kStRowsT) ||
+      if (!make_map(&mapH_strT, h->h16, T, d, tc_bn(R) / 2) ||
+          !make_map(&mapHa_strT, h->h_aug, T, Plan::kAugWidth, tc_bn(R) / 2) ||
           !make_map_ld(&mapXt, h->xt, 2 * R, T, h->Tcap, R))
         return fail(LORA_CE_ECUDA, "cuTensorMapEncodeTiled failed for pass 2");
       int rc = launch_gemm_tc<2, R>(h->mapW_res, mapH_strT, h->mapWa_res, mapHa_strT, mapXt, g,
@@ -1026,7 +1026,7 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
     }
     p1 = std::max<long long>(p1, (long long)col_parts(16) * seg * n_a1 * res_rows);
     if (h->tc) {  // 192-column vocab tiles
-      const int n_b1t = (int)((V + kBNT - 1) / kBNT);
+      const int n_b1t = (int)((V + tc_bn(R) - 1) / tc_bn(R));
       int segt = 0;
       for (int chunks : {1, step_chunks(n_a1)}) {
         for (int c = 0; c < chunks; ++c) {
@@ -1045,7 +1045,7 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
     s2 = std::max(s2, col_parts(16) * max_segments(n_a2, n_b2, G));
   }
   if (h->tc) {  // 192-column position tiles, one slot per segment
-    for (int n_b2 = 1; (long long)(n_b2 - 1) * kBNT < Tcap; ++n_b2) {
+    for (int n_b2 = 1; (long long)(n_b2 - 1) * tc_bn(R) < Tcap; ++n_b2) {
       const long long total = (long long)n_a2 * n_b2;
       const int G = (int)std::min<long long>(h->units2t, total);
       s2 = std::max(s2, max_segments(n_a2, n_b2, G));
@@ -1086,7 +1086,7 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
   if (!rc && R > 16 && !h->tc) rc = dalloc(&h->tokc, (size_t)(R / 16) * Tcap * kChunkRec);
   if (!rc && h->tc) rc = dalloc(&h->xv, (size_t)2 * R * Vpad);
   if (!rc && h->tc) rc = dalloc(&h->xt, (size_t)2 * R * Tcap);
-  if (!rc && h->tc) rc = dalloc(&h->nml, (size_t)Tcap + kBNT);
+  if (!rc && h->tc) rc = dalloc(&h->nml, (size_t)Tcap + kMaxBNT);
   if (!rc && (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess ||
               cudaStreamCreateWithFlags(&h->cstream, cudaStreamNonBlocking) != cudaSuccess))
     rc = fail(LORA_CE_ECUDA, "cudaStreamCreate failed");
@@ -1103,8 +1103,8 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
                        make_map(&h->mapWa_str, h->w_aug, V, aug_width, kBN)))
     rc = fail(LORA_CE_ECUDA, "cuTensorMapEncodeTiled failed for the rank augmentation");
   if (!rc && h->tc &&
-      !(make_map(&h->mapW_strT, h->W, V, d, kStRowsT) &&
-        make_map(&h->mapWa_strT, h->w_aug, V, aug_width, kStRowsT) &&
+      !(make_map(&h->mapW_strT, h->W, V, d, tc_bn(R) / 2) &&
+        make_map(&h->mapWa_strT, h->w_aug, V, aug_width, tc_bn(R) / 2) &&
         make_map_ld(&h->mapXv, h->xv, 2 * R, V, Vpad, R)))
     rc = fail(LORA_CE_ECUDA, "cuTensorMapEncodeTiled failed for the tensor-core rank sums");
   if (!aug) {  // never read without augmentation; any valid map fills the kernel parameter

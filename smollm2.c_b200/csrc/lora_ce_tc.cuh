@@ -6,19 +6,20 @@
 //   pass 1  q[t][:]  = sum_v e^(z[t][v] - m_t) * B[:, v]       (for dU)
 //   pass 2  dB[v][:] = sum_t p[t][v] * s*U[t][:]                 (the p part of dB)
 // Both are products of the probability tile with a skinny matrix.  Here the
-// epilogue only turns each logit tile into probabilities, stored as f16 in a
-// TMEM buffer of their own, and the MMA warp multiplies that tile (A operand
-// in TMEM) with the matching rows of B or s*U (B operand in shared memory,
-// loaded by TMA) into a third TMEM accumulator that lives for the whole
-// resident block:
-//   TMEM columns [0, 128), [128, 256): logit tiles (double buffered)
-//                [256, 384):           probability tile
-//                [384, 384 + 2R):      rank accumulator (hi | lo halves)
-// Streamed tiles are 128 columns wide so the four fit in 512 columns.  The
-// logit MMAs of tile i+1 are issued right behind the rank MMAs of tile i-1
-// (the logit buffer is free once the epilogue has read it), so the tensor
-// pipe does not wait for the rank MMAs to complete.
-//
+// epilogue only turns each logit tile into probabilities, stored as f16 in
+// TMEM, and the MMA warp multiplies that tile (A operand in TMEM) with the
+// matching rows of B or s*U (B operand in shared memory, loaded by TMA) into
+// a third TMEM accumulator that lives for the whole resident block.  TMEM
+// layouts (512 columns):
+//   ranks <= 32: [0, 192), [192, 384): logit tiles (double buffered); the
+//                probabilities overwrite the tile's own logit columns;
+//                [384, 384 + 2R): rank accumulator (hi | lo halves).  The
+//                logits of tile i+2 wait for tile i's rank MMAs.
+//   rank 64:     [0, 128), [128, 256): logit tiles; [256, 384): a separate
+//                probability tile; [384, 512): rank accumulator.  The logits
+//                of tile i+1 go into tile i-1's buffer once the epilogue has
+//                read it, without waiting for tile i-1's rank MMAs.
+
 // Precision: both factors are split x = x_hi + x_lo into f16 pairs.  The
 // probability tile is stored as [P_hi (8 cols) | P_lo (8 cols)] per 16
 // columns, and the rank operand as 2R rows [X_hi ; X_lo] (the pair's CTAs
@@ -39,22 +40,26 @@
 
 namespace lce {
 
-constexpr int kBNT = 128;                      // streamed rows per tile
-constexpr int kStRowsT = kBNT / 2;             // per CTA of the pair
-constexpr int kStBytesT = kStRowsT * kBK * 2;  // 8 KB ring stage
+// Streamed rows per tile.  Up to rank 32 the probabilities overwrite the
+// logit columns they came from (the tile's rank MMAs finish before the next
+// logits go into that buffer), so two 192-column logit tiles and the rank
+// accumulator fit in TMEM; rank 64 keeps a separate 128-column probability
+// tile beside two 128-column logit tiles.
+__host__ __device__ constexpr int tc_bn(int R) { return R <= 32 ? 192 : 128; }
+__host__ __device__ constexpr bool tc_in_place(int R) { return R <= 32; }
+constexpr int kMaxBNT = 192;
 constexpr int kMaxStT = 8;
-constexpr int kXBlocksT = kBNT / kBK;          // K-blocks of the rank product per tile
 constexpr int kEpiWarpsT = 8;                  // two per TMEM lane quarter
 constexpr int kThreadsT = 32 * (kEpiWarpsT + 3);
 constexpr int kXWarpT = 2 + kEpiWarpsT;        // rank-operand loader
-constexpr uint32_t kPColT = 2 * kBNT;          // probability tile column
-constexpr uint32_t kQColT = 3 * kBNT;          // rank accumulator column
+constexpr uint32_t kPColT = 256;               // separate probability tile (rank 64)
+constexpr uint32_t kQColT = 384;               // rank accumulator column
 constexpr float kP1Exp = 4.0f;                 // pass 1 stores 2^4 e^(z - m)
 constexpr float kP2Exp = 14.0f;                // pass 2 stores 2^14 p
 constexpr float kLazyT = 8.0f;                 // pass 1 moves its max only past this
 // Smallest rank whose handles use these passes by default.
 #ifndef LCE_TC_MIN_RANK
-#define LCE_TC_MIN_RANK 32
+#define LCE_TC_MIN_RANK 16
 #endif
 
 enum : int {
@@ -70,7 +75,8 @@ enum : int {
   kTQFull = kTXEmpty + 2,      // the block's rank accumulator is complete
   kTQEmpty,                    // ... and has been read
   kTDrain,
-  kTNumBars
+  kTAccEmpty,                  // in place: the tile's rank MMAs are done (2 buffers)
+  kTNumBars = kTAccEmpty + 2
 };
 
 // Dynamic shared memory: [resident K-blocks | ring | rank operand (xbufs
@@ -79,16 +85,18 @@ enum : int {
 // its ring still has 4 stages beside 11 resident K-blocks.
 struct TcLayout {
   static __host__ __device__ constexpr int xbufs(int R) { return R >= 64 ? 1 : 2; }
+  // streamed K-block of one CTA (tc_bn / 2 rows of 128 B): one ring stage
+  static __host__ __device__ constexpr int stage_bytes(int R) { return tc_bn(R) / 2 * kBK * 2; }
   static __host__ __device__ constexpr int ring_off(int kblocks) { return kblocks * kAKBytes; }
-  static __host__ __device__ constexpr int x_off(int kblocks, int stages) {
-    return ring_off(kblocks) + stages * kStBytesT;
+  static __host__ __device__ constexpr int x_off(int kblocks, int stages, int R) {
+    return ring_off(kblocks) + stages * stage_bytes(R);
   }
   static __host__ __device__ constexpr int x_kblock_bytes(int R) { return R * 128; }
   static __host__ __device__ constexpr int x_buf_bytes(int R) {
-    return kXBlocksT * x_kblock_bytes(R);
+    return tc_bn(R) / kBK * x_kblock_bytes(R);
   }
   static __host__ __device__ constexpr int xch_off(int kblocks, int stages, int R) {
-    return x_off(kblocks, stages) + xbufs(R) * x_buf_bytes(R);
+    return x_off(kblocks, stages, R) + xbufs(R) * x_buf_bytes(R);
   }
   static __host__ __device__ constexpr int bar_off(int kblocks, int stages, int R) {
     return xch_off(kblocks, stages, R) + 2 * 2 * kBM * 4;
@@ -98,8 +106,8 @@ struct TcLayout {
   }
   // the most ring stages that fit beside the rest
   static __host__ __device__ constexpr int stages(int kblocks, int R) {
-    return (kMaxDynSmem - bytes(kblocks, 0, R)) / kStBytesT < kMaxStT
-               ? (kMaxDynSmem - bytes(kblocks, 0, R)) / kStBytesT
+    return (kMaxDynSmem - bytes(kblocks, 0, R)) / stage_bytes(R) < kMaxStT
+               ? (kMaxDynSmem - bytes(kblocks, 0, R)) / stage_bytes(R)
                : kMaxStT;
   }
 };
@@ -155,6 +163,11 @@ __global__ void __launch_bounds__(kThreadsT, 1)
   constexpr int kXKB = TcLayout::x_kblock_bytes(R);
   constexpr int kXBuf = TcLayout::x_buf_bytes(R);
   constexpr int kXN = TcLayout::xbufs(R);
+  constexpr int kBNT = tc_bn(R);
+  constexpr bool kInPlace = tc_in_place(R);
+  constexpr int kStRowsT = kBNT / 2;
+  constexpr int kStBytesT = TcLayout::stage_bytes(R);
+  constexpr int kXBlocksT = kBNT / kBK;
   constexpr int kResRows = 2 * kBM;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const int kSt = g.stages;
@@ -171,7 +184,7 @@ __global__ void __launch_bounds__(kThreadsT, 1)
   uint8_t* smem = smem_raw + pad;
   uint8_t* sA = smem;
   uint8_t* sB = smem + TcLayout::ring_off(g.kblocks);
-  uint8_t* sX = smem + TcLayout::x_off(g.kblocks, kSt);
+  uint8_t* sX = smem + TcLayout::x_off(g.kblocks, kSt, R);
   float* xch = reinterpret_cast<float*>(smem + TcLayout::xch_off(g.kblocks, kSt, R));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TcLayout::bar_off(g.kblocks, kSt, R));
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kTNumBars);
@@ -203,6 +216,8 @@ __global__ void __launch_bounds__(kThreadsT, 1)
     mbar_init(&bars[kTQFull], 1);
     mbar_init(&bars[kTQEmpty], 2 * kEpiWarpsT);
     mbar_init(&bars[kTDrain], 1);
+    mbar_init(&bars[kTAccEmpty], 1);
+    mbar_init(&bars[kTAccEmpty + 1], 1);
     fence_mbar_init();
     prefetch_tmap(&map_res);
     prefetch_tmap(&map_str);
@@ -308,16 +323,18 @@ __global__ void __launch_bounds__(kThreadsT, 1)
           return false;
         tc_fence_after();
         const uint8_t* xs = sX + xb * kXBuf;
+        const uint32_t p_src = kInPlace ? tmem_base + (uint32_t)((prev_li & 1) * kBNT) : p_tmem;
 #pragma unroll
         for (int k = 0; k < kBNT / 16; ++k) {
           const uint64_t bdesc =
               sw128_kmajor_desc(smem_u32(xs + (k >> 2) * kXKB)) + (uint64_t)(2 * (k & 3));
-          umma_f16_ts_pair(q_tmem, p_tmem + (uint32_t)(16 * k), bdesc, kIdescX,
+          umma_f16_ts_pair(q_tmem, p_src + (uint32_t)(16 * k), bdesc, kIdescX,
                            (prev_first && k == 0) ? 0u : 1u);
-          umma_f16_ts_pair(q_tmem, p_tmem + (uint32_t)(16 * k + 8), bdesc, kIdescX, 1u);
+          umma_f16_ts_pair(q_tmem, p_src + (uint32_t)(16 * k + 8), bdesc, kIdescX, 1u);
         }
         umma_commit_pair(&bars[kTXEmpty + xb], 0x3);
-        umma_commit_pair(&bars[kTPEmpty], 0x3);
+        if constexpr (kInPlace) umma_commit_pair(&bars[kTAccEmpty + (int)(prev_li & 1)], 0x3);
+        else umma_commit_pair(&bars[kTPEmpty], 0x3);
         if (prev_last) umma_commit_pair(&bars[kTQFull], 0x3);
         return true;
       };
@@ -331,6 +348,11 @@ __global__ void __launch_bounds__(kThreadsT, 1)
           ++blk;
         }
         const int buf = (int)(li & 1);
+        // in place, tile li-2's probabilities sit in this buffer until its
+        // rank MMAs are done
+        if (kInPlace && !mbar_wait(&bars[kTAccEmpty + buf], (uint32_t)(((li >> 1) & 1) ^ 1), g.err,
+                                   kErrWaitMma))
+          break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(buf * kBNT);
         for (int kb = 0; kb < g.kmain; ++kb) {
@@ -495,8 +517,11 @@ __global__ void __launch_bounds__(kThreadsT, 1)
       const int gcol = b * kBNT + half * kHalfCols;
       const int limit = kPass == 1 ? g.V : g.T;
       const bool tail = gcol + kHalfCols > limit;
-      // the rank MMAs of tile li-1 are done with the probability buffer
-      bool p_free = li == 0;
+      // Probabilities: in place over this tile's logits, or in the separate
+      // buffer once tile li-1's rank MMAs are done with it.  Either way a
+      // rescale of the rank accumulator waits for those rank MMAs.
+      const uint32_t pb = kInPlace ? zb : p_addr;
+      bool p_free = kInPlace || li == 0;
       auto wait_p_free = [&]() {
         if (!p_free && !failed &&
             !mbar_wait(&bars[kTPEmpty], (uint32_t)((li - 1) & 1), g.err, kErrWaitEpilogue))
@@ -504,29 +529,45 @@ __global__ void __launch_bounds__(kThreadsT, 1)
         p_free = true;
         tc_fence_after();
       };
+      auto wait_prev_rank = [&]() {
+        if constexpr (kInPlace) {
+          if (li > 0 && !failed &&
+              !mbar_wait(&bars[kTAccEmpty + (int)((li - 1) & 1)], (uint32_t)(((li - 1) >> 1) & 1),
+                         g.err, kErrWaitEpilogue))
+            failed = true;
+          tc_fence_after();
+        } else {
+          wait_p_free();
+        }
+      };
       if constexpr (kPass == 1) {
         // (a) the row's max over the tile; the two halves of a row meet in
         // shared memory (a 64-thread barrier per lane quarter, passed by both
         // warps on every tile, failed or not)
         float cm = -INFINITY;
         if (!failed) {
-          float z0[32], z1[32];
-          tmem_ld<32>(zb, z0);
-          tmem_ld<32>(zb + 32u, z1);
-          tmem_ld_wait<32>(z0);
-          tmem_ld_wait<32>(z1);
+          constexpr int NL = kHalfCols / 32;
+          float zz[NL][32];
+#pragma unroll
+          for (int l = 0; l < NL; ++l) tmem_ld<32>(zb + (uint32_t)(32 * l), zz[l]);
+#pragma unroll
+          for (int l = 0; l < NL; ++l) tmem_ld_wait<32>(zz[l]);
           if (tail) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              if (gcol + i >= g.V) z0[i] = -INFINITY;
-              if (gcol + 32 + i >= g.V) z1[i] = -INFINITY;
-            }
+            for (int l = 0; l < NL; ++l)
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (gcol + 32 * l + i >= g.V) zz[l][i] = -INFINITY;
           }
           float mx[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            mx[i] = fmaxf(fmaxf(fmaxf(z0[i], z0[i + 8]), fmaxf(z0[i + 16], z0[i + 24])),
-                          fmaxf(fmaxf(z1[i], z1[i + 8]), fmaxf(z1[i + 16], z1[i + 24])));
+          for (int i = 0; i < 8; ++i) {
+            mx[i] = fmaxf(fmaxf(zz[0][i], zz[0][i + 8]), fmaxf(zz[0][i + 16], zz[0][i + 24]));
+#pragma unroll
+            for (int l = 1; l < NL; ++l)
+              mx[i] = fmaxf(mx[i], fmaxf(fmaxf(zz[l][i], zz[l][i + 8]),
+                                         fmaxf(zz[l][i + 16], zz[l][i + 24])));
+          }
           cm = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
                      fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
         }
@@ -540,7 +581,7 @@ __global__ void __launch_bounds__(kThreadsT, 1)
           if (!first_tile) {
             // rescale this half's columns of the rank accumulator once the
             // previous tile's rank MMAs have landed
-            wait_p_free();
+            wait_prev_rank();
             if (!failed) {
 #pragma unroll 1
               for (int j0 = 0; j0 < R; j0 += kQW) {
@@ -588,8 +629,8 @@ __global__ void __launch_bounds__(kThreadsT, 1)
               g.z_tgt[rr] = zt;
             }
             if (c == 0) wait_p_free();
-            tmem_st<8>(p_addr + (uint32_t)(16 * c), hi);
-            tmem_st<8>(p_addr + (uint32_t)(16 * c + 8), lo);
+            tmem_st<8>(pb + (uint32_t)(16 * c), hi);
+            tmem_st<8>(pb + (uint32_t)(16 * c + 8), lo);
           };
           tmem_ld<16>(zb, za);
           tmem_ld_wait<16>(za);
@@ -623,8 +664,8 @@ __global__ void __launch_bounds__(kThreadsT, 1)
               split_f16x2(e2, hi[p], lo[p]);
             }
             if (c == 0) wait_p_free();
-            tmem_st<8>(p_addr + (uint32_t)(16 * c), hi);
-            tmem_st<8>(p_addr + (uint32_t)(16 * c + 8), lo);
+            tmem_st<8>(pb + (uint32_t)(16 * c), hi);
+            tmem_st<8>(pb + (uint32_t)(16 * c + 8), lo);
           };
           tmem_ld<16>(zb, za);
           ld_vec<16>(g.nml + gcol, na);
