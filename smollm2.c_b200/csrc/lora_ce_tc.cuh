@@ -19,7 +19,7 @@
 //                probability tile; [384, 512): rank accumulator.  The logits
 //                of tile i+1 go into tile i-1's buffer once the epilogue has
 //                read it, without waiting for tile i-1's rank MMAs.
-
+//
 // Precision: both factors are split x = x_hi + x_lo into f16 pairs.  The
 // probability tile is stored as [P_hi (8 cols) | P_lo (8 cols)] per 16
 // columns, and the rank operand as 2R rows [X_hi ; X_lo] (the pair's CTAs
