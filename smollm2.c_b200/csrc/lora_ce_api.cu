@@ -650,12 +650,16 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
   g.Bt = Bfull;
   // 3. merge partials -> M, 1/S, loss_t, dU
   mark(h, kPhCombine);
-  lce_combine<R><<<(T + 7) / 8, 256, 0, st>>>(T, cp1, res_rows, n_b1, units1, chunks, stride1,
-                                                  h->p_max,
-                                                  h->p_sum,
-                                                  h->p_q, h->z_tgt, Bfull, h->cfg.scale, h->tok,
-                                                  h->dU, h->loss_tok,
-                                                  rank_chunks ? h->tokc : nullptr, tokc_stride);
+  if constexpr (R >= 16)  // lanes over ranks
+    lce_combine_wide<R><<<(T + 7) / 8, 256, 0, st>>>(
+        T, cp1, res_rows, n_b1, units1, chunks, stride1, h->p_max, h->p_sum, h->p_q, h->z_tgt,
+        Bfull, h->cfg.scale, h->tok, h->dU, h->loss_tok, rank_chunks ? h->tokc : nullptr,
+        tokc_stride);
+  else
+    lce_combine<R><<<(T + 7) / 8, 256, 0, st>>>(T, cp1, res_rows, n_b1, units1, chunks, stride1,
+                                                h->p_max, h->p_sum, h->p_q, h->z_tgt, Bfull,
+                                                h->cfg.scale, h->tok, h->dU, h->loss_tok,
+                                                rank_chunks ? h->tokc : nullptr, tokc_stride);
   ++launches;
   // onehot part of dB (order-independent fixed-point sums)
   lce_onehot<R><<<(T + 63) / 64, 64, 0, st>>>(T, h->tok, h->corr_fx, h->err);

@@ -1187,6 +1187,70 @@ __global__ void lce_combine(int T, int cparts, int res_rows, int n_b1, int units
   for (int j = 0; j < R; ++j) dU[(long long)t * R + j] = scale * (Q[j] * inv - Bt[bidx(tg, j, R)]);
 }
 
+// lce_combine for ranks 16..64, lanes over ranks: every lane walks the few
+// partial slots of its position (the max and the sum are the same in every
+// lane), and lane l merges q and writes dU for ranks l, l + 32 (< R), so no
+// warp reduction of R sums is needed and the dU row is written by all lanes.
+template <int R>
+__global__ void lce_combine_wide(int T, int cparts, int res_rows, int n_b1, int units1, int chunks,
+                                 long long Tcap, const float* __restrict__ p_max,
+                                 const float* __restrict__ p_sum, const float* __restrict__ p_q,
+                                 const float* __restrict__ z_tgt, const float* __restrict__ Bt,
+                                 float scale, float* __restrict__ tok, float* __restrict__ dU,
+                                 float* __restrict__ loss_tok, float* __restrict__ tokc,
+                                 long long tokc_stride) {
+  static_assert(R >= 16 && R <= 64, "wide combine: ranks 16..64");
+  constexpr int kPer = (R + 31) / 32;  // ranks per lane
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const int n_a = (T + res_rows - 1) / res_rows;
+  const int ab = t / res_rows;
+  const int c = tile_owner(ab, n_a, chunks);
+  const int a_lo = (int)tile_start(c, n_a, chunks), a_hi = (int)tile_start(c + 1, n_a, chunks);
+  const int a = ab - a_lo;
+  const long long total = (long long)(a_hi - a_lo) * n_b1;
+  const int G1 = (int)(total < units1 ? total : units1);
+  const int s0 = tile_owner((long long)a * n_b1, total, G1);
+  const int s1 = tile_owner((long long)a * n_b1 + n_b1 - 1, total, G1);
+  const int nslot = cparts * (s1 - s0 + 1);
+  float M = -INFINITY;
+  for (int k = 0; k < nslot; ++k) M = fmaxf(M, p_max[(long long)k * Tcap + t]);
+  float S = 0.f, Q[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) Q[i] = 0.f;
+  for (int k = 0; k < nslot; ++k) {
+    const long long o = (long long)k * Tcap + t;
+    const float pm = p_max[o];
+    if (pm == -INFINITY) continue;  // a slice that saw no valid column
+    const float f = expf(pm - M);
+    S = fmaf(p_sum[o], f, S);
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int j = lane + 32 * i;
+      if (j < R) Q[i] = fmaf(p_q[o * R + j], f, Q[i]);
+    }
+  }
+  const float inv = 1.0f / S;
+  const int tg = __float_as_int(tok[tidx(t, R + 2, R)]);
+  if (lane == 0) {
+    const float pt = expf(z_tgt[t] - M) * inv;
+    loss_tok[t] = -logf(pt + 1e-12f);
+    tok[tidx(t, R, R)] = -(M * kLog2e);
+    tok[tidx(t, R + 1, R)] = inv;
+    if (tokc)  // the rank chunks' records of position t (pass 2 of each chunk)
+      for (int cc = 0; cc < R / 16; ++cc) {
+        tokc[cc * tokc_stride + crec_idx(t, 16)] = -(M * kLog2e);
+        tokc[cc * tokc_stride + crec_idx(t, 17)] = inv;
+      }
+  }
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int j = lane + 32 * i;
+    if (j < R) dU[(long long)t * R + j] = scale * (Q[i] * inv - Bt[bidx(tg, j, R)]);
+  }
+}
+
 // The onehot part of dl = p - onehot for dB: corr[v][j] = -(sum of
 // s*U[t][j] over the positions t whose target is v).  Each term is rounded
 // to a 64-bit fixed-point number (2^-30 resolution) and added with integer
