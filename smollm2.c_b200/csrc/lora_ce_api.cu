@@ -476,7 +476,7 @@ void plan_units(lora_ce_handle* h, int* u1, int* u2) {
       cudaFuncSetAttribute(lce_prep<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem) !=
           cudaSuccess)
     *u1 = 0;
-  if constexpr (R >= 32) {
+  if constexpr (R >= 16) {
     if (cudaFuncSetAttribute(lce_prep_wide<R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              prep_wide_smem(R, h->d)) != cudaSuccess)
       *u1 = 0;
@@ -602,7 +602,7 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
     const int t_lo = a_lo * res_rows;
     const int t_hi = c + 1 == chunks ? (int)Tpad : a_hi * res_rows;  // last chunk pads to Tpad
     if (chunk_ready) LCE_CUDA(cudaStreamWaitEvent(st, chunk_ready[c], 0));
-    if constexpr (R >= 32) {  // lanes over ranks, one block per SM
+    if constexpr (R >= 16) {  // lanes over ranks, one block per SM
       const int warps_blk = prep_wide_warps(R, d);
       const int per_block = warps_blk * prep_wide_rows(R);
       const int blocks = (int)std::min<long long>((t_hi - t_lo + per_block - 1) / per_block,
