@@ -14,9 +14,17 @@ on the library's stream.
 Prints one JSON line (rank 0).  `value` is the device-resident step
 throughput (tokens/s over all ranks); `e2e` is the same step through the
 public C ABI call with pinned host buffers (h and targets copied in, loss
-read back, all inside the timed region).  `roofline` describes the
-dominant kernel, `cpu_baseline` the reference CPU path timed on this
-host's cores.
+read back, all inside the timed region), with a breakdown of where a
+host-input step's time goes (host enqueue and wait, the chunked copies).
+`roofline` describes the dominant kernel, `cpu_baseline` the reference CPU
+path timed on this host's cores.  The default line also carries `strong`:
+the rank-16 workload with 65,536 positions split over the N GPUs (strong
+scaling), with its per-rank all-reduce and pass times.
+
+Other modes: --config 3/4/5 (the rank-16, Q4_K and rank-64 workloads as the
+main line), --tokens T (positions per rank), --op merge / q4k (the merge and
+dequantisation kernels), --kernel-run (only the device steps, the command
+to capture under ncu), --impl reference (the reference's CPU path).
 """
 from __future__ import annotations
 
@@ -333,10 +341,10 @@ def run_reference_arm(args):
         "ms_per_step": 1e3 * step_tokens(world) / value,
         "higher_is_better": True, "scaling": CONFIG["scaling"], "vs_baseline": None,
         "dtype": "f32", "data": "synthetic (seeded; bf16 h, f16 W, Zipf(1.1) targets)",
-        "config": {"workload": CONFIG["desc"] + "; each step a sample of positions on the "
-                               "reference's CPU path (f16 W: the reference has no Q4_K)",
-                   "tokens_per_step": step_tokens(world), "rank": R,
-                   "parallelism": f"dp{world}"},
+        "config": dict(config_dict(args.config, world, step_tokens(world) // world),
+                       tokens_per_step=step_tokens(world),
+                       sample="each step a bounded sample of positions on the reference's CPU "
+                              "path (f16 W: the reference has no Q4_K)"),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": steps[0]["cores"],
                          "kind": steps[0]["kind"], "sample": steps[0]["sample"]},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -542,6 +550,187 @@ def run_q4k(args):
 
 
 # ----------------------------------------------------------------- GPU leg
+def cfg_workload(n: int, world: int, tokens: int | None = None):
+    """(rank, alpha, positions per rank, clip, q4k) of workload n at world ranks."""
+    c = CONFIGS[n]
+    T = tokens or c["tokens"]
+    T_rank = T // world if c["scaling"] == "strong" else T
+    return c["rank"], c["alpha"], T_rank, c.get("clip", 0.0), c["q4k"]
+
+
+def make_handle(n, world, rank, local, tokens=None, seed=1000):
+    """A handle and its device / host inputs for workload n on this rank."""
+    import numpy as np
+    import torch
+    import lora_ce
+    import workload as wl
+
+    r, alpha, T, clip, q4k = cfg_workload(n, world, tokens)
+    h, tgt, _, _ = wl.make_step_inputs(seed + rank, T, V, D, r)
+    _, _, A, B = wl.make_step_inputs(seed, 8, V, D, r)  # same adapter on every rank
+    cfg = lora_ce.default_config(D, V, r, T, scale=alpha / r, lr=LR, weight_decay=WD,
+                                 clip_norm=clip, device=local)
+    m = lora_ce.LoraCE(cfg)
+    if q4k:
+        m.set_weight_q4k(wl.make_weight_q4k(1, V, D))
+    else:
+        m.set_weight(wl.make_weight(1, V, D))
+    m.set_adapter(A, B, 0)
+    dev = torch.device("cuda", local)
+    dH = torch.from_numpy(h.view(np.int16)).to(dev)
+    dT = torch.from_numpy(tgt).to(dev)
+    return m, h, tgt, dH, dT, T
+
+
+class Rig:
+    """The per-process measurement set-up: device, L2 flush buffer, barrier
+    and max-over-ranks reductions."""
+
+    def __init__(self, torch, dist, local):
+        self.torch, self.dist = torch, dist
+        self.dev = torch.device("cuda", local)
+        self.flush_buf = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=self.dev)
+
+    def barrier(self):
+        self.torch.cuda.synchronize(self.dev)
+        if self.dist is not None:
+            self.dist.barrier()
+
+    def max_over_ranks(self, x: float) -> float:
+        t = self.torch.tensor([x], dtype=self.torch.float64, device=self.dev)
+        if self.dist is not None:
+            self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def gather(self, obj):
+        if self.dist is None:
+            return [obj]
+        out = [None] * self.dist.get_world_size()
+        self.dist.all_gather_object(out, obj)
+        return out
+
+    def timed(self, st, fn, n):
+        """n calls of fn, each bracketed by CUDA events on stream st with an
+        L2 flush (256 MB write) before it; per-call ms."""
+        torch = self.torch
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(n)]
+        for s, e in evs:
+            with torch.cuda.stream(st):
+                self.flush_buf.fill_(1.0)
+            s.record(st)
+            fn()
+            e.record(st)
+        torch.cuda.synchronize(self.dev)
+        return [s.elapsed_time(e) for s, e in evs]
+
+
+def measure(rig, m, h, tgt, dH, dT, T, world, steps, warmup, clocks=None, breakdown=True):
+    """Device-resident and end-to-end throughput of one workload's step on
+    this rank's handle; max over ranks for the timed totals."""
+    import numpy as np
+    import torch
+    import lora_ce
+
+    st = torch.cuda.ExternalStream(m.stream, device=rig.dev)
+    dLoss = torch.zeros(2, dtype=torch.float32, device=rig.dev)
+
+    def dev_step():
+        m.step_device(dH.data_ptr(), lora_ce.BF16, T, dT.data_ptr(), dLoss.data_ptr())
+
+    for _ in range(warmup):
+        dev_step()
+    m.sync()
+    rig.barrier()
+    if clocks is not None:
+        with clocks:
+            ms = rig.timed(st, dev_step, steps)
+    else:
+        ms = rig.timed(st, dev_step, steps)
+    m.sync()
+    launches = m.last_launches
+    rig.barrier()
+    total_ms = rig.max_over_ranks(sum(ms))
+    out = {"T": T, "ms": ms, "total_ms": total_ms, "launches": launches,
+           "value": world * T * steps / (total_ms / 1e3)}
+    if clocks is not None:
+        out["clocks"] = clocks.summary()
+
+    # per-kernel durations (same stream), for the roofline and the breakdown
+    m.set_profiling(True)
+    phase = {}
+    for _ in range(max(3, steps // 2)):
+        with torch.cuda.stream(st):
+            rig.flush_buf.fill_(1.0)
+        dev_step()
+        for k, v in m.phase_times().items():
+            phase.setdefault(k, []).append(v)
+    m.set_profiling(False)
+    out["phase_ms"] = {k: sum(v) / len(v) for k, v in phase.items()}
+
+    # end to end through the public API with pinned host buffers
+    hH = torch.from_numpy(h.view(np.int16)).pin_memory()
+    hT = torch.from_numpy(tgt).pin_memory()
+    hHn, hTn = hH.numpy().view(np.uint16), hT.numpy()
+    for _ in range(2):
+        m.step(hHn, hTn)
+    rig.barrier()
+    e2e_ms = rig.timed(st, lambda: m.step(hHn, hTn), steps)
+    out["e2e_ms"] = e2e_ms
+    out["e2e_value"] = world * T * steps / (rig.max_over_ranks(sum(e2e_ms)) / 1e3)
+    out["h2d_bytes"] = int(hH.numel() * 2 + hT.numel() * 4)
+    if breakdown:
+        # the same end-to-end steps again with event nodes in the graph: where
+        # each step's time goes (host enqueue, host wait, the chunk copies)
+        m.set_copy_timing(True)
+        for _ in range(2):
+            m.step(hHn, hTn)
+        rows = []
+        for _ in range(steps):
+            with torch.cuda.stream(st):
+                rig.flush_buf.fill_(1.0)
+            m.step(hHn, hTn)
+            rows.append(m.copy_times())
+        m.set_copy_timing(False)
+        med = statistics.median
+        nch = len(rows[0]["chunk_ms"])
+        out["e2e_breakdown"] = {
+            "steps": len(rows),
+            "host_enqueue_us": {"min": round(min(r["host_us"] for r in rows), 1),
+                                "median": round(med(r["host_us"] for r in rows), 1),
+                                "max": round(max(r["host_us"] for r in rows), 1)},
+            "host_wait_us": {"min": round(min(r["wait_us"] for r in rows), 1),
+                             "median": round(med(r["wait_us"] for r in rows), 1),
+                             "max": round(max(r["wait_us"] for r in rows), 1)},
+            "copy_start_ms_median": round(med(r["copy_wait_ms"] for r in rows), 4),
+            "chunk_copy_ms_median": [round(med(r["chunk_ms"][c] for r in rows), 4)
+                                     for c in range(nch)],
+            "h2d_GBps_median": round(out["h2d_bytes"] / 1e6 /
+                                     med(sum(r["chunk_ms"]) for r in rows), 2),
+            "graph_step_ms": {"min": round(min(r["step_ms"] for r in rows), 4),
+                              "median": round(med(r["step_ms"] for r in rows), 4),
+                              "max": round(max(r["step_ms"] for r in rows), 4)},
+        }
+    return out
+
+
+def kernel_run(args):
+    """Only the device step of the chosen workload, `--steps` times after
+    `--warmup` untimed steps, nothing else: the command to run under ncu for
+    a kernel capture (small --tokens keep the capture short)."""
+    import torch
+    import lora_ce
+
+    torch.cuda.set_device(0)
+    m, h, tgt, dH, dT, T = make_handle(args.config, 1, 0, 0, args.tokens)
+    for _ in range(args.warmup + args.steps):
+        m.step_device(dH.data_ptr(), lora_ce.BF16, T, dT.data_ptr(), 0)
+    m.sync()
+    m.close()
+    print(f"kernel run ok: config {args.config}, rank {CONFIG['rank']}, T {T}, "
+          f"{args.warmup + args.steps} steps", flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -551,9 +740,18 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--op", default="step", choices=["step", "merge", "q4k"])
     ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="positions per step (per rank for weak scaling) instead of the "
+                         "workload's own")
+    ap.add_argument("--no-strong", action="store_true",
+                    help="leave out the rank-16 strong-scaling object of the default line")
+    ap.add_argument("--kernel-run", action="store_true",
+                    help="run only the device steps (the command for an ncu capture)")
     ap.add_argument("--merge-rank", type=int, default=R)
     args = ap.parse_args()
     apply_config(args.config)
+    if args.tokens:
+        CONFIG["tokens"] = args.tokens
     if args.impl == "reference":
         run_reference_arm(args)
         return
@@ -563,12 +761,12 @@ def main():
     if args.op == "q4k":
         run_q4k(args)
         return
+    if args.kernel_run:
+        kernel_run(args)
+        return
     args.warmup = max(args.warmup, 3)
 
-    import numpy as np
     import torch
-    import lora_ce
-    import workload as wl
 
     rank = env_int("RANK", 0)
     world = env_int("WORLD_SIZE", 1)
@@ -588,140 +786,102 @@ def main():
         cpu = ref.sample(15.0)
         ref.close()
     numa_cpus = bind_near_gpu(local)  # after the CPU pool, which uses every core
+    rig = Rig(torch, dist, local)
 
-    T = step_tokens(world) // world  # this rank's positions (strong scaling splits the total)
-    h, tgt, A, B = wl.make_step_inputs(1000 + rank, T, V, D, R)
-    _, _, A, B = wl.make_step_inputs(1000, 8, V, D, R)  # same adapter on every rank
-    cfg = lora_ce.default_config(D, V, R, T, scale=ALPHA / R, lr=LR, weight_decay=WD,
-                                 clip_norm=CONFIG.get("clip", 0.0), device=local)
-    m = lora_ce.LoraCE(cfg)
-    if CONFIG["q4k"]:
-        m.set_weight_q4k(wl.make_weight_q4k(1, V, D))
-    else:
-        m.set_weight(wl.make_weight(1, V, D))
-    m.set_adapter(A, B, 0)
-    if world > 1:
-        uid = [lora_ce.LoraCE.nccl_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0)
-        m.comm_init(world, rank, uid[0])
+    def with_comm(m):
+        if world > 1:
+            uid = [m.nccl_unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(uid, src=0)
+            m.comm_init(world, rank, uid[0])
+        return m
 
-    dev = torch.device("cuda", local)
-    st = torch.cuda.ExternalStream(m.stream, device=dev)
-    dH = torch.from_numpy(h.view(np.int16)).to(dev)
-    dT = torch.from_numpy(tgt).to(dev)
-    dLoss = torch.zeros(2, dtype=torch.float32, device=dev)
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
-
-    def flush_l2():
-        with torch.cuda.stream(st):
-            flush.fill_(1.0)
-
-    def barrier():
-        torch.cuda.synchronize(dev)
-        if dist is not None:
-            dist.barrier()
-
-    def timed(fn, n):
-        """n calls of fn, each bracketed by CUDA events on the library's
-        stream with an L2 flush in between; returns per-call ms."""
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(n)]
-        for s, e in evs:
-            flush_l2()
-            s.record(st)
-            fn()
-            e.record(st)
-        torch.cuda.synchronize(dev)
-        return [s.elapsed_time(e) for s, e in evs]
-
-    def dev_step():
-        m.step_device(dH.data_ptr(), lora_ce.BF16, T, dT.data_ptr(), dLoss.data_ptr())
-
-    # device-resident throughput
-    for _ in range(args.warmup):
-        flush_l2()
-        dev_step()
-    m.sync()
-    barrier()
-    with ClockSampler(local) as clk:
-        ms = timed(dev_step, args.steps)
-    m.sync()
-    launches_per_step = m.last_launches
-    barrier()
-    step_ms = sum(ms) / len(ms)
-    t_max = torch.tensor([sum(ms)], dtype=torch.float64, device=dev)
-    if dist is not None:
-        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
-    total_ms = float(t_max.item())
-    value = world * T * args.steps / (total_ms / 1e3)
-
-    # per-kernel durations (same stream), for the roofline of the dominant kernel
-    m.set_profiling(True)
-    phase = {}
-    for _ in range(max(3, args.steps // 2)):
-        flush_l2()
-        dev_step()
-        for k, v in m.phase_times().items():
-            phase.setdefault(k, []).append(v)
-    m.set_profiling(False)
-    phase_ms = {k: sum(v) / len(v) for k, v in phase.items()}
+    m, h, tgt, dH, dT, T = make_handle(args.config, world, rank, local, CONFIG["tokens"])
+    with_comm(m)
+    res = measure(rig, m, h, tgt, dH, dT, T, world, args.steps, args.warmup,
+                  clocks=ClockSampler(local))
+    clk = res.pop("clocks", None)
+    m.close()
+    phase_ms = res["phase_ms"]
     dom = max(("pass1_lse", "pass2_grad"), key=lambda k: phase_ms[k])
     peak_tf, hbm, peak_kind = peaks()
     achieved = F_PASS * T / (phase_ms[dom] * 1e-3) / 1e12
     traffic = None
     tp = os.path.join(REPO, "profiles", "traffic.json")
-    if os.path.exists(tp):
+    if os.path.exists(tp) and not args.tokens:
         with open(tp) as f:  # per workload: the GEMM passes' DRAM bytes per launch
             traffic = json.load(f).get(f"config{args.config}", {}).get(dom)
 
-    # end to end through the public API with pinned host buffers
-    hH = torch.from_numpy(h.view(np.int16)).pin_memory()
-    hT = torch.from_numpy(tgt).pin_memory()
-    hHn, hTn = hH.numpy().view(np.uint16), hT.numpy()
-    for _ in range(2):
-        m.step(hHn, hTn)
-    barrier()
-    e2e_ms = timed(lambda: m.step(hHn, hTn), args.steps)
-    e2e_t = torch.tensor([sum(e2e_ms)], dtype=torch.float64, device=dev)
-    if dist is not None:
-        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
-    e2e_value = world * T * args.steps / (float(e2e_t.item()) / 1e3)
+    # the rank-16 strong-scaling workload (65,536 positions split over the
+    # ranks) at this world size, beside the default line
+    strong = None
+    if args.config == 2 and not args.no_strong:
+        r3 = CONFIGS[3]["rank"]
+        m3, h3, tgt3, dH3, dT3, T3 = make_handle(3, world, rank, local, None, seed=3000)
+        with_comm(m3)
+        s3 = measure(rig, m3, h3, tgt3, dH3, dT3, T3, world, args.steps, args.warmup,
+                     breakdown=False)
+        m3.close()
+        per_rank = rig.gather({"rank": rank, "phase_ms": {k: round(v, 4)
+                                                          for k, v in s3["phase_ms"].items()}})
+        f3 = flops(r3)[0]
+        strong = {
+            "workload": CONFIGS[3]["desc"], "config": 3, "scaling": "strong",
+            "tokens_per_step": CONFIGS[3]["tokens"], "T_per_gpu": T3, "rank": r3,
+            "value": s3["value"], "unit": UNIT, "ms_per_step": s3["total_ms"] / args.steps,
+            "frac_step_of_peak": f3 * s3["value"] / world / 1e12 / peak_tf,
+            "e2e": {"value": s3["e2e_value"], "unit": UNIT,
+                    "h2d_bytes_per_step": s3["h2d_bytes"] * world, "d2h_bytes_per_step": 8},
+            "allreduce_us_per_rank": [round(1e3 * p["phase_ms"].get("allreduce", 0.0), 1)
+                                      for p in per_rank],
+            "pass_ms_per_rank": [{"pass1": p["phase_ms"]["pass1_lse"],
+                                  "pass2": p["phase_ms"]["pass2_grad"]} for p in per_rank],
+            "phase_ms_rank0": per_rank[0]["phase_ms"],
+            "gpu_launches": s3["launches"] * args.steps,
+        }
 
     if rank == 0:
+        e2e_ms = res["e2e_ms"]
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+            "metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": res["total_ms"] / args.steps,
             "higher_is_better": True, "scaling": CONFIG["scaling"], "vs_baseline": None,
             "dtype": "f16",
             "data": "synthetic (seeded; h bf16 N(0,1), W " +
                     ("Q4_K blocks" if CONFIG["q4k"] else "f16 N(0,0.02)") + ", Zipf(1.1) targets)",
-            "config": {"workload": CONFIG["desc"], "config": args.config,
-                       "T_per_gpu": T, "vocab": V, "dim": D, "rank": R, "lr": LR,
-                       "weight_decay": WD, "parallelism": f"dp{world}",
-                       "l2": "flushed (256 MB write) before every timed step"},
-            "tflops_step": F_TOK * T * world / (total_ms / args.steps * 1e-3) / 1e12 / world,
-            "frac_step_of_peak": F_TOK * T / (step_ms * 1e-3) / 1e12 / peak_tf,
+            "config": config_dict(args.config, world, T),
+            "tflops_step": F_TOK * T * world / (res["total_ms"] / args.steps * 1e-3) / 1e12 / world,
+            "frac_step_of_peak": F_TOK * T / (res["total_ms"] / args.steps * 1e-3) / 1e12 / peak_tf,
             "phase_ms": {k: round(v, 4) for k, v in phase_ms.items()},
             "roofline": {"kernel": dom, "bound": "tensor", "achieved": achieved,
                          "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf,
                          "peak_kind": f"{peak_kind} bf16 dense burst",
                          "flops_per_launch": F_PASS * T, "traffic": traffic},
             "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": UNIT,
-                    "h2d_bytes_per_step": int(hH.numel() * 2 + hT.numel() * 4),
-                    "d2h_bytes_per_step": 8,
+            "e2e": {"value": res["e2e_value"], "unit": UNIT,
+                    "h2d_bytes_per_step": res["h2d_bytes"], "d2h_bytes_per_step": 8,
                     "host_cpus": numa_cpus,
                     "ms_per_step": {"min": round(min(e2e_ms), 4),
                                     "median": round(statistics.median(e2e_ms), 4),
-                                    "max": round(max(e2e_ms), 4)}},
-            "gpu_launches": launches_per_step * args.steps,
-            "clocks": clk.summary(),
+                                    "max": round(max(e2e_ms), 4)},
+                    "breakdown": res.get("e2e_breakdown")},
+            "gpu_launches": res["launches"] * args.steps,
+            "clocks": clk,
         }
+        if strong is not None:
+            line["strong"] = strong
         print(json.dumps(line), flush=True)
-    m.close()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def config_dict(n: int, world: int, T: int) -> dict:
+    """The `config` object of a line (the same keys in both arms)."""
+    return {"workload": CONFIGS[n]["desc"], "config": n, "T_per_gpu": T, "vocab": V, "dim": D,
+            "rank": CONFIGS[n]["rank"], "lr": LR, "weight_decay": WD,
+            "parallelism": f"dp{world}",
+            "l2": "flushed (256 MB write) before every timed step"}
 
 
 if __name__ == "__main__":

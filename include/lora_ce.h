@@ -137,6 +137,16 @@ int lora_ce_get_grads(lora_ce_handle* h, float* gA_dxr, float* gB_rxv,
 /* Per-position loss of the last step on this rank (T floats). */
 int lora_ce_get_token_loss(lora_ce_handle* h, float* loss_t, int32_t T);
 
+/* One optimizer step from caller-supplied gradient SUMS over n_pred
+ * positions (gA [d][r], gB [r][V], reference layouts, host buffers):
+ * g = sum * (1/n_pred), then the optional clip and weight decay, then the
+ * Adam update, advancing the step counter.  This is the mean and
+ * adam_update of train_step (src/train.c:230-239 and 175-196) with the
+ * gradients supplied by the caller instead of lora_accum (for example
+ * sums accumulated over several micro-batches). */
+int lora_ce_apply_grads(lora_ce_handle* h, const float* gA_dxr, const float* gB_rxv,
+                        float n_pred);
+
 /* Data-parallel token sharding: every rank runs the same steps on its own
  * positions; one NCCL sum all-reduce of [dA | dB | loss | n_pred] runs
  * between the gradient and the Adam kernels.  lora_ce_nccl_unique_id fills
@@ -157,6 +167,18 @@ int lora_ce_sync(lora_ce_handle* h);
 int lora_ce_set_profiling(lora_ce_handle* h, int32_t enable);
 int32_t lora_ce_phase_times(lora_ce_handle* h, float* ms, int32_t cap);
 const char* lora_ce_phase_name(int32_t i);
+
+/* Timing of host-input steps (lora_ce_step), to see where the time of a
+ * step that starts from host memory goes.  When enabled (the step's graph
+ * is re-captured with event nodes), lora_ce_copy_times waits for the last
+ * host-input step and writes: [0] host us inside lora_ce_step before the
+ * wait (argument checks, graph launch), [1] host us waiting for the
+ * result, [2] ms from the step's start on the compute stream to the start
+ * of the copies, [3 .. 3+c) ms of each of the c chunk copies of h, [3+c]
+ * ms from the step's start to the result read-back.  Returns how many
+ * values it wrote (at most cap). */
+int lora_ce_set_copy_timing(lora_ce_handle* h, int32_t enable);
+int32_t lora_ce_copy_times(lora_ce_handle* h, float* out, int32_t cap);
 
 /* The CUDA stream the handle launches on (a cudaStream_t). */
 void* lora_ce_stream(lora_ce_handle* h);

@@ -154,47 +154,181 @@ typedef struct {
     int status;
 } block_job;
 
-/* lora_accum (src/train.c:144-173) for the tokens of one block, with the
- * base logits of each position computed as in oracle_base_logits. */
+/* Base logits of OB_P positions at once.  Every logit is the same
+ * sequential fp64 sum over the hidden index as base_logits_f32w: each f16 x
+ * f32 product is exact in fp64, so only the order of the adds matters (and
+ * a fused multiply-add of an exact product rounds like the separate add).
+ * The position block only lets one pass over W serve OB_P positions, which
+ * makes the checker fast enough for full-size workloads.  hT is [d][OB_P]
+ * (position-minor, zero rows past the block), out [OB_P][V]. */
+#define OB_P 16
+#include <immintrin.h>
+
+__attribute__((target("avx2,fma")))
+static void base_logits_blk_fma(const float* Wf, const double* hT, int d, int V,
+                                float* out) {
+    int o = 0;
+    for (; o + 2 <= V; o += 2) {
+        const float* w0 = Wf + (size_t)o * d;
+        const float* w1 = w0 + d;
+        __m256d a0 = _mm256_setzero_pd(), a1 = a0, a2 = a0, a3 = a0;
+        __m256d b0 = a0, b1 = a0, b2 = a0, b3 = a0;
+        for (int i = 0; i < d; i++) {
+            const double* hp = hT + (size_t)i * OB_P;
+            const __m256d h0 = _mm256_loadu_pd(hp), h1 = _mm256_loadu_pd(hp + 4);
+            const __m256d h2 = _mm256_loadu_pd(hp + 8), h3 = _mm256_loadu_pd(hp + 12);
+            const __m256d x0 = _mm256_set1_pd((double)w0[i]);
+            const __m256d x1 = _mm256_set1_pd((double)w1[i]);
+            a0 = _mm256_fmadd_pd(x0, h0, a0);
+            a1 = _mm256_fmadd_pd(x0, h1, a1);
+            a2 = _mm256_fmadd_pd(x0, h2, a2);
+            a3 = _mm256_fmadd_pd(x0, h3, a3);
+            b0 = _mm256_fmadd_pd(x1, h0, b0);
+            b1 = _mm256_fmadd_pd(x1, h1, b1);
+            b2 = _mm256_fmadd_pd(x1, h2, b2);
+            b3 = _mm256_fmadd_pd(x1, h3, b3);
+        }
+        double ra[OB_P], rb[OB_P];
+        _mm256_storeu_pd(ra, a0); _mm256_storeu_pd(ra + 4, a1);
+        _mm256_storeu_pd(ra + 8, a2); _mm256_storeu_pd(ra + 12, a3);
+        _mm256_storeu_pd(rb, b0); _mm256_storeu_pd(rb + 4, b1);
+        _mm256_storeu_pd(rb + 8, b2); _mm256_storeu_pd(rb + 12, b3);
+        for (int p = 0; p < OB_P; p++) {
+            out[(size_t)p * V + o] = (float)ra[p];
+            out[(size_t)p * V + o + 1] = (float)rb[p];
+        }
+    }
+    for (; o < V; o++) {
+        const float* w = Wf + (size_t)o * d;
+        for (int p = 0; p < OB_P; p++) {
+            double acc = 0.0;
+            for (int i = 0; i < d; i++) acc += (double)w[i] * hT[(size_t)i * OB_P + p];
+            out[(size_t)p * V + o] = (float)acc;
+        }
+    }
+}
+
+static void base_logits_blk_plain(const float* Wf, const double* hT, int d, int V,
+                                  float* out) {
+    for (int o = 0; o < V; o++) {
+        const float* w = Wf + (size_t)o * d;
+        double acc[OB_P];
+        for (int p = 0; p < OB_P; p++) acc[p] = 0.0;
+        for (int i = 0; i < d; i++) {
+            const double x = (double)w[i];
+            for (int p = 0; p < OB_P; p++) acc[p] += x * hT[(size_t)i * OB_P + p];
+        }
+        for (int p = 0; p < OB_P; p++) out[(size_t)p * V + o] = (float)acc[p];
+    }
+}
+
+static void base_logits_blk(const float* Wf, const double* hT, int d, int V, float* out) {
+    static int have_fma = -1;
+    if (have_fma < 0) {
+        __builtin_cpu_init();
+        have_fma = __builtin_cpu_supports("avx2") && __builtin_cpu_supports("fma");
+    }
+    if (have_fma) base_logits_blk_fma(Wf, hT, d, V, out);
+    else base_logits_blk_plain(Wf, hT, d, V, out);
+}
+
+/* lora_accum (src/train.c:144-173) for the tokens of one block, OB_P
+ * positions at a time.  Every running sum of the reference keeps its own
+ * order: matmul_hA sums over d, matmul_midB over r, the dU sum over v, and
+ * the gA / gB accumulators take the positions in increasing order.  The
+ * loops only interleave independent sums (positions, ranks or vocabulary
+ * columns side by side), so each value is bit-identical to the reference's
+ * one-position loops. */
+#define OB_VT 2048
 static void* run_block(void* arg) {
     block_job* j = (block_job*)arg;
     const int d = j->d, V = j->V, R = j->r;
-    float* logits = (float*)malloc((size_t)V * sizeof(float));
-    float* delta = (float*)malloc((size_t)V * sizeof(float));
-    float mid[ORACLE_MAX_RANK], d_mid[ORACLE_MAX_RANK];
-    if (!logits || !delta) { j->status = -1; free(logits); free(delta); return NULL; }
-    for (int t = j->t0; t < j->t1; t++) {
-        const float* h = j->H + (size_t)t * d;
-        base_logits_f32w(j->Wf, h, d, V, logits);
-        /* matmul_hA */
-        for (int r = 0; r < R; r++) {
-            float s = 0;
-            for (int i = 0; i < d; i++) s += h[i] * j->A[i * R + r];
-            mid[r] = s;
-        }
-        /* matmul_midB */
-        for (int v = 0; v < V; v++) {
-            float s = 0;
-            for (int r = 0; r < R; r++) s += mid[r] * j->B[r * V + v];
-            delta[v] = s;
-        }
-        for (int v = 0; v < V; v++) logits[v] += j->scale * delta[v];
-        float* dl = delta; /* reuse, as the reference does */
-        j->loss[t] = ce_row(logits, V, j->tgt[t], dl);
-        for (int r = 0; r < R; r++) {
-            float s = 0;
-            for (int v = 0; v < V; v++) {
-                j->gB[r * V + v] += j->scale * mid[r] * dl[v];
-                s += j->B[r * V + v] * dl[v];
-            }
-            d_mid[r] = j->scale * s;
-        }
-        for (int i = 0; i < d; i++)
-            for (int r = 0; r < R; r++)
-                j->gA[i * R + r] += h[i] * d_mid[r];
+    const float sc = j->scale;
+    float* logits = (float*)malloc((size_t)OB_P * V * sizeof(float));
+    float* delta = (float*)malloc((size_t)OB_P * V * sizeof(float));
+    float* dlT = (float*)malloc((size_t)OB_P * V * sizeof(float));
+    double* hT = (double*)malloc((size_t)d * OB_P * sizeof(double));
+    float* mid = (float*)malloc((size_t)OB_P * R * sizeof(float));
+    float* d_mid = (float*)malloc((size_t)OB_P * R * sizeof(float));
+    if (!logits || !delta || !dlT || !hT || !mid || !d_mid) {
+        j->status = -1;
+        free(logits); free(delta); free(dlT); free(hT); free(mid); free(d_mid);
+        return NULL;
     }
-    free(logits);
-    free(delta);
+    for (int t0 = j->t0; t0 < j->t1; t0 += OB_P) {
+        const int np = j->t1 - t0 < OB_P ? j->t1 - t0 : OB_P;
+        const float* Hb = j->H + (size_t)t0 * d;
+        for (int i = 0; i < d; i++)
+            for (int p = 0; p < OB_P; p++)
+                hT[(size_t)i * OB_P + p] = p < np ? (double)Hb[(size_t)p * d + i] : 0.0;
+        base_logits_blk(j->Wf, hT, d, V, logits);
+        /* matmul_hA: mid[r] = sum over i in index order */
+        for (int p = 0; p < np; p++) {
+            const float* restrict h = Hb + (size_t)p * d;
+            float* restrict m = mid + (size_t)p * R;
+            for (int r = 0; r < R; r++) m[r] = 0.0f;
+            for (int i = 0; i < d; i++) {
+                const float hi = h[i];
+                const float* restrict Ai = j->A + (size_t)i * R;
+                for (int r = 0; r < R; r++) m[r] += hi * Ai[r];
+            }
+        }
+        /* matmul_midB: delta[v] = sum over r in rank order (vocabulary
+         * tiles, so each tile of B is read once per position block) */
+        for (int v0 = 0; v0 < V; v0 += OB_VT) {
+            const int n = V - v0 < OB_VT ? V - v0 : OB_VT;
+            for (int p = 0; p < np; p++) memset(delta + (size_t)p * V + v0, 0, (size_t)n * 4);
+            for (int r = 0; r < R; r++) {
+                const float* restrict Br = j->B + (size_t)r * V + v0;
+                for (int p = 0; p < np; p++) {
+                    const float mr = mid[(size_t)p * R + r];
+                    float* restrict dp = delta + (size_t)p * V + v0;
+                    for (int v = 0; v < n; v++) dp[v] += mr * Br[v];
+                }
+            }
+        }
+        /* z += s.delta, softmax-CE; delta becomes dlogits (reused, as the
+         * reference does) */
+        for (int p = 0; p < np; p++) {
+            float* restrict lg = logits + (size_t)p * V;
+            float* restrict dp = delta + (size_t)p * V;
+            for (int v = 0; v < V; v++) lg[v] += sc * dp[v];
+            j->loss[t0 + p] = ce_row(lg, V, j->tgt[t0 + p], dp);
+        }
+        /* dlogits transposed [v][OB_P] (zero past the block) for the dU sums */
+        for (int v = 0; v < V; v++)
+            for (int p = 0; p < OB_P; p++)
+                dlT[(size_t)v * OB_P + p] = p < np ? delta[(size_t)p * V + v] : 0.0f;
+        for (int r = 0; r < R; r++) {
+            /* gB[r][v] += (s.mid[r]).dl[v], positions in order */
+            float* restrict g = j->gB + (size_t)r * V;
+            for (int p = 0; p < np; p++) {
+                const float c = sc * mid[(size_t)p * R + r];
+                const float* restrict dp = delta + (size_t)p * V;
+                for (int v = 0; v < V; v++) g[v] += c * dp[v];
+            }
+            /* dU[r] = s . sum over v in index order, one chain per position */
+            const float* restrict Br = j->B + (size_t)r * V;
+            float sacc[OB_P];
+            for (int p = 0; p < OB_P; p++) sacc[p] = 0.0f;
+            for (int v = 0; v < V; v++) {
+                const float bv = Br[v];
+                const float* restrict x = dlT + (size_t)v * OB_P;
+                for (int p = 0; p < OB_P; p++) sacc[p] += bv * x[p];
+            }
+            for (int p = 0; p < np; p++) d_mid[(size_t)p * R + r] = sc * sacc[p];
+        }
+        /* gA[i][r] += h[i].dU[r], positions in order */
+        for (int i = 0; i < d; i++) {
+            float* restrict gAi = j->gA + (size_t)i * R;
+            for (int p = 0; p < np; p++) {
+                const float hi = Hb[(size_t)p * d + i];
+                const float* restrict dm = d_mid + (size_t)p * R;
+                for (int r = 0; r < R; r++) gAi[r] += hi * dm[r];
+            }
+        }
+    }
+    free(logits); free(delta); free(dlT); free(hT); free(mid); free(d_mid);
     j->status = 0;
     return NULL;
 }

@@ -32,7 +32,9 @@ def build(ref: bool = True) -> None:
     """Compile the restatement (and the reference harness when the
     reference tree is present)."""
     targets = ["oracle", "ref"] if ref else ["oracle"]
-    subprocess.run(["make", "-s", "-C", HERE] + targets, check=True)
+    tree = os.environ.get("SMOLLM2_REF", "") or os.path.join(os.path.dirname(os.path.dirname(HERE)),
+                                                             "reference")
+    subprocess.run(["make", "-s", "-C", HERE, "REF=" + tree] + targets, check=True)
 
 
 def _load(path: str) -> C.CDLL:
@@ -119,6 +121,24 @@ class Oracle:
         loss = np.float32(total * np.float32(np.float32(1.0) / np.float32(T)))
         return dict(loss=float(loss), loss_tok=loss_tok, gA=gA, gB=gB, A=A, B=B, state=state)
 
+    def adam(self, A_dr, B_rv, gA_sum, gB_sum, n_pred, lr, wd=0.0, clip=0.0, state=None):
+        """The optimizer part alone (oracle_adam): mean over n_pred, the
+        extensions, Adam.  Returns (A, B, state)."""
+        d, r = A_dr.shape
+        V = B_rv.shape[1]
+        if state is None:
+            state = dict(step=0, mA=np.zeros((d, r), np.float32), vA=np.zeros((d, r), np.float32),
+                         mB=np.zeros((r, V), np.float32), vB=np.zeros((r, V), np.float32))
+        A = np.array(A_dr, np.float32, copy=True, order="C")
+        B = np.array(B_rv, np.float32, copy=True, order="C")
+        gA = np.array(gA_sum, np.float32, copy=True, order="C")
+        gB = np.array(gB_sum, np.float32, copy=True, order="C")
+        stp = C.c_int(state["step"])
+        self.lib.oracle_adam(d, V, r, float(lr), float(wd), float(clip), int(n_pred), C.byref(stp),
+                             A, B, gA, gB, state["mA"], state["vA"], state["mB"], state["vB"])
+        state["step"] = stp.value
+        return A, B, state
+
     def train_step_tokens(self, W16, A_dr, B_rv, H, tokens, seq_max, scale, lr,
                           wd=0.0, clip=0.0, nthreads=1, state=None):
         """train_step semantics on a raw token sample (target indexing
@@ -186,7 +206,26 @@ class RefHarness:
         lib.ref_save_adapter.restype = C.c_int
         lib.ref_grad_check_softmax_ce.argtypes = [C.c_int, C.c_float]
         lib.ref_grad_check_softmax_ce.restype = C.c_float
+        lib.ref_adam_steps.argtypes = [C.c_int, C.c_int, C.c_int, C.c_float, C.c_int, C.c_int,
+                                       _f32p, _f32p, _i32p, _f32p, _f32p]
+        lib.ref_adam_steps.restype = C.c_int
         self.lib = lib
+
+    def adam_steps(self, A_dr, B_rv, gA_sums, gB_sums, n_pred, lr, step0=0):
+        """The reference's mean + adam_update on given gradient sums:
+        gA_sums [k][d][r], gB_sums [k][r][V], n_pred [k]; returns (A, B)."""
+        d, r = A_dr.shape
+        V = B_rv.shape[1]
+        A = np.array(A_dr, np.float32, order="C")
+        B = np.array(B_rv, np.float32, order="C")
+        k = len(n_pred)
+        rc = self.lib.ref_adam_steps(d, V, r, float(lr), int(step0), k,
+                                     np.ascontiguousarray(gA_sums, np.float32),
+                                     np.ascontiguousarray(gB_sums, np.float32),
+                                     np.ascontiguousarray(n_pred, np.int32), A, B)
+        if rc != 0:
+            raise RuntimeError("reference adam_update harness failed")
+        return A, B
 
     def train_steps(self, W16, H, tokens, rank, alpha, lr, seq_max, n_steps=1,
                     A_dr=None, B_rv=None, seed=42):

@@ -189,3 +189,40 @@ int ref_train_merge(const char* base_gguf, const char* adapter, const char* out_
     fflush(stdout);
     return rc;
 }
+
+/* The reference's own gradient mean and adam_update (src/train.c:230-239,
+ * 175-196) on caller-supplied gradient sums: n_steps updates of one
+ * train_state, update k taking gA_sums[k] [d][r], gB_sums[k] [r][V] and
+ * n_pred[k], the Adam step counter starting at step0 and the moments at
+ * zero (carried from update to update).  A_io/B_io hold the adapter in and
+ * out.  Pins the GPU Adam kernel bit for bit. */
+int ref_adam_steps(int d, int V, int rank, float lr, int step0, int n_steps,
+                   const float* gA_sums, const float* gB_sums, const int* n_pred,
+                   float* A_io, float* B_io) {
+    forward_ctx f = {d, V, NULL, NULL, 0, 0, NULL};
+    train_params p;
+    memset(&p, 0, sizeof(p));
+    p.mode = TRAIN_LORA;
+    p.lora_rank = rank;
+    p.lora_alpha = 2 * rank;
+    p.lr = lr;
+    train_state* t = train_create(&f, &p);
+    if (!t) return -1;
+    const size_t a_sz = (size_t)d * rank, b_sz = (size_t)rank * V;
+    memcpy(t->A, A_io, a_sz * sizeof(float));
+    memcpy(t->B, B_io, b_sz * sizeof(float));
+    t->step = step0;
+    for (int k = 0; k < n_steps; k++) {
+        memcpy(t->gA, gA_sums + (size_t)k * a_sz, a_sz * sizeof(float));
+        memcpy(t->gB, gB_sums + (size_t)k * b_sz, b_sz * sizeof(float));
+        /* train_step's mean (src/train.c:233-237) */
+        float inv = 1.0f / (float)n_pred[k];
+        for (size_t i = 0; i < a_sz; i++) t->gA[i] *= inv;
+        for (size_t i = 0; i < b_sz; i++) t->gB[i] *= inv;
+        adam_update(t);
+    }
+    memcpy(A_io, t->A, a_sz * sizeof(float));
+    memcpy(B_io, t->B, b_sz * sizeof(float));
+    train_free(t);
+    return 0;
+}

@@ -7,6 +7,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <chrono>
 #include <cmath>
 #include <cstdlib>
 #include <cstdio>
@@ -243,6 +244,14 @@ struct lora_ce_handle {
   // optional per-phase timing (events on the handle's stream)
   bool prof = false;
   cudaEvent_t ev[kNumPhases + 1] = {};
+  // optional timing of host-input steps (events captured into the step's
+  // graph): [0] compute stream at step start, [1] copy stream before the
+  // first chunk, [2 .. 2+chunks) after each chunk, [kMaxChunks + 2] result
+  // read back; plus the host's own time inside the last lora_ce_step
+  bool ctime = false;
+  cudaEvent_t tev[kMaxChunks + 3] = {};
+  int ctime_chunks = 0;
+  float host_us[2] = {0.f, 0.f};  // enqueue (or graph launch), wait for the result
 };
 
 namespace {
@@ -813,6 +822,7 @@ void drop_graphs(lora_ce_handle* h) {
 int enqueue_step(lora_ce_handle* h, bool host, const void* H, int dtype, int T,
                  const int32_t* targets, float* d_loss) {
   if (!host) return dispatch_step(h, H, dtype, T, targets, d_loss);
+  if (h->ctime) LCE_CUDA(cudaEventRecord(h->tev[0], h->stream));
   LCE_CUDA(cudaMemcpyAsync(h->in_tgt, targets, (size_t)T * 4, cudaMemcpyHostToDevice, h->stream));
   const int res_rows = kBM * h->pair;
   const int n_a1 = (T + res_rows - 1) / res_rows;
@@ -820,6 +830,7 @@ int enqueue_step(lora_ce_handle* h, bool host, const void* H, int dtype, int T,
   const size_t row_bytes = (size_t)h->d * elt_size(dtype);
   LCE_CUDA(cudaEventRecord(h->ev_start, h->stream));  // the previous step is done with in_H
   LCE_CUDA(cudaStreamWaitEvent(h->cstream, h->ev_start, 0));
+  if (h->ctime) LCE_CUDA(cudaEventRecord(h->tev[1], h->cstream));
   for (int c = 0; c < chunks; ++c) {
     const long long t_lo = tile_start(c, n_a1, chunks) * res_rows;
     const long long t_hi = std::min<long long>(T, tile_start(c + 1, n_a1, chunks) * res_rows);
@@ -827,11 +838,14 @@ int enqueue_step(lora_ce_handle* h, bool host, const void* H, int dtype, int T,
                              static_cast<const char*>(H) + t_lo * row_bytes,
                              (size_t)(t_hi - t_lo) * row_bytes, cudaMemcpyHostToDevice, h->cstream));
     LCE_CUDA(cudaEventRecord(h->ev_chunk[c], h->cstream));
+    if (h->ctime) LCE_CUDA(cudaEventRecord(h->tev[2 + c], h->cstream));
   }
+  h->ctime_chunks = chunks;
   int rc = dispatch_step(h, h->in_H, dtype, T, h->in_tgt, h->d_loss, chunks, h->ev_chunk);
   if (rc) return rc;
   LCE_CUDA(cudaMemcpyAsync(h->d_loss + 1, h->err, 4, cudaMemcpyDeviceToDevice, h->stream));
   LCE_CUDA(cudaMemcpyAsync(h->res_host, h->d_loss, 8, cudaMemcpyDeviceToHost, h->stream));
+  if (h->ctime) LCE_CUDA(cudaEventRecord(h->tev[kMaxChunks + 2], h->stream));
   return 0;
 }
 
@@ -1134,6 +1148,8 @@ int lora_ce_destroy(lora_ce_handle* h) {
   if (h->comm) nccl().CommDestroy(h->comm);
   for (cudaEvent_t e : h->ev)
     if (e) cudaEventDestroy(e);
+  for (cudaEvent_t e : h->tev)
+    if (e) cudaEventDestroy(e);
   free_all(h);
   free_streams(h);
   delete h;
@@ -1272,6 +1288,8 @@ int lora_ce_step_device(lora_ce_handle* h, const void* dH, int32_t dtype, int32_
 
 int lora_ce_step(lora_ce_handle* h, const void* H, int32_t dtype, int32_t T,
                  const int32_t* targets, float* loss_out) {
+  using clk = std::chrono::steady_clock;
+  const auto t0 = clk::now();
   int rc = check_step_args(h, H, dtype, T, targets);
   if (rc) return rc;
   LCE_CUDA(cudaSetDevice(h->cfg.device));
@@ -1280,7 +1298,11 @@ int lora_ce_step(lora_ce_handle* h, const void* H, int32_t dtype, int32_t T,
     h->poisoned = true;
     return rc;
   }
+  const auto t1 = clk::now();
   LCE_CUDA(cudaStreamSynchronize(h->stream));
+  const auto t2 = clk::now();
+  h->host_us[0] = std::chrono::duration<float, std::micro>(t1 - t0).count();
+  h->host_us[1] = std::chrono::duration<float, std::micro>(t2 - t1).count();
   float res[2];
   memcpy(res, h->res_host, 8);
   int e;
@@ -1293,6 +1315,32 @@ int lora_ce_step(lora_ce_handle* h, const void* H, int32_t dtype, int32_t T,
                                                       : "device pipeline error (bounded wait expired)");
   }
   if (loss_out) *loss_out = res[0];
+  return 0;
+}
+
+int lora_ce_apply_grads(lora_ce_handle* h, const float* gA, const float* gB, float n_pred) {
+  if (!h || !gA || !gB || !(n_pred > 0.f)) return fail(LORA_CE_EINVAL, "bad argument");
+  if (h->poisoned) return fail(LORA_CE_ESTATE, "handle poisoned by an earlier error");
+  LCE_CUDA(cudaSetDevice(h->cfg.device));
+  const int r = h->r, R = h->R, d = h->d, V = h->V;
+  const long long nA = (long long)d * R, nparam = nA + h->Vpad * R;
+  // G in the kernels' layout: [dA (d x R) | dB (pair-interleaved) | loss | n_pred]
+  std::vector<float> G((size_t)nparam + 2, 0.f);
+  for (int i = 0; i < d; ++i)
+    for (int j = 0; j < r; ++j) G[(size_t)i * R + j] = gA[(size_t)i * r + j];
+  for (int j = 0; j < r; ++j)
+    for (int v = 0; v < V; ++v) G[(size_t)(nA + bidx(v, j, R))] = gB[(size_t)j * V + v];
+  G[(size_t)nparam + 1] = n_pred;
+  LCE_CUDA(cudaMemcpyAsync(h->Gbuf, G.data(), G.size() * 4, cudaMemcpyHostToDevice, h->stream));
+  const int32_t next_step = h->step + 1;
+  AdamArgs aa = adam_args(h, nparam, next_step);
+  if (aa.clip > 0.f) lce_sqnorm<<<256, 256, 0, h->stream>>>(nparam, h->Gbuf, h->norm_parts);
+  const int blocks = (int)std::min<long long>((nparam + 255) / 256, 8LL * h->num_sms);
+  lce_adam<<<blocks, 256, 0, h->stream>>>(aa, h->params, h->mom1, h->mom2, h->Gbuf, h->gmean,
+                                           h->norm_parts, nullptr);
+  LCE_CUDA(cudaGetLastError());
+  LCE_CUDA(cudaStreamSynchronize(h->stream));
+  h->step = next_step;
   return 0;
 }
 
@@ -1347,6 +1395,44 @@ int32_t lora_ce_phase_times(lora_ce_handle* h, float* ms, int32_t cap) {
     if (cudaEventElapsedTime(&ms[i], h->ev[i], h->ev[i + 1]) != cudaSuccess)
       return fail(LORA_CE_ECUDA, "cudaEventElapsedTime failed");
   return n;
+}
+
+int lora_ce_set_copy_timing(lora_ce_handle* h, int32_t enable) {
+  if (!h) return fail(LORA_CE_EINVAL, "null handle");
+  LCE_CUDA(cudaSetDevice(h->cfg.device));
+  if (enable && !h->tev[0])
+    for (cudaEvent_t& e : h->tev) LCE_CUDA(cudaEventCreate(&e));
+  if ((enable != 0) != h->ctime) drop_graphs(h);  // recapture with (or without) the events
+  h->ctime = enable != 0;
+  return 0;
+}
+
+int32_t lora_ce_copy_times(lora_ce_handle* h, float* out, int32_t cap) {
+  if (!h || !out || !h->ctime || h->ctime_chunks < 1)
+    return fail(LORA_CE_EINVAL, "copy timing not enabled or no host-input step yet");
+  if (cudaSetDevice(h->cfg.device) != cudaSuccess ||
+      cudaEventSynchronize(h->tev[kMaxChunks + 2]) != cudaSuccess)
+    return fail(LORA_CE_ECUDA, "cudaEventSynchronize failed");
+  const int nc = h->ctime_chunks;
+  float v[4 + kMaxChunks + 1];
+  int n = 0;
+  v[n++] = h->host_us[0];
+  v[n++] = h->host_us[1];
+  float ms = 0.f;
+  if (cudaEventElapsedTime(&ms, h->tev[0], h->tev[1]) != cudaSuccess)
+    return fail(LORA_CE_ECUDA, "cudaEventElapsedTime failed");
+  v[n++] = ms;
+  for (int c = 0; c < nc; ++c) {
+    if (cudaEventElapsedTime(&ms, h->tev[1 + c], h->tev[2 + c]) != cudaSuccess)
+      return fail(LORA_CE_ECUDA, "cudaEventElapsedTime failed");
+    v[n++] = ms;
+  }
+  if (cudaEventElapsedTime(&ms, h->tev[0], h->tev[kMaxChunks + 2]) != cudaSuccess)
+    return fail(LORA_CE_ECUDA, "cudaEventElapsedTime failed");
+  v[n++] = ms;
+  const int m = cap < n ? cap : n;
+  for (int i = 0; i < m; ++i) out[i] = v[i];
+  return m;
 }
 
 const char* lora_ce_phase_name(int32_t i) {

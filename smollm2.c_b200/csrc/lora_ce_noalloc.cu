@@ -199,6 +199,12 @@ extern "C" int lora_ce_token_loss_noalloc(const uint16_t* d_W, int32_t vocab, in
   if (vocab < 1 || vocab > kNaMaxV) return na_fail(LORA_CE_EINVAL, "vocab must be in [1, 49152]");
   if (dim < 64 || dim % 64 != 0 || dim > kNaMaxD)
     return na_fail(LORA_CE_EINVAL, "dim must be a multiple of 64 in [64, 576]");
+  // every argument check comes before anything is enqueued or set up, so a
+  // rejected call leaves the stream and the shared scratch untouched
+  if ((reinterpret_cast<uintptr_t>(d_H) & 15) != 0)
+    return na_fail(LORA_CE_EINVAL, "hidden states must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(d_W) & 15) != 0)
+    return na_fail(LORA_CE_EINVAL, "W must be 16-byte aligned (TMA operand)");
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return na_fail(LORA_CE_ECUDA, "cudaGetDevice failed");
@@ -230,8 +236,6 @@ extern "C" int lora_ce_token_loss_noalloc(const uint16_t* d_W, int32_t vocab, in
     return na_fail(LORA_CE_ECUDA, "cudaMemcpyAsync failed");
   float* Bp = s->params + (size_t)d * R;
   na_pack_B<<<256, 256, 0, st>>>(d_B, V, Vpad, Bp);
-  if ((reinterpret_cast<uintptr_t>(d_H) & 15) != 0)
-    return na_fail(LORA_CE_EINVAL, "hidden states must be 16-byte aligned");
   lce_prep<R><<<(int)std::min<long long>((Tpad + 7) / 8, 592), 256, (size_t)d * R * 4, st>>>(
       d_H, h_dtype, 0, (int)Tpad, T, d, s->params, scale, d_targets, V, s->h16, s->tok, s->err,
       nullptr, 0, 0, nullptr, 0);

@@ -47,7 +47,8 @@ EXPORTS = [
     "lora_ce_token_loss_noalloc", "lora_ce_noalloc_last_error", "lora_ce_merge_weight",
     "lora_ce_merge_weight_device", "lora_ce_merge_last_error", "lora_ce_set_scale",
     "lora_ce_set_weight_q4k", "lora_ce_q4k_dequant", "lora_ce_q4k_dequant_device",
-    "lora_ce_q4k_last_error",
+    "lora_ce_q4k_last_error", "lora_ce_apply_grads", "lora_ce_set_copy_timing",
+    "lora_ce_copy_times",
 ]
 
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
@@ -108,6 +109,10 @@ def load_library() -> C.CDLL:
     lib.lora_ce_step_device.argtypes = [vp, vp, C.c_int32, C.c_int32, vp, vp]
     lib.lora_ce_get_grads.argtypes = [vp, vp, vp, C.POINTER(C.c_float), C.POINTER(C.c_float)]
     lib.lora_ce_get_token_loss.argtypes = [vp, vp, C.c_int32]
+    lib.lora_ce_apply_grads.argtypes = [vp, vp, vp, C.c_float]
+    lib.lora_ce_set_copy_timing.argtypes = [vp, C.c_int32]
+    lib.lora_ce_copy_times.argtypes = [vp, C.POINTER(C.c_float), C.c_int32]
+    lib.lora_ce_copy_times.restype = C.c_int32
     lib.lora_ce_nccl_unique_id.argtypes = [vp]
     lib.lora_ce_comm_init.argtypes = [vp, C.c_int32, C.c_int32, vp]
     lib.lora_ce_sync.argtypes = [vp]
@@ -310,6 +315,16 @@ class LoraCE:
         _check(self.lib.lora_ce_get_token_loss(self.h, _ptr(out), T), "get_token_loss")
         return out
 
+    def apply_grads(self, gA_sum: np.ndarray, gB_sum: np.ndarray, n_pred: float) -> None:
+        """One optimizer step from gradient sums over n_pred positions
+        (lora_ce_apply_grads)."""
+        gA = np.ascontiguousarray(gA_sum, np.float32)
+        gB = np.ascontiguousarray(gB_sum, np.float32)
+        assert gA.shape == (self.cfg.dim, self.cfg.rank)
+        assert gB.shape == (self.cfg.rank, self.cfg.vocab)
+        _check(self.lib.lora_ce_apply_grads(self.h, _ptr(gA), _ptr(gB), float(n_pred)),
+               "apply_grads")
+
     # -- steps
     def step(self, H: np.ndarray, targets: np.ndarray, dtype: int | None = None) -> float:
         """H: [T][d] as bf16 bits (uint16, dtype BF16 by default), float16 or
@@ -355,6 +370,21 @@ class LoraCE:
         if n < 0:
             _check(n, "phase_times")
         return {self.lib.lora_ce_phase_name(i).decode(): float(buf[i]) for i in range(n)}
+
+    def set_copy_timing(self, enable: bool = True) -> None:
+        _check(self.lib.lora_ce_set_copy_timing(self.h, int(enable)), "set_copy_timing")
+
+    def copy_times(self) -> dict:
+        """Where the last host-input step's time went (needs
+        set_copy_timing(True)): host_us (enqueue), wait_us (host waiting for
+        the result), copy_wait_ms, chunk_ms [...], step_ms."""
+        buf = (C.c_float * 16)()
+        n = self.lib.lora_ce_copy_times(self.h, buf, 16)
+        if n < 0:
+            _check(n, "copy_times")
+        v = [float(buf[i]) for i in range(n)]
+        return {"host_us": v[0], "wait_us": v[1], "copy_wait_ms": v[2], "chunk_ms": v[3:-1],
+                "step_ms": v[-1]}
 
     @property
     def stream(self) -> int:

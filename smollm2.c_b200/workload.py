@@ -99,3 +99,17 @@ def q4k_dequant_np(blocks: np.ndarray) -> np.ndarray:
     mm = (dmin[:, None] * mn.astype(np.float32)).astype(np.float32)
     p = (dsc[:, :, None] * nib.astype(np.float32)).astype(np.float32)
     return (p - mm[:, :, None]).astype(np.float32).reshape(-1)
+
+
+def make_adam_inputs(seed: int, d: int, V: int, r: int, k: int):
+    """An adapter and k steps of gradient sums for optimizer-only checks:
+    A [d][r], B [r][V], gA [k][d][r], gB [k][r][V] with magnitudes spread
+    over many decades (and some exact zeros), n_pred [k]."""
+    rng = np.random.default_rng(seed)
+    A = (rng.standard_normal((d, r)) / np.sqrt(d)).astype(np.float32)
+    B = (rng.standard_normal((r, V)) * 1e-3).astype(np.float32)
+    gA = (rng.standard_normal((k, d, r)) * 10.0 ** rng.uniform(-6, 2, (k, d, r))).astype(np.float32)
+    gB = (rng.standard_normal((k, r, V)) * 10.0 ** rng.uniform(-9, 1, (k, r, V))).astype(np.float32)
+    gB[:, :, ::97] = 0.0
+    n_pred = rng.integers(1, 70000, k).astype(np.int32)
+    return A, B, gA, gB, n_pred

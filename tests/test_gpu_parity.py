@@ -418,3 +418,26 @@ def test_rank64_adamw_clip_and_graph_replay(oracle):
         state, Ao, Bo = ref["state"], ref["A"], ref["B"]
         assert abs(runs[0][0][k] - ref["loss"]) <= LOSS_RTOL * ref["loss"]
     assert rel(runs[0][1], Ao) <= L2_RTOL and rel(runs[0][2], Bo) <= L2_RTOL
+
+
+@pytest.mark.parametrize("V,d,r", [(49152, 576, 4), (3001, 64, 13), (49152, 576, 64)])
+def test_adam_kernel_bit_exact_with_reference_adam_update(V, d, r):
+    """lce_adam (through lora_ce_apply_grads) against the reference's own
+    mean + adam_update (src/train.c:230-239, 175-196; oracle/_ref) on
+    identical gradient sums: three updates with the moments carried, the
+    adapter bit-equal after each run (weight decay 0, no clip: the
+    reference's Adam)."""
+    import oracle as orc
+
+    k = 3
+    A, B, gA, gB, n_pred = wl.make_adam_inputs(V + r, d, V, r, k)
+    m = lora_ce.LoraCE(lora_ce.default_config(d, V, r, 16, scale=2.0, lr=1e-3))
+    m.set_adapter(A, B, 0)
+    for i in range(k):
+        m.apply_grads(gA[i], gB[i], float(n_pred[i]))
+    A1, B1, step = m.get_adapter()
+    m.close()
+    Ar, Br = orc.RefHarness().adam_steps(A, B, gA, gB, n_pred, 1e-3)
+    assert step == k
+    assert np.array_equal(A1.view(np.uint32), Ar.view(np.uint32))
+    assert np.array_equal(B1.view(np.uint32), Br.view(np.uint32))

@@ -166,3 +166,19 @@ def test_q4k_restatements_agree(oracle, golden):
     a = oracle.q4k_dequant(blocks)
     np.testing.assert_array_equal(a.view(np.uint32), wl.q4k_dequant_np(blocks).view(np.uint32))
     assert sha(a) == golden["q4k_seed4_49152x576_sha"]
+
+
+@pytest.mark.skipif(not orc.ref_available(), reason="reference not built here")
+def test_oracle_adam_bit_exact_with_reference_adam_update(oracle):
+    """The oracle's mean + Adam against the reference's own adam_update
+    (src/train.c:175-196, via oracle/_ref) on identical gradient sums, three
+    updates with the moments carried: bit-equal."""
+    d, V, r, k = 64, 3001, 5, 3
+    A, B, gA, gB, n_pred = wl.make_adam_inputs(11, d, V, r, k)
+    Ar, Br = orc.RefHarness().adam_steps(A, B, gA, gB, n_pred, 1e-3)
+    Ao, Bo, state = A, B, None
+    for i in range(k):
+        Ao, Bo, state = oracle.adam(Ao, Bo, gA[i], gB[i], n_pred[i], 1e-3, state=state)
+    assert state["step"] == k
+    assert np.array_equal(Ao.view(np.uint32), Ar.view(np.uint32))
+    assert np.array_equal(Bo.view(np.uint32), Br.view(np.uint32))
