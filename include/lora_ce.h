@@ -155,6 +155,14 @@ int lora_ce_nccl_unique_id(void* id128);
 int lora_ce_comm_init(lora_ce_handle* h, int32_t nranks, int32_t rank,
                       const void* id128);
 
+/* Bound, in ms (default 60000), on every wait that involves the
+ * communicator: its initialisation, an all-reduce's enqueue and a step's
+ * completion.  The communicator is non-blocking: a collective that does not
+ * complete in time (a peer rank that left) or that reports an asynchronous
+ * error is aborted (ncclCommAbort), the call returns LORA_CE_ENCCL and the
+ * handle is poisoned, so every rank sees an error instead of a hang. */
+int lora_ce_set_comm_timeout(lora_ce_handle* h, int32_t timeout_ms);
+
 /* Wait for the handle's stream and report a device-side error of the steps
  * launched since the last check (lora_ce_step_device does not wait). */
 int lora_ce_sync(lora_ce_handle* h);

@@ -158,9 +158,25 @@ int ref_merge_weight(const uint16_t* W, const float* A, const float* B, int dim,
 /* The reference's own train_run (src/train.c:295-389) over a packed dataset,
  * every sample's hidden rows served from H by position, with the adapter
  * from train_create (seeded Kaiming A, B = 0).  Returns train_run's rc. */
+int ref_train_run_mem(int d, int V, int rank, int alpha, float lr, int seq_max, int seed,
+                      int epochs, int max_steps, int checkpoint_every, const uint16_t* W,
+                      const float* H, int n_pos, const char* packed, const char* out_dir,
+                      long simulate_mem_kb);
+
 int ref_train_run(int d, int V, int rank, int alpha, float lr, int seq_max, int seed,
                   int epochs, int max_steps, int checkpoint_every, const uint16_t* W,
                   const float* H, int n_pos, const char* packed, const char* out_dir) {
+    return ref_train_run_mem(d, V, rank, alpha, lr, seq_max, seed, epochs, max_steps,
+                             checkpoint_every, W, H, n_pos, packed, out_dir, 0);
+}
+
+/* ref_train_run with train_params.simulate_mem_kb set: the memory figure
+ * train_run's watchdog compares with its emergency threshold
+ * (src/train.c:355-369). */
+int ref_train_run_mem(int d, int V, int rank, int alpha, float lr, int seq_max, int seed,
+                      int epochs, int max_steps, int checkpoint_every, const uint16_t* W,
+                      const float* H, int n_pos, const char* packed, const char* out_dir,
+                      long simulate_mem_kb) {
     forward_ctx f = {d, V, W, H, n_pos, 0, NULL};
     f.wrow = (float*)malloc((size_t)d * sizeof(float));
     train_params p;
@@ -175,6 +191,7 @@ int ref_train_run(int d, int V, int rank, int alpha, float lr, int seq_max, int 
     p.max_steps = max_steps;
     p.checkpoint_every = checkpoint_every;
     p.seed = seed;
+    p.simulate_mem_kb = simulate_mem_kb;
     train_state* t = train_create(&f, &p);
     int rc = t ? train_run(t, packed, &p, out_dir) : -1;
     fflush(stdout);

@@ -8,6 +8,7 @@
 #include <nccl.h>
 
 #include <chrono>
+#include <thread>
 #include <cmath>
 #include <cstdlib>
 #include <cstdio>
@@ -98,13 +99,21 @@ long long round_up(long long x, long long m) { return (x + m - 1) / m * m; }
 // NCCL is loaded on first use (a communicator is only needed for
 // multi-GPU runs), preferring a libnccl already loaded in the process (for
 // example PyTorch's) so that two different NCCL builds never meet in one
-// process; otherwise the system libnccl.so.2.
+// process; otherwise the system libnccl.so.2.  Communicators are
+// non-blocking: every NCCL call returns at once, its completion (and any
+// asynchronous error) is polled against a host deadline, and a collective
+// that does not finish in time is aborted (ncclCommAbort ends NCCL's
+// kernels) and reported as LORA_CE_ENCCL.
 struct NcclApi {
   ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
-  ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
   ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                             cudaStream_t) = nullptr;
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*CommFinalize)(ncclComm_t) = nullptr;
   ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+  const char* (*GetErrorString)(ncclResult_t) = nullptr;
   bool ok = false;
 };
 
@@ -116,16 +125,45 @@ const NcclApi& nccl() {
     void* lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
     if (!lib) lib = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
     if (lib) {
-      api.GetUniqueId = reinterpret_cast<decltype(api.GetUniqueId)>(dlsym(lib, "ncclGetUniqueId"));
-      api.CommInitRank =
-          reinterpret_cast<decltype(api.CommInitRank)>(dlsym(lib, "ncclCommInitRank"));
-      api.AllReduce = reinterpret_cast<decltype(api.AllReduce)>(dlsym(lib, "ncclAllReduce"));
-      api.CommDestroy =
-          reinterpret_cast<decltype(api.CommDestroy)>(dlsym(lib, "ncclCommDestroy"));
-      api.ok = api.GetUniqueId && api.CommInitRank && api.AllReduce && api.CommDestroy;
+      auto sym = [lib](auto& fn, const char* name) {
+        fn = reinterpret_cast<std::remove_reference_t<decltype(fn)>>(dlsym(lib, name));
+      };
+      sym(api.GetUniqueId, "ncclGetUniqueId");
+      sym(api.CommInitRankConfig, "ncclCommInitRankConfig");
+      sym(api.AllReduce, "ncclAllReduce");
+      sym(api.CommGetAsyncError, "ncclCommGetAsyncError");
+      sym(api.CommFinalize, "ncclCommFinalize");
+      sym(api.CommDestroy, "ncclCommDestroy");
+      sym(api.CommAbort, "ncclCommAbort");
+      sym(api.GetErrorString, "ncclGetErrorString");
+      api.ok = api.GetUniqueId && api.CommInitRankConfig && api.AllReduce &&
+               api.CommGetAsyncError && api.CommFinalize && api.CommDestroy && api.CommAbort;
     }
   }
   return api;
+}
+
+using Clock = std::chrono::steady_clock;
+
+double ms_since(Clock::time_point t0) {
+  return std::chrono::duration<double, std::milli>(Clock::now() - t0).count();
+}
+
+// Poll a non-blocking communicator until its last call has completed
+// (ncclSuccess), failed, or `timeout_ms` passed (ncclInProgress returned).
+ncclResult_t nccl_settle(ncclComm_t comm, double timeout_ms) {
+  const Clock::time_point t0 = Clock::now();
+  for (;;) {
+    ncclResult_t st = ncclInProgress;
+    if (nccl().CommGetAsyncError(comm, &st) != ncclSuccess) return ncclInternalError;
+    if (st != ncclInProgress) return st;
+    if (ms_since(t0) > timeout_ms) return ncclInProgress;
+    std::this_thread::yield();
+  }
+}
+
+const char* nccl_str(ncclResult_t r) {
+  return nccl().GetErrorString ? nccl().GetErrorString(r) : "NCCL error";
 }
 
 // Largest number of CTA segments any resident tile's run of n_b tiles is
@@ -183,8 +221,9 @@ struct lora_ce_handle {
     float* d_loss = nullptr;
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
-    cudaGraphNode_t adam = nullptr;
+    cudaGraphNode_t adam = nullptr;  // the node that takes the Adam arguments
     cudaKernelNodeParams adam_p{};
+    int adam_nargs = 0;
     long long nparam = 0;
     int launches = 0;
     unsigned long long last_use = 0;
@@ -241,6 +280,8 @@ struct lora_ce_handle {
   CUtensorMap mapW_strT{}, mapWa_strT{}, mapXv{};
   ncclComm_t comm = nullptr;
   int nranks = 1, rank = 0;
+  double comm_timeout_ms = 60000.0;  // bound on any wait that involves a collective
+  bool stuck = false;  // streams still busy after an aborted collective
   // optional per-phase timing (events on the handle's stream)
   bool prof = false;
   cudaEvent_t ev[kNumPhases + 1] = {};
@@ -309,6 +350,23 @@ int check_cfg(const lora_ce_config* c) {
       !(c->clip_norm >= 0.f) || !std::isfinite(c->scale))
     return fail(LORA_CE_EINVAL, "bad optimizer hyper-parameters");
   return 0;
+}
+
+// The finalize kernel blocks (a grid-stride pass over the parameters) and
+// the norm partials they may write.
+constexpr int kFinBlocksMax = 2048;
+// Parameter counts of the two kernels whose AdamArgs a graph replay updates.
+constexpr int kAdamArgs = 8;
+constexpr int kFinalizeArgs = 21;
+
+const void* fused_finalize_fn(int R) {
+  switch (R) {
+    case 4: return reinterpret_cast<const void*>(lce_finalize<4, kFinAdam>);
+    case 8: return reinterpret_cast<const void*>(lce_finalize<8, kFinAdam>);
+    case 16: return reinterpret_cast<const void*>(lce_finalize<16, kFinAdam>);
+    case 32: return reinterpret_cast<const void*>(lce_finalize<32, kFinAdam>);
+    default: return reinterpret_cast<const void*>(lce_finalize<64, kFinAdam>);
+  }
 }
 
 using GemmKernel = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap,
@@ -721,30 +779,40 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
     ++launches;
   }
   const long long nparam = (long long)d * R + h->Vpad * R;
+  const int32_t next_step = h->step + 1;
+  AdamArgs aa = adam_args(h, nparam, next_step);
+  // Without a collective the optimizer fuses into the finalize pass: the
+  // whole update (no clip) or the clip's norm partials (clip).  With one,
+  // the all-reduce has to sit between the gradient sums and the update.
+  const int fin_blocks = (int)std::min<long long>((nparam + 255) / 256, kFinBlocksMax);
+  const int fin_mode = h->comm ? kFinG : aa.clip > 0.f ? kFinNorm : kFinAdam;
+  if (fin_mode == kFinNorm) aa.n_norm_parts = fin_blocks;
   mark(h, kPhFinalize);
   {
-    const int blocks = (int)std::min<long long>((nparam + 255) / 256, 8LL * h->num_sms);
-    lce_finalize<R><<<blocks, 256, 0, st>>>(T, cp2, d, V, h->Vpad, n_chunks, h->gAp, res_rows, n_b2, G2,
-                                            h->gBp, h->corr_fx, h->loss_tok, h->Gbuf);
+    auto fin = fin_mode == kFinAdam ? lce_finalize<R, kFinAdam>
+               : fin_mode == kFinNorm ? lce_finalize<R, kFinNorm> : lce_finalize<R, kFinG>;
+    fin<<<fin_blocks, 256, 0, st>>>(aa, T, cp2, d, V, h->Vpad, n_chunks, h->gAp, res_rows, n_b2,
+                                    G2, h->gBp, h->corr_fx, h->loss_tok, h->Gbuf, h->params,
+                                    h->mom1, h->mom2, h->gmean, h->norm_parts, d_loss_out);
     ++launches;
   }
   // 7. data-parallel sum over ranks
   mark(h, kPhAllReduce);
   if (h->comm) {
-    if (nccl().AllReduce(h->Gbuf, h->Gbuf, (size_t)(nparam + 2), ncclFloat, ncclSum, h->comm,
-                         st) != ncclSuccess)
-      return fail(LORA_CE_ENCCL, "ncclAllReduce failed");
+    ncclResult_t r = nccl().AllReduce(h->Gbuf, h->Gbuf, (size_t)(nparam + 2), ncclFloat, ncclSum,
+                                      h->comm, st);
+    if (r == ncclInProgress) r = nccl_settle(h->comm, h->comm_timeout_ms);
+    if (r != ncclSuccess)
+      return fail(LORA_CE_ENCCL, std::string("ncclAllReduce: ") + nccl_str(r));
   }
   // 8. clip norm (optional), 9. Adam
-  const int32_t next_step = h->step + 1;
-  AdamArgs aa = adam_args(h, nparam, next_step);
   mark(h, kPhNorm);
-  if (aa.clip > 0.f) {
+  if (fin_mode == kFinG && aa.clip > 0.f) {
     lce_sqnorm<<<256, 256, 0, st>>>(nparam, h->Gbuf, h->norm_parts);
     ++launches;
   }
   mark(h, kPhAdam);
-  {
+  if (fin_mode != kFinAdam) {
     const int blocks = (int)std::min<long long>((nparam + 255) / 256, 8LL * h->num_sms);
     lce_adam<<<blocks, 256, 0, st>>>(aa, h->params, h->mom1, h->mom2, h->Gbuf, h->gmean,
                                      h->norm_parts, d_loss_out);
@@ -784,10 +852,59 @@ int check_step_args(lora_ce_handle* h, const void* H, int dtype, int T, const in
 
 int elt_size(int dtype) { return dtype == LORA_CE_F32 ? 4 : 2; }
 
+// Abort the communicator after a failed or expired collective: NCCL's
+// kernels end, the handle's streams drain, the graphs (which hold the
+// communicator's calls) are dropped and the handle is poisoned.
+int abort_comm(lora_ce_handle* h, const std::string& why) {
+  nccl().CommAbort(h->comm);
+  h->comm = nullptr;
+  h->poisoned = true;
+  // the streams should drain once NCCL's kernels have ended; the wait for
+  // that is bounded too, and streams that do not drain are left alone (the
+  // handle then keeps its device memory at destroy rather than block)
+  const Clock::time_point t0 = Clock::now();
+  while (cudaStreamQuery(h->stream) == cudaErrorNotReady ||
+         cudaStreamQuery(h->cstream) == cudaErrorNotReady) {
+    if (ms_since(t0) > h->comm_timeout_ms) {
+      h->stuck = true;
+      return fail(LORA_CE_ENCCL, why + "; the handle's streams did not drain after the abort");
+    }
+    std::this_thread::yield();
+  }
+  cudaGetLastError();
+  drop_graphs(h);
+  return fail(LORA_CE_ENCCL, why);
+}
+
+// Wait for the handle's stream.  With a communicator the wait is bounded:
+// the stream is polled together with the communicator's asynchronous
+// error, and a collective that has not completed within comm_timeout_ms
+// (a peer that left, a failed link) is aborted.
+int wait_stream(lora_ce_handle* h) {
+  if (!h->comm) {
+    LCE_CUDA(cudaStreamSynchronize(h->stream));
+    return 0;
+  }
+  const Clock::time_point t0 = Clock::now();
+  for (;;) {
+    const cudaError_t q = cudaStreamQuery(h->stream);
+    if (q == cudaSuccess) return 0;
+    if (q != cudaErrorNotReady) return fail(LORA_CE_ECUDA, cudaGetErrorString(q));
+    ncclResult_t ae = ncclSuccess;
+    nccl().CommGetAsyncError(h->comm, &ae);
+    if (ae != ncclSuccess && ae != ncclInProgress)
+      return abort_comm(h, std::string("NCCL asynchronous error: ") + nccl_str(ae));
+    if (ms_since(t0) > h->comm_timeout_ms)
+      return abort_comm(h, "collective timed out (a peer rank did not take part); "
+                           "communicator aborted, handle poisoned");
+    std::this_thread::yield();
+  }
+}
+
 int check_device_error(lora_ce_handle* h) {
   int e = 0;
   LCE_CUDA(cudaMemcpyAsync(&e, h->err, sizeof(int), cudaMemcpyDeviceToHost, h->stream));
-  LCE_CUDA(cudaStreamSynchronize(h->stream));
+  if (int rc = wait_stream(h)) return rc;
   if (e != 0) {
     h->poisoned = true;
     char buf[96];
@@ -815,6 +932,16 @@ void drop_graphs(lora_ce_handle* h) {
   for (auto& gph : h->graphs) drop_graph(gph);
 }
 
+// A timing event on stream s.  Under stream capture a plain record only
+// orders work inside the graph, so timing events become external event
+// nodes there, recorded each time the graph runs.
+cudaError_t record_timing(cudaEvent_t e, cudaStream_t s) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cs) != cudaSuccess) return cudaErrorUnknown;
+  return cs == cudaStreamCaptureStatusActive ? cudaEventRecordWithFlags(e, s, cudaEventRecordExternal)
+                                             : cudaEventRecord(e, s);
+}
+
 // Everything one step enqueues on the handle's streams.  Host-input steps
 // (H, targets in host memory) copy them in (h in chunks on the copy stream,
 // see run_step) and read [loss, error code] back into res_host;
@@ -822,7 +949,7 @@ void drop_graphs(lora_ce_handle* h) {
 int enqueue_step(lora_ce_handle* h, bool host, const void* H, int dtype, int T,
                  const int32_t* targets, float* d_loss) {
   if (!host) return dispatch_step(h, H, dtype, T, targets, d_loss);
-  if (h->ctime) LCE_CUDA(cudaEventRecord(h->tev[0], h->stream));
+  if (h->ctime) LCE_CUDA(record_timing(h->tev[0], h->stream));
   LCE_CUDA(cudaMemcpyAsync(h->in_tgt, targets, (size_t)T * 4, cudaMemcpyHostToDevice, h->stream));
   const int res_rows = kBM * h->pair;
   const int n_a1 = (T + res_rows - 1) / res_rows;
@@ -830,7 +957,7 @@ int enqueue_step(lora_ce_handle* h, bool host, const void* H, int dtype, int T,
   const size_t row_bytes = (size_t)h->d * elt_size(dtype);
   LCE_CUDA(cudaEventRecord(h->ev_start, h->stream));  // the previous step is done with in_H
   LCE_CUDA(cudaStreamWaitEvent(h->cstream, h->ev_start, 0));
-  if (h->ctime) LCE_CUDA(cudaEventRecord(h->tev[1], h->cstream));
+  if (h->ctime) LCE_CUDA(record_timing(h->tev[1], h->cstream));
   for (int c = 0; c < chunks; ++c) {
     const long long t_lo = tile_start(c, n_a1, chunks) * res_rows;
     const long long t_hi = std::min<long long>(T, tile_start(c + 1, n_a1, chunks) * res_rows);
@@ -838,14 +965,14 @@ int enqueue_step(lora_ce_handle* h, bool host, const void* H, int dtype, int T,
                              static_cast<const char*>(H) + t_lo * row_bytes,
                              (size_t)(t_hi - t_lo) * row_bytes, cudaMemcpyHostToDevice, h->cstream));
     LCE_CUDA(cudaEventRecord(h->ev_chunk[c], h->cstream));
-    if (h->ctime) LCE_CUDA(cudaEventRecord(h->tev[2 + c], h->cstream));
+    if (h->ctime) LCE_CUDA(record_timing(h->tev[2 + c], h->cstream));
   }
   h->ctime_chunks = chunks;
   int rc = dispatch_step(h, h->in_H, dtype, T, h->in_tgt, h->d_loss, chunks, h->ev_chunk);
   if (rc) return rc;
   LCE_CUDA(cudaMemcpyAsync(h->d_loss + 1, h->err, 4, cudaMemcpyDeviceToDevice, h->stream));
   LCE_CUDA(cudaMemcpyAsync(h->res_host, h->d_loss, 8, cudaMemcpyDeviceToHost, h->stream));
-  if (h->ctime) LCE_CUDA(cudaEventRecord(h->tev[kMaxChunks + 2], h->stream));
+  if (h->ctime) LCE_CUDA(record_timing(h->tev[kMaxChunks + 2], h->stream));
   return 0;
 }
 
@@ -890,19 +1017,24 @@ lora_ce_handle::StepGraph* step_graph(lora_ce_handle* h, bool host, const void* 
   cudaGraphGetNodes(graph, nullptr, &n);
   std::vector<cudaGraphNode_t> nodes(n);
   cudaGraphGetNodes(graph, nodes.data(), &n);
+  // (lce_adam, or the finalize kernel with the update fused in; both take
+  // the AdamArgs as their first parameter)
   cudaGraphNode_t adam = nullptr;
   cudaKernelNodeParams ap{};
+  int nargs = 0;
+  const void* fused = fused_finalize_fn(h->R);
   for (cudaGraphNode_t nd : nodes) {
     cudaGraphNodeType ty;
     if (cudaGraphNodeGetType(nd, &ty) != cudaSuccess || ty != cudaGraphNodeTypeKernel) continue;
     cudaKernelNodeParams p{};
-    if (cudaGraphKernelNodeGetParams(nd, &p) == cudaSuccess &&
-        p.func == reinterpret_cast<void*>(lce_adam)) {
+    if (cudaGraphKernelNodeGetParams(nd, &p) != cudaSuccess) continue;
+    if (p.func == reinterpret_cast<void*>(lce_adam) || p.func == fused) {
       adam = nd;
       ap = p;
+      nargs = p.func == fused ? kFinalizeArgs : kAdamArgs;
     }
   }
-  if (!adam) {
+  if (!adam || !ap.kernelParams) {
     cudaGraphExecDestroy(exec);
     cudaGraphDestroy(graph);
     return nullptr;
@@ -918,6 +1050,7 @@ lora_ce_handle::StepGraph* step_graph(lora_ce_handle* h, bool host, const void* 
   slot->exec = exec;
   slot->adam = adam;
   slot->adam_p = ap;
+  slot->adam_nargs = nargs;
   slot->nparam = (long long)h->d * h->R + h->Vpad * h->R;
   slot->launches = new_launches;
   slot->last_use = ++h->graph_clock;
@@ -926,10 +1059,15 @@ lora_ce_handle::StepGraph* step_graph(lora_ce_handle* h, bool host, const void* 
 
 // Replay: set this step's Adam arguments, launch the graph.
 int launch_step_graph(lora_ce_handle* h, lora_ce_handle::StepGraph* gph, int T) {
-  AdamArgs aa = adam_args(h, gph->nparam, h->step + 1);
-  float* d_loss = gph->host ? h->d_loss : gph->d_loss;
-  void* args[] = {&aa, &h->params, &h->mom1, &h->mom2, &h->Gbuf, &h->gmean, &h->norm_parts,
-                  &d_loss};
+  // the captured AdamArgs with this step's bias corrections; every other
+  // argument keeps its captured value
+  AdamArgs aa = *static_cast<const AdamArgs*>(gph->adam_p.kernelParams[0]);
+  const AdamArgs fresh = adam_args(h, gph->nparam, h->step + 1);
+  aa.b1t = fresh.b1t;
+  aa.b2t = fresh.b2t;
+  void* args[kFinalizeArgs];
+  args[0] = &aa;
+  for (int i = 1; i < gph->adam_nargs; ++i) args[i] = gph->adam_p.kernelParams[i];
   cudaKernelNodeParams p = gph->adam_p;
   p.kernelParams = args;
   p.extra = nullptr;
@@ -1091,7 +1229,7 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
   if (!rc) rc = dalloc(&h->gAp, (size_t)((Tcap + kDAChunk - 1) / kDAChunk) * d * R);
   if (!rc) rc = dalloc(&h->gBp, (size_t)s2 * Vpad * R);
   if (!rc) rc = dalloc(&h->corr_fx, (size_t)Vpad * R);
-  if (!rc) rc = dalloc(&h->norm_parts, 256);
+  if (!rc) rc = dalloc(&h->norm_parts, kFinBlocksMax);
   if (!rc) rc = dalloc(&h->err, 1);
   if (!rc) rc = dalloc(&h->d_loss, 2);
   if (!rc) rc = dalloc(reinterpret_cast<char**>(&h->in_H), (size_t)Tcap * d * 4);
@@ -1142,10 +1280,23 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
 int lora_ce_destroy(lora_ce_handle* h) {
   if (!h) return 0;
   cudaSetDevice(h->cfg.device);
+  if (h->stuck) {  // never block on streams an aborted collective left busy
+    delete h;
+    return fail(LORA_CE_ENCCL, "handle destroyed with busy streams; its device memory is kept");
+  }
   if (h->stream) cudaStreamSynchronize(h->stream);
   if (h->cstream) cudaStreamSynchronize(h->cstream);
   drop_graphs(h);  // graphs holding NCCL calls go before the communicator
-  if (h->comm) nccl().CommDestroy(h->comm);
+  if (h->comm) {
+    // finalize (flush), bounded; a communicator that does not settle is aborted
+    ncclResult_t r = nccl().CommFinalize(h->comm);
+    if (r == ncclInProgress) r = nccl_settle(h->comm, h->comm_timeout_ms);
+    if (r == ncclSuccess)
+      nccl().CommDestroy(h->comm);
+    else
+      nccl().CommAbort(h->comm);
+    h->comm = nullptr;
+  }
   for (cudaEvent_t e : h->ev)
     if (e) cudaEventDestroy(e);
   for (cudaEvent_t e : h->tev)
@@ -1299,7 +1450,7 @@ int lora_ce_step(lora_ce_handle* h, const void* H, int32_t dtype, int32_t T,
     return rc;
   }
   const auto t1 = clk::now();
-  LCE_CUDA(cudaStreamSynchronize(h->stream));
+  if ((rc = wait_stream(h))) return rc;
   const auto t2 = clk::now();
   h->host_us[0] = std::chrono::duration<float, std::micro>(t1 - t0).count();
   h->host_us[1] = std::chrono::duration<float, std::micro>(t2 - t1).count();
@@ -1369,10 +1520,25 @@ int lora_ce_comm_init(lora_ce_handle* h, int32_t nranks, int32_t rank, const voi
   ncclUniqueId id;
   memcpy(&id, id128, 128);
   drop_graphs(h);  // steps captured without the all-reduce
-  if (nccl().CommInitRank(&h->comm, nranks, id, rank) != ncclSuccess)
-    return fail(LORA_CE_ENCCL, "ncclCommInitRank failed");
+  ncclConfig_t config = NCCL_CONFIG_INITIALIZER;
+  config.blocking = 0;
+  ncclComm_t comm = nullptr;
+  ncclResult_t r = nccl().CommInitRankConfig(&comm, nranks, id, rank, &config);
+  if (r == ncclInProgress) r = nccl_settle(comm, h->comm_timeout_ms);
+  if (r != ncclSuccess) {
+    if (comm) nccl().CommAbort(comm);
+    return fail(LORA_CE_ENCCL, std::string("ncclCommInitRankConfig: ") +
+                                   (r == ncclInProgress ? "timed out" : nccl_str(r)));
+  }
+  h->comm = comm;
   h->nranks = nranks;
   h->rank = rank;
+  return 0;
+}
+
+int lora_ce_set_comm_timeout(lora_ce_handle* h, int32_t timeout_ms) {
+  if (!h || timeout_ms < 1) return fail(LORA_CE_EINVAL, "bad argument");
+  h->comm_timeout_ms = (double)timeout_ms;
   return 0;
 }
 

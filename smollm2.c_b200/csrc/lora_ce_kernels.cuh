@@ -1350,20 +1350,60 @@ __global__ void __launch_bounds__(32 * da_rows(R)) lce_dA_partial(int T, int d,
   }
 }
 
+struct AdamArgs {
+  long long n;       // d*R + V*R parameters
+  float lr, b1, b2, c1, c2, eps, wd;  // c1 = 1 - b1, c2 = 1 - b2 (in f32)
+  float b1t, b2t;    // 1 - b^step, computed on the host with powf
+  float clip;
+  int n_norm_parts;
+};
+
+// The optimizer update of one parameter from its mean gradient g: decoupled
+// decay, then the Adam update (src/train.c:175-196), written with
+// explicitly rounded operations so that it is the reference's f32
+// arithmetic, op for op.
+__device__ __forceinline__ void adam_element(const AdamArgs& a, long long k, float g,
+                                             float* __restrict__ params,
+                                             float* __restrict__ mom1,
+                                             float* __restrict__ mom2) {
+  float p = params[k];
+  if (a.wd > 0.f) p = __fsub_rn(p, __fmul_rn(__fmul_rn(a.lr, a.wd), p));
+  const float m = __fadd_rn(__fmul_rn(a.b1, mom1[k]), __fmul_rn(a.c1, g));
+  const float v = __fadd_rn(__fmul_rn(a.b2, mom2[k]), __fmul_rn(__fmul_rn(a.c2, g), g));
+  mom1[k] = m;
+  mom2[k] = v;
+  const float mhat = __fdiv_rn(m, a.b1t);
+  const float vhat = __fdiv_rn(v, a.b2t);
+  p = __fsub_rn(p, __fdiv_rn(__fmul_rn(a.lr, mhat), __fadd_rn(__fsqrt_rn(vhat), a.eps)));
+  params[k] = p;
+}
+
 // Pack the step's gradient sums: G = [dA (d*R) | dB (V*R, vocab-major) |
 // sum of losses | n_pred].  Every output element is summed in a fixed
-// order, so the step is deterministic.
-template <int R>
-__global__ void lce_finalize(int T, int cparts, int d, int V, long long Vpad, int n_chunks,
-                             const float* __restrict__ gAp, int res_rows, int n_b2, int G2,
-                             const float* __restrict__ gBp,
-                             unsigned long long* __restrict__ corr_fx,
-                             const float* __restrict__ loss_tok, float* __restrict__ Gbuf) {
+// order, so the step is deterministic.  Modes (template kMode):
+//   kFinG:     G only (a collective and/or the clip follow);
+//   kFinNorm:  G and, per block, the sum of squares of g = G / n_pred (the
+//              clip's global norm without a separate pass; no collective);
+//   kFinAdam:  G, then g = G / n_pred and the whole optimizer update of the
+//              element in the same pass (no collective, no clip): the
+//              finalize, norm and Adam kernels of a step fused into one.
+// Without a collective n_pred is this step's T.
+enum : int { kFinG = 0, kFinNorm = 1, kFinAdam = 2 };
+template <int R, int kMode>
+__global__ void __launch_bounds__(256) lce_finalize(
+    AdamArgs aa, int T, int cparts, int d, int V, long long Vpad, int n_chunks,
+    const float* __restrict__ gAp, int res_rows, int n_b2, int G2, const float* __restrict__ gBp,
+    unsigned long long* __restrict__ corr_fx, const float* __restrict__ loss_tok,
+    float* __restrict__ Gbuf, float* __restrict__ params, float* __restrict__ mom1,
+    float* __restrict__ mom2, float* __restrict__ gmean, double* __restrict__ norm_parts,
+    float* __restrict__ loss_out) {
   const long long nA = (long long)d * R;
   const long long nB = Vpad * R;  // pair layout, entries of vocab ids >= V stay zero
   const long long stride = (long long)gridDim.x * blockDim.x;
   const int n_a2 = (V + res_rows - 1) / res_rows;
   const long long total2 = (long long)n_a2 * n_b2;
+  const float inv = __fdiv_rn(1.0f, (float)T);
+  double ss = 0.0;
   for (long long k = (long long)blockIdx.x * blockDim.x + threadIdx.x; k < nA + nB; k += stride) {
     float s = 0.f;
     if (k < nA) {
@@ -1371,24 +1411,40 @@ __global__ void lce_finalize(int T, int cparts, int d, int V, long long Vpad, in
     } else {
       const long long e = k - nA;
       const int v = (int)(2 * (e / (2 * R)) + (e & 1));
-      if (v >= V) {
-        Gbuf[k] = 0.f;
-        continue;
-      }
-      const int a = v / res_rows;
-      const int s0 = tile_owner((long long)a * n_b2, total2, G2);
-      const int s1 = tile_owner((long long)a * n_b2 + n_b2 - 1, total2, G2);
-      for (int q = 0; q < cparts * (s1 - s0 + 1); ++q) s += gBp[(long long)q * Vpad * R + e];
-      const long long c = (long long)corr_fx[e];
-      if (c != 0) {
-        s -= (float)((double)c * kFixInv);
-        corr_fx[e] = 0ull;  // ready for the next step
+      if (v < V) {
+        const int a = v / res_rows;
+        const int s0 = tile_owner((long long)a * n_b2, total2, G2);
+        const int s1 = tile_owner((long long)a * n_b2 + n_b2 - 1, total2, G2);
+        for (int q = 0; q < cparts * (s1 - s0 + 1); ++q) s += gBp[(long long)q * Vpad * R + e];
+        const long long c = (long long)corr_fx[e];
+        if (c != 0) {
+          s -= (float)((double)c * kFixInv);
+          corr_fx[e] = 0ull;  // ready for the next step
+        }
       }
     }
     Gbuf[k] = s;
+    if constexpr (kMode == kFinNorm) {
+      const float g = s * inv;
+      ss += (double)g * (double)g;
+    } else if constexpr (kMode == kFinAdam) {
+      const float g = __fmul_rn(s, inv);
+      gmean[k] = g;
+      adam_element(aa, k, g, params, mom1, mom2);
+    }
+  }
+  __shared__ float red[256];
+  __shared__ double dred[256];
+  if constexpr (kMode == kFinNorm) {
+    dred[threadIdx.x] = ss;
+    __syncthreads();
+    for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+      if (threadIdx.x < w) dred[threadIdx.x] += dred[threadIdx.x + w];
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) norm_parts[blockIdx.x] = dred[0];
   }
   if (blockIdx.x == 0) {
-    __shared__ float red[256];
     float s = 0.f;
     for (int t = threadIdx.x; t < T; t += blockDim.x) s += loss_tok[t];
     red[threadIdx.x] = s;
@@ -1400,6 +1456,7 @@ __global__ void lce_finalize(int T, int cparts, int d, int V, long long Vpad, in
     if (threadIdx.x == 0) {
       Gbuf[nA + nB] = red[0];
       Gbuf[nA + nB + 1] = (float)T;
+      if (kMode == kFinAdam && loss_out) *loss_out = __fmul_rn(red[0], inv);
     }
   }
 }
@@ -1422,14 +1479,6 @@ static __global__ void lce_sqnorm(long long n, const float* __restrict__ Gbuf, d
   }
   if (threadIdx.x == 0) part[blockIdx.x] = red[0];
 }
-
-struct AdamArgs {
-  long long n;       // d*R + V*R parameters
-  float lr, b1, b2, c1, c2, eps, wd;  // c1 = 1 - b1, c2 = 1 - b2 (in f32)
-  float b1t, b2t;    // 1 - b^step, computed on the host with powf
-  float clip;
-  int n_norm_parts;
-};
 
 // g = G / n_pred (x clip coefficient); decoupled decay; Adam update
 // (src/train.c:175-196), written with explicitly rounded operations so the
@@ -1454,16 +1503,7 @@ static __global__ void lce_adam(AdamArgs a, float* __restrict__ params, float* _
     float g = __fmul_rn(Gbuf[k], inv);
     if (coef != 1.0f) g = __fmul_rn(g, coef);
     gmean[k] = g;
-    float p = params[k];
-    if (a.wd > 0.f) p = __fsub_rn(p, __fmul_rn(__fmul_rn(a.lr, a.wd), p));
-    const float m = __fadd_rn(__fmul_rn(a.b1, mom1[k]), __fmul_rn(a.c1, g));
-    const float v = __fadd_rn(__fmul_rn(a.b2, mom2[k]), __fmul_rn(__fmul_rn(a.c2, g), g));
-    mom1[k] = m;
-    mom2[k] = v;
-    const float mhat = __fdiv_rn(m, a.b1t);
-    const float vhat = __fdiv_rn(v, a.b2t);
-    p = __fsub_rn(p, __fdiv_rn(__fmul_rn(a.lr, mhat), __fadd_rn(__fsqrt_rn(vhat), a.eps)));
-    params[k] = p;
+    adam_element(a, k, g, params, mom1, mom2);
   }
 }
 

@@ -48,7 +48,7 @@ EXPORTS = [
     "lora_ce_merge_weight_device", "lora_ce_merge_last_error", "lora_ce_set_scale",
     "lora_ce_set_weight_q4k", "lora_ce_q4k_dequant", "lora_ce_q4k_dequant_device",
     "lora_ce_q4k_last_error", "lora_ce_apply_grads", "lora_ce_set_copy_timing",
-    "lora_ce_copy_times",
+    "lora_ce_copy_times", "lora_ce_set_comm_timeout",
 ]
 
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
@@ -111,6 +111,7 @@ def load_library() -> C.CDLL:
     lib.lora_ce_get_token_loss.argtypes = [vp, vp, C.c_int32]
     lib.lora_ce_apply_grads.argtypes = [vp, vp, vp, C.c_float]
     lib.lora_ce_set_copy_timing.argtypes = [vp, C.c_int32]
+    lib.lora_ce_set_comm_timeout.argtypes = [vp, C.c_int32]
     lib.lora_ce_copy_times.argtypes = [vp, C.POINTER(C.c_float), C.c_int32]
     lib.lora_ce_copy_times.restype = C.c_int32
     lib.lora_ce_nccl_unique_id.argtypes = [vp]
@@ -370,6 +371,9 @@ class LoraCE:
         if n < 0:
             _check(n, "phase_times")
         return {self.lib.lora_ce_phase_name(i).decode(): float(buf[i]) for i in range(n)}
+
+    def set_comm_timeout(self, ms: int) -> None:
+        _check(self.lib.lora_ce_set_comm_timeout(self.h, int(ms)), "set_comm_timeout")
 
     def set_copy_timing(self, enable: bool = True) -> None:
         _check(self.lib.lora_ce_set_copy_timing(self.h, int(enable)), "set_copy_timing")

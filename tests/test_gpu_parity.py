@@ -441,3 +441,27 @@ def test_adam_kernel_bit_exact_with_reference_adam_update(V, d, r):
     assert step == k
     assert np.array_equal(A1.view(np.uint32), Ar.view(np.uint32))
     assert np.array_equal(B1.view(np.uint32), Br.view(np.uint32))
+
+
+def test_copy_timing_of_host_steps():
+    """lora_ce_set_copy_timing: the host-input step's graph is re-captured
+    with event nodes; the step's results do not change, and the reported
+    times are consistent (chunk copies inside the step)."""
+    V, d, r, T = 49152, 576, 4, 8192
+    W, H, _, tgt, A, B = make(V, d, r, T, 91)
+    res = []
+    for timing in (False, True):
+        m = lora_ce.LoraCE(lora_ce.default_config(d, V, r, T, scale=2.0, lr=1e-3))
+        m.set_weight(W)
+        m.set_adapter(A, B, 0)
+        m.set_copy_timing(timing)
+        losses = [m.step(H, tgt) for _ in range(3)]
+        if timing:
+            t = m.copy_times()
+            assert len(t["chunk_ms"]) == 4
+            assert t["host_us"] > 0 and t["wait_us"] >= 0
+            assert 0 < sum(t["chunk_ms"]) < t["step_ms"]
+        res.append((losses, m.get_adapter()[1]))
+        m.close()
+    assert res[0][0] == res[1][0]
+    assert np.array_equal(res[0][1], res[1][1])

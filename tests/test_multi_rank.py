@@ -138,3 +138,4 @@ def test_two_gpus_match_oracle(oracle, tmp_path, r):
             assert np.linalg.norm(r[k] - ref[k]) <= 1e-3 * np.linalg.norm(ref[k]), k
     for k in ("A", "B"):
         np.testing.assert_array_equal(out[0][k], out[1][k])
+

@@ -358,3 +358,101 @@ def test_train_run_packs_samples_when_asked(env, oracle, tmp_path, capfd):
         assert np.linalg.norm(a - b) <= 1e-3 * np.linalg.norm(b)
     env.lib.train_free(t)
     env.env.env_forward_free(f)
+
+
+# ------------------------------------------------------- failure paths (GPU)
+@pytest.mark.gpu
+@pytest.mark.skipif(not orc.ref_available(), reason="reference not built here")
+def test_train_run_emergency_save_matches_reference(env, tmp_path, capfd):
+    """train_run's watchdog (src/train.c:355-369) with simulate_mem_kb below
+    the emergency threshold: after the first step both trainers write
+    emergency_1.bin, print the same lines and return 0 without a final
+    save."""
+    import ctypes as C
+    d, V = 128, 3000
+    W, H, samples = _run_inputs(d=d, V=V)
+    ref = orc.RefHarness()
+    f = ref.lib.ref_train_run_mem
+    f.argtypes = [C.c_int] * 4 + [C.c_float] + [C.c_int] * 5 + [C.c_void_p, C.c_void_p, C.c_int,
+                                                                C.c_char_p, C.c_char_p, C.c_long]
+    packed = str(tmp_path / "data.bin")
+    sf.write_packed(packed, samples)
+    ref_out = str(tmp_path / "ref_out")
+    rc = f(d, V, 4, 8, 1e-3, 64, 42, 1, 4, 2, W.ctypes.data, H.ctypes.data, H.shape[0],
+           packed.encode(), ref_out.encode(), 1024)
+    assert rc == 0
+    ref_cap = capfd.readouterr()
+    fw = env.forward(H, V)
+    p = sf.params(rank=4, alpha=8, seq_max=64, lr=1e-3, max_steps=4, checkpoint_every=2, seed=42,
+                  simulate_mem_kb=1024)
+    t = env.lib.train_create(fw, p)
+    assert env.lib.lora_train_set_lm_head(t, W.ctypes.data) == 0
+    out = str(tmp_path / "gpu_out")
+    assert env.lib.train_run(t, packed.encode(), p, out.encode()) == 0
+    env.flush()
+    cap = capfd.readouterr()
+    env.lib.train_free(t)
+    env.env.env_forward_free(fw)
+    lines, ref_lines = cap.out.strip().splitlines(), ref_cap.out.strip().splitlines()
+    assert len(lines) == len(ref_lines) == 1
+    a, b = STEP_RE.match(lines[0]).groups(), STEP_RE.match(ref_lines[0]).groups()
+    assert a[:3] == b[:3] and abs(float(a[3]) - float(b[3])) <= 1e-4 * float(b[3]) + 1e-4
+    emerg = [x for x in cap.err.splitlines() if x.startswith("train: emergency save")]
+    ref_emerg = [x for x in ref_cap.err.splitlines() if x.startswith("train: emergency save")]
+    assert emerg == ref_emerg and len(emerg) == 1
+    assert sorted(os.listdir(out)) == sorted(os.listdir(ref_out)) == ["emergency_1.bin"]
+    A, B, s, sc = _read_adapter(os.path.join(out, "emergency_1.bin"), d, V, 4)
+    Ar, Br, sr, scr = _read_adapter(os.path.join(ref_out, "emergency_1.bin"), d, V, 4)
+    assert (s, sc) == (sr, scr) == (1, 2.0)
+    for x, y in ((A, Ar), (B, Br)):
+        assert np.linalg.norm(x - y) <= 1e-3 * np.linalg.norm(y)
+
+
+@pytest.mark.gpu
+def test_train_create_host_allocation_failure(tmp_path):
+    """A host allocation that fails inside train_create (the buffer of
+    gathered hidden states, made to fail by a preloaded malloc fake in a
+    child process) makes it return NULL, as the reference's does, after
+    releasing the GPU handle it had created; a second train_create in the
+    same process then succeeds."""
+    import subprocess
+    import sys
+    so = str(tmp_path / "libfail_alloc.so")
+    subprocess.run(["gcc", "-O2", "-fPIC", "-shared", "-o", so,
+                    os.path.join(REPO, "tests", "fault", "fail_alloc.c")], check=True)
+    d, seq_max = 128, 1237
+    size = (seq_max - 1) * d * 4  # train_create's t->H: max_pred x dim floats
+    script = f"""
+import sys, numpy as np
+sys.path[:0] = {[REPO, os.path.join(REPO, 'tests'), os.path.join(REPO, 'smollm2.c_b200'),
+                 os.path.join(REPO, 'oracle')]!r}
+import studio_fixtures as sf
+env = sf.TrainerEnv()
+H = np.zeros((4, {d}), np.float32)
+f = env.forward(H, 1000)
+p = sf.params(seq_max={seq_max})
+t = env.lib.train_create(f, p)
+print("first", t is None)
+import os
+os.environ["FAIL_ALLOC_SIZE"] = "0"
+t = env.lib.train_create(f, p)
+print("second", t is not None)
+env.lib.train_free(t)
+env.env.env_forward_free(f)
+"""
+    envv = dict(os.environ, LD_PRELOAD=so, FAIL_ALLOC_SIZE=str(size))
+    r = subprocess.run([sys.executable, "-c", script], env=envv, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert "first True" in r.stdout and "second True" in r.stdout
+
+
+@pytest.mark.gpu
+def test_device_allocation_failure_is_enomem():
+    """A handle whose buffers cannot be allocated on the device (a T far
+    beyond the GPU's memory) is refused with LORA_CE_ENOMEM, and the next
+    handle on the same device works."""
+    with pytest.raises(lora_ce.LoraCEError, match="ENOMEM"):
+        lora_ce.LoraCE(lora_ce.default_config(576, 49152, 4, 1 << 30))
+    m = lora_ce.LoraCE(lora_ce.default_config(64, 1000, 4, 16))
+    m.close()
