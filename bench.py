@@ -732,6 +732,10 @@ def kernel_run(args):
 
 
 def main():
+    import faulthandler
+    # a run that stalls prints every thread's stack and exits instead of
+    # holding the GPUs until an outer limit kills it
+    faulthandler.dump_traceback_later(float(os.environ.get("BENCH_WATCHDOG_S", "1200")), exit=True)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)

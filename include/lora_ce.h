@@ -177,8 +177,9 @@ int32_t lora_ce_phase_times(lora_ce_handle* h, float* ms, int32_t cap);
 const char* lora_ce_phase_name(int32_t i);
 
 /* Timing of host-input steps (lora_ce_step), to see where the time of a
- * step that starts from host memory goes.  When enabled (the step's graph
- * is re-captured with event nodes), lora_ce_copy_times waits for the last
+ * step that starts from host memory goes.  While enabled, host-input steps
+ * launch their kernels and copies directly (not as a replayed CUDA graph)
+ * with timing events between them; lora_ce_copy_times waits for the last
  * host-input step and writes: [0] host us inside lora_ce_step before the
  * wait (argument checks, graph launch), [1] host us waiting for the
  * result, [2] ms from the step's start on the compute stream to the start

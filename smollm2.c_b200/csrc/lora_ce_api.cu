@@ -166,6 +166,10 @@ const char* nccl_str(ncclResult_t r) {
   return nccl().GetErrorString ? nccl().GetErrorString(r) : "NCCL error";
 }
 
+// Largest T a handle may be created for (the planning loops below and the
+// position-indexed buffers are sized from it).
+constexpr int kMaxTokens = 1 << 24;
+
 // Largest number of CTA segments any resident tile's run of n_b tiles is
 // split into, for n_a x n_b tiles over G CTAs.
 int max_segments(int n_a, int n_b, int G) {
@@ -301,8 +305,11 @@ void drop_graphs(lora_ce_handle* h);
 
 template <class T>
 int dalloc(T** p, size_t count) {
-  if (cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T) + 16) != cudaSuccess)
+  if (cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T) + 16) != cudaSuccess) {
+    *p = nullptr;
+    cudaGetLastError();  // not sticky: clear it so later launch checks do not see it
     return fail(LORA_CE_ENOMEM, "cudaMalloc failed");
+  }
   if (cudaMemset(*p, 0, count * sizeof(T) + 16) != cudaSuccess)
     return fail(LORA_CE_ECUDA, "cudaMemset failed");
   return 0;
@@ -344,7 +351,8 @@ int check_cfg(const lora_ce_config* c) {
   if (c->rank < 1 || c->rank > 64) return fail(LORA_CE_EINVAL, "rank must be in [1, 64]");
   if (c->dim / 64 + aug_width_of(kernel_rank(c->rank)) / 64 > kMaxKBlocks)
     return fail(LORA_CE_EINVAL, "dim too large for this rank (resident K-blocks)");
-  if (c->max_tokens < 1) return fail(LORA_CE_EINVAL, "max_tokens must be positive");
+  if (c->max_tokens < 1 || c->max_tokens > kMaxTokens)
+    return fail(LORA_CE_EINVAL, "max_tokens must be in [1, 2^24]");
   if (!(c->lr >= 0.f) || !(c->eps > 0.f) || !(c->beta1 >= 0.f && c->beta1 < 1.f) ||
       !(c->beta2 >= 0.f && c->beta2 < 1.f) || !(c->weight_decay >= 0.f) ||
       !(c->clip_norm >= 0.f) || !std::isfinite(c->scale))
@@ -932,16 +940,6 @@ void drop_graphs(lora_ce_handle* h) {
   for (auto& gph : h->graphs) drop_graph(gph);
 }
 
-// A timing event on stream s.  Under stream capture a plain record only
-// orders work inside the graph, so timing events become external event
-// nodes there, recorded each time the graph runs.
-cudaError_t record_timing(cudaEvent_t e, cudaStream_t s) {
-  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(s, &cs) != cudaSuccess) return cudaErrorUnknown;
-  return cs == cudaStreamCaptureStatusActive ? cudaEventRecordWithFlags(e, s, cudaEventRecordExternal)
-                                             : cudaEventRecord(e, s);
-}
-
 // Everything one step enqueues on the handle's streams.  Host-input steps
 // (H, targets in host memory) copy them in (h in chunks on the copy stream,
 // see run_step) and read [loss, error code] back into res_host;
@@ -949,7 +947,7 @@ cudaError_t record_timing(cudaEvent_t e, cudaStream_t s) {
 int enqueue_step(lora_ce_handle* h, bool host, const void* H, int dtype, int T,
                  const int32_t* targets, float* d_loss) {
   if (!host) return dispatch_step(h, H, dtype, T, targets, d_loss);
-  if (h->ctime) LCE_CUDA(record_timing(h->tev[0], h->stream));
+  if (h->ctime) LCE_CUDA(cudaEventRecord(h->tev[0], h->stream));
   LCE_CUDA(cudaMemcpyAsync(h->in_tgt, targets, (size_t)T * 4, cudaMemcpyHostToDevice, h->stream));
   const int res_rows = kBM * h->pair;
   const int n_a1 = (T + res_rows - 1) / res_rows;
@@ -957,7 +955,7 @@ int enqueue_step(lora_ce_handle* h, bool host, const void* H, int dtype, int T,
   const size_t row_bytes = (size_t)h->d * elt_size(dtype);
   LCE_CUDA(cudaEventRecord(h->ev_start, h->stream));  // the previous step is done with in_H
   LCE_CUDA(cudaStreamWaitEvent(h->cstream, h->ev_start, 0));
-  if (h->ctime) LCE_CUDA(record_timing(h->tev[1], h->cstream));
+  if (h->ctime) LCE_CUDA(cudaEventRecord(h->tev[1], h->cstream));
   for (int c = 0; c < chunks; ++c) {
     const long long t_lo = tile_start(c, n_a1, chunks) * res_rows;
     const long long t_hi = std::min<long long>(T, tile_start(c + 1, n_a1, chunks) * res_rows);
@@ -965,14 +963,14 @@ int enqueue_step(lora_ce_handle* h, bool host, const void* H, int dtype, int T,
                              static_cast<const char*>(H) + t_lo * row_bytes,
                              (size_t)(t_hi - t_lo) * row_bytes, cudaMemcpyHostToDevice, h->cstream));
     LCE_CUDA(cudaEventRecord(h->ev_chunk[c], h->cstream));
-    if (h->ctime) LCE_CUDA(record_timing(h->tev[2 + c], h->cstream));
+    if (h->ctime) LCE_CUDA(cudaEventRecord(h->tev[2 + c], h->cstream));
   }
   h->ctime_chunks = chunks;
   int rc = dispatch_step(h, h->in_H, dtype, T, h->in_tgt, h->d_loss, chunks, h->ev_chunk);
   if (rc) return rc;
   LCE_CUDA(cudaMemcpyAsync(h->d_loss + 1, h->err, 4, cudaMemcpyDeviceToDevice, h->stream));
   LCE_CUDA(cudaMemcpyAsync(h->res_host, h->d_loss, 8, cudaMemcpyDeviceToHost, h->stream));
-  if (h->ctime) LCE_CUDA(record_timing(h->tev[kMaxChunks + 2], h->stream));
+  if (h->ctime) LCE_CUDA(cudaEventRecord(h->tev[kMaxChunks + 2], h->stream));
   return 0;
 }
 
@@ -1081,7 +1079,8 @@ int launch_step_graph(lora_ce_handle* h, lora_ce_handle::StepGraph* gph, int T) 
 
 int run_or_replay(lora_ce_handle* h, bool host, const void* H, int dtype, int T,
                   const int32_t* targets, float* d_loss) {
-  if (h->use_graphs && !h->prof) {
+  // timed host-input steps launch directly (their events are plain records)
+  if (h->use_graphs && !h->prof && !(host && h->ctime)) {
     lora_ce_handle::StepGraph* gph = step_graph(h, host, H, dtype, T, targets, d_loss);
     if (gph) return launch_step_graph(h, gph, T);
     h->use_graphs = false;  // capture failed: launch directly from now on
@@ -1568,7 +1567,6 @@ int lora_ce_set_copy_timing(lora_ce_handle* h, int32_t enable) {
   LCE_CUDA(cudaSetDevice(h->cfg.device));
   if (enable && !h->tev[0])
     for (cudaEvent_t& e : h->tev) LCE_CUDA(cudaEventCreate(&e));
-  if ((enable != 0) != h->ctime) drop_graphs(h);  // recapture with (or without) the events
   h->ctime = enable != 0;
   return 0;
 }

@@ -444,9 +444,9 @@ def test_adam_kernel_bit_exact_with_reference_adam_update(V, d, r):
 
 
 def test_copy_timing_of_host_steps():
-    """lora_ce_set_copy_timing: the host-input step's graph is re-captured
-    with event nodes; the step's results do not change, and the reported
-    times are consistent (chunk copies inside the step)."""
+    """lora_ce_set_copy_timing: timed host-input steps launch directly with
+    events between the copies; the step's results do not change, and the
+    reported times are consistent (chunk copies inside the step)."""
     V, d, r, T = 49152, 576, 4, 8192
     W, H, _, tgt, A, B = make(V, d, r, T, 91)
     res = []

@@ -448,11 +448,22 @@ env.env.env_forward_free(f)
 
 
 @pytest.mark.gpu
-def test_device_allocation_failure_is_enomem():
-    """A handle whose buffers cannot be allocated on the device (a T far
-    beyond the GPU's memory) is refused with LORA_CE_ENOMEM, and the next
-    handle on the same device works."""
+def test_device_allocation_failure_is_enomem(oracle):
+    """A handle whose buffers cannot be allocated on the device (a vocabulary
+    whose weight alone would need 1.2 TB) is refused with LORA_CE_ENOMEM, the
+    failed allocation leaves no error behind, and the next handle on the same
+    device steps correctly."""
     with pytest.raises(lora_ce.LoraCEError, match="ENOMEM"):
-        lora_ce.LoraCE(lora_ce.default_config(576, 49152, 4, 1 << 30))
-    m = lora_ce.LoraCE(lora_ce.default_config(64, 1000, 4, 16))
+        lora_ce.LoraCE(lora_ce.default_config(576, 1 << 30, 4, 16))
+    with pytest.raises(lora_ce.LoraCEError, match="EINVAL"):
+        lora_ce.LoraCE(lora_ce.default_config(576, 49152, 4, (1 << 24) + 1))
+    V, d, T = 1000, 64, 40
+    W = wl.make_weight(2, V, d)
+    h, tgt, A, B = wl.make_step_inputs(2, T, V, d, 4)
+    m = lora_ce.LoraCE(lora_ce.default_config(d, V, 4, T, scale=2.0, lr=1e-3))
+    m.set_weight(W)
+    m.set_adapter(A, B, 0)
+    loss = m.step(h, tgt)
     m.close()
+    ref = oracle.step(W, A, B, wl.oracle_hidden(h), tgt, 2.0, 1e-3)
+    assert abs(loss - ref["loss"]) <= 1e-4 * ref["loss"]
