@@ -284,7 +284,7 @@ class CpuReference:
     train.c (oracle/_ref, single-threaded by design) run as one process per
     core, each on its own shard of positions (the data-parallel split the
     GPU path uses); the oracle port on all cores when oracle/_ref is absent.
-    The pool is spawned (never forked) and started before any GPU work."""
+    The pool is spawned (never forked), so it is safe to start after GPU work."""
 
     def __init__(self):
         import oracle as orc
@@ -550,6 +550,11 @@ def run_q4k(args):
 
 
 # ----------------------------------------------------------------- GPU leg
+def note(msg: str) -> None:
+    """Progress on stderr (the JSON line is the only stdout)."""
+    print(f"[bench] {msg}", file=sys.stderr, flush=True)
+
+
 def cfg_workload(n: int, world: int, tokens: int | None = None):
     """(rank, alpha, positions per rank, clip, q4k) of workload n at world ranks."""
     c = CONFIGS[n]
@@ -634,6 +639,7 @@ def measure(rig, m, h, tgt, dH, dT, T, world, steps, warmup, clocks=None, breakd
 
     st = torch.cuda.ExternalStream(m.stream, device=rig.dev)
     dLoss = torch.zeros(2, dtype=torch.float32, device=rig.dev)
+    note("device-resident steps")
 
     def dev_step():
         m.step_device(dH.data_ptr(), lora_ce.BF16, T, dT.data_ptr(), dLoss.data_ptr())
@@ -669,6 +675,7 @@ def measure(rig, m, h, tgt, dH, dT, T, world, steps, warmup, clocks=None, breakd
     out["phase_ms"] = {k: sum(v) / len(v) for k, v in phase.items()}
 
     # end to end through the public API with pinned host buffers
+    note("end-to-end steps")
     hH = torch.from_numpy(h.view(np.int16)).pin_memory()
     hT = torch.from_numpy(tgt).pin_memory()
     hHn, hTn = hH.numpy().view(np.uint16), hT.numpy()
@@ -682,6 +689,7 @@ def measure(rig, m, h, tgt, dH, dT, T, world, steps, warmup, clocks=None, breakd
     if breakdown:
         # the same end-to-end steps again with event nodes in the graph: where
         # each step's time goes (host enqueue, host wait, the chunk copies)
+        note("end-to-end breakdown")
         m.set_copy_timing(True)
         for _ in range(2):
             m.step(hHn, hTn)
@@ -783,13 +791,7 @@ def main():
         dist.init_process_group(backend="cpu:gloo,cuda:nccl",
                                 timeout=datetime.timedelta(seconds=120))
 
-    # CPU baseline first (spawned pool, before any GPU work in this process)
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        ref = CpuReference()
-        cpu = ref.sample(15.0)
-        ref.close()
-    numa_cpus = bind_near_gpu(local)  # after the CPU pool, which uses every core
+    numa_cpus = bind_near_gpu(local)
     rig = Rig(torch, dist, local)
 
     def with_comm(m):
@@ -801,8 +803,9 @@ def main():
 
     m, h, tgt, dH, dT, T = make_handle(args.config, world, rank, local, CONFIG["tokens"])
     with_comm(m)
+    note(f"workload {args.config}: T {T} per rank, rank {R}")
     res = measure(rig, m, h, tgt, dH, dT, T, world, args.steps, args.warmup,
-                  clocks=ClockSampler(local))
+                  clocks=ClockSampler(local), breakdown=args.config == 2)
     clk = res.pop("clocks", None)
     m.close()
     phase_ms = res["phase_ms"]
@@ -819,6 +822,7 @@ def main():
     # ranks) at this world size, beside the default line
     strong = None
     if args.config == 2 and not args.no_strong:
+        note("strong-scaling workload")
         r3 = CONFIGS[3]["rank"]
         m3, h3, tgt3, dH3, dT3, T3 = make_handle(3, world, rank, local, None, seed=3000)
         with_comm(m3)
@@ -842,6 +846,16 @@ def main():
             "phase_ms_rank0": per_rank[0]["phase_ms"],
             "gpu_launches": s3["launches"] * args.steps,
         }
+
+    # The CPU reference last: its pool (spawned, all host cores) runs after
+    # the GPU legs, so that the host-memory churn of its processes cannot
+    # affect the pinned buffers of the end-to-end leg.
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        note("CPU reference")
+        ref = CpuReference()
+        cpu = ref.sample(15.0)
+        ref.close()
 
     if rank == 0:
         e2e_ms = res["e2e_ms"]
