@@ -22,6 +22,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liblora_oracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libref_train.so")
+REF_BODY_SO = os.path.join(HERE, "_ref", "libref_body.so")
 
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
@@ -254,3 +255,37 @@ class RefHarness:
 
     def grad_check_softmax_ce(self, vocab: int = 32, eps: float = 1e-3) -> float:
         return float(self.lib.ref_grad_check_softmax_ce(vocab, eps))
+
+
+def ref_body_available() -> bool:
+    return os.path.exists(REF_BODY_SO)
+
+
+class RefBody:
+    """The reference's own body forward (src/forward.c via
+    oracle/_ref/libref_body.so), driven as train_step drives it: every
+    position's forward_last_hidden."""
+
+    def __init__(self, model_path: str, max_seq: int) -> None:
+        lib = _load(REF_BODY_SO)
+        lib.ref_body_load.argtypes = [C.c_char_p, C.c_int]
+        lib.ref_body_load.restype = C.c_int
+        lib.ref_body_hidden.argtypes = [_i32p, C.c_int, _f32p]
+        lib.ref_body_hidden.restype = C.c_double
+        lib.ref_body_free.argtypes = []
+        lib.ref_body_free.restype = None
+        if lib.ref_body_load(model_path.encode(), int(max_seq)) != 0:
+            raise RuntimeError("reference forward_load failed")
+        self.lib = lib
+
+    def hidden(self, tokens, dim: int):
+        """(H [n][dim] of one sequence, seconds in the reference forward)."""
+        tok = np.ascontiguousarray(tokens, np.int32)
+        out = np.empty((len(tok), dim), np.float32)
+        secs = self.lib.ref_body_hidden(tok, len(tok), out)
+        if secs < 0:
+            raise RuntimeError("reference forward failed")
+        return out, float(secs)
+
+    def close(self) -> None:
+        self.lib.ref_body_free()

@@ -1,0 +1,682 @@
+// lora_body.cu — the SmolLM2 body forward on the GPU for every position of
+// a batch of sequences at once (C ABI: include/lora_body.h).  The reference
+// computes the same hidden states one position at a time on the CPU
+// (forward_prefill / forward_decode, src/forward.c:935-1093, 1129-1256).
+//
+// Exactness.  The integer parts are exact: int8 weights (per-row scales)
+// and int8 activations (per-tensor scales) are quantised with the
+// reference's own rounding rules and summed in int32, so each matmul output
+// is bit-identical given bit-identical inputs.  The float parts follow the
+// reference's operation order with explicitly rounded operations (no
+// contraction, as the reference's -std=c99 build has none): RoPE from f32
+// cos / sin tables computed on the host with the same libm calls, the
+// attention dot products and weighted sums in the reference's order, the
+// residual adds.  Two things differ: the RMSNorm's f64 sum of squares is
+// added in a different order (a difference below f32 resolution in
+// practice), and expf (softmax, sigmoid) is CUDA's, which can differ from
+// glibc's in the last bit; either can move an int8 activation by one step
+// now and then, which the tests bound.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "lora_body.h"
+
+namespace {
+
+thread_local std::string g_body_error;
+
+int bfail(int code, const std::string& msg) {
+  g_body_error = msg;
+  return code;
+}
+
+#define BD_CUDA(call)                                                                   \
+  do {                                                                                  \
+    cudaError_t e_ = (call);                                                            \
+    if (e_ != cudaSuccess)                                                              \
+      return bfail(LORA_CE_ECUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+constexpr int kHd = 64;          // head dimension (the reference's attention rows)
+constexpr int kMaxSeqBody = 4096;
+constexpr int kGemmTile = 64;    // tokens x outputs per GEMM block
+constexpr int kAttnWarps = 4;
+
+// ------------------------------------------------------------------ kernels
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// quantize_f16_rows_to_q8_perrow (src/forward.c:441-462): per row, scale =
+// amax / 127, q = (int)(v * (127 / amax) + 0.5) clamped to [-127, 127].
+__global__ void bd_quant_rows(const __half* __restrict__ W, int rows, int cols,
+                              int8_t* __restrict__ q, float* __restrict__ scale) {
+  const int r = blockIdx.x;
+  if (r >= rows) return;
+  const __half* w = W + (size_t)r * cols;
+  float amax = 0.f;
+  for (int i = threadIdx.x; i < cols; i += blockDim.x) amax = fmaxf(amax, fabsf(__half2float(w[i])));
+  __shared__ float red[32];
+  amax = warp_max(amax);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    v = warp_max(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  amax = red[0];
+  const float inv = amax > 0.f ? __fdiv_rn(127.0f, amax) : 0.f;
+  for (int i = threadIdx.x; i < cols; i += blockDim.x) {
+    int v = __float2int_rz(__fadd_rn(__fmul_rn(__half2float(w[i]), inv), 0.5f));
+    v = v > 127 ? 127 : v < -127 ? -127 : v;
+    q[(size_t)r * cols + i] = (int8_t)v;
+  }
+  if (threadIdx.x == 0) scale[r] = amax > 0.f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+}
+
+// x[t] = token_embd[tokens[t]] in f32 (exact); an id out of range reads row
+// 0 and sets the error flag.
+__global__ void bd_embed(const int32_t* __restrict__ tokens, int T, int d, int V,
+                         const __half* __restrict__ embd, float* __restrict__ x, int* err) {
+  const long long n = (long long)T * d;
+  for (long long k = (long long)blockIdx.x * blockDim.x + threadIdx.x; k < n;
+       k += (long long)gridDim.x * blockDim.x) {
+    const int t = (int)(k / d), i = (int)(k % d);
+    int tok = tokens[t];
+    if (tok < 0 || tok >= V) {
+      if (i == 0) atomicExch(err, 1);
+      tok = 0;
+    }
+    x[k] = __half2float(embd[(size_t)tok * d + i]);
+  }
+}
+
+// Per-tensor int8 quantisation of one row (the x86 branch of
+// quantize_row_to_q8_tensor, src/forward.c:157-166): scale = amax / 127,
+// q = (int)roundf(v * (127 / amax)) clamped to [-127, 127].  One warp.
+__device__ __forceinline__ void quant_row_warp(const float* __restrict__ src, int n,
+                                               int8_t* __restrict__ dst, float* scale_out,
+                                               int lane) {
+  float amax = 0.f;
+  for (int i = lane; i < n; i += 32) amax = fmaxf(amax, fabsf(src[i]));
+  amax = warp_max(amax);
+  const float inv = amax > 0.f ? __fdiv_rn(127.0f, amax) : 0.f;
+  for (int i = lane; i < n; i += 32) {
+    int v = (int)roundf(__fmul_rn(src[i], inv));
+    v = v > 127 ? 127 : v < -127 ? -127 : v;
+    dst[i] = (int8_t)v;
+  }
+  if (lane == 0) *scale_out = amax > 0.f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+}
+
+// rmsnorm (the x86 branch, src/forward.c:366-371): f64 sum of squares,
+// inv = 1 / sqrtf(ss / n + eps), out = x * inv * w.  One warp per row;
+// the normalised row goes to `xn` (scratch), then either int8 + scale
+// (quantised) or the final hidden state in h_dtype.
+__global__ void bd_norm(const float* __restrict__ x, const float* __restrict__ w, int T, int d,
+                        float eps, float* __restrict__ xn, int8_t* __restrict__ xq,
+                        float* __restrict__ xs, void* __restrict__ out, int out_dtype) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  const float* xr = x + (size_t)warp * d;
+  double ss = 0.0;
+  for (int i = lane; i < d; i += 32) ss += (double)xr[i] * (double)xr[i];
+  ss = warp_sum_d(ss);
+  ss /= d;
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)ss, eps)));
+  float* nr = xn + (size_t)warp * d;
+  for (int i = lane; i < d; i += 32) nr[i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+  __syncwarp();
+  if (xq) {
+    quant_row_warp(nr, d, xq + (size_t)warp * d, xs + warp, lane);
+  } else {
+    for (int i = lane; i < d; i += 32) {
+      const float v = nr[i];
+      const size_t k = (size_t)warp * d + i;
+      if (out_dtype == LORA_CE_F32)
+        static_cast<float*>(out)[k] = v;
+      else if (out_dtype == LORA_CE_BF16)
+        static_cast<__nv_bfloat16*>(out)[k] = __float2bfloat16_rn(v);
+      else
+        static_cast<__half*>(out)[k] = __float2half_rn(v);
+    }
+  }
+}
+
+// Per-tensor int8 quantisation of rows of n floats, one warp per row.
+__global__ void bd_quant_act(const float* __restrict__ src, int T, int n, int8_t* __restrict__ q,
+                             float* __restrict__ s) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  quant_row_warp(src + (size_t)warp * n, n, q + (size_t)warp * n, s + warp, lane);
+}
+
+// SwiGLU then int8: a = g * (1 / (1 + expf(-g))) * u (src/forward.c:1239-1242),
+// quantised over the row.  gu is [T][2*ffn] (gate | up); one warp per row.
+__global__ void bd_act_quant(const float* __restrict__ gu, int T, int ffn, float* __restrict__ a,
+                             int8_t* __restrict__ q, float* __restrict__ s) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  const float* g = gu + (size_t)warp * 2 * ffn;
+  float* ar = a + (size_t)warp * ffn;
+  for (int i = lane; i < ffn; i += 32) {
+    const float gv = g[i];
+    const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gv)));
+    ar[i] = __fmul_rn(__fmul_rn(gv, sig), g[ffn + i]);
+  }
+  __syncwarp();
+  quant_row_warp(ar, ffn, q + (size_t)warp * ffn, s + warp, lane);
+}
+
+// Y[t][n] (+)= (float)(sum_k X[t][k] * W[n][k]) * xs[t] * ws[n]: the
+// reference's matmul_q8_dot_perrow (src/forward.c:470-511, int32 sums, two
+// rounded multiplies), with `accumulate` adding it to Y as the residual
+// add does.  64 x 64 tiles, K in 64-byte steps (K % 64 == 0), dp4a.
+__global__ void __launch_bounds__(256) bd_gemm_q8(const int8_t* __restrict__ X,
+                                                  const float* __restrict__ xs, int T, int K,
+                                                  const int8_t* __restrict__ W,
+                                                  const float* __restrict__ ws, int N,
+                                                  float* __restrict__ Y, int ldy, int accumulate) {
+  __shared__ int sX[kGemmTile][17];
+  __shared__ int sW[kGemmTile][17];
+  const int t0 = blockIdx.y * kGemmTile, n0 = blockIdx.x * kGemmTile;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  int acc[4][4];
+#pragma unroll
+  for (int m = 0; m < 4; ++m)
+#pragma unroll
+    for (int n = 0; n < 4; ++n) acc[m][n] = 0;
+  for (int k0 = 0; k0 < K; k0 += 64) {
+    for (int i = threadIdx.x; i < kGemmTile * 16; i += 256) {
+      const int r = i >> 4, c = i & 15;
+      const int tr = t0 + r, nr = n0 + r;
+      sX[r][c] = tr < T ? *reinterpret_cast<const int*>(X + (size_t)tr * K + k0 + 4 * c) : 0;
+      sW[r][c] = nr < N ? *reinterpret_cast<const int*>(W + (size_t)nr * K + k0 + 4 * c) : 0;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      int a[4], b[4];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) a[m] = sX[ty * 4 + m][c];
+#pragma unroll
+      for (int n = 0; n < 4; ++n) b[n] = sW[tx * 4 + n][c];
+#pragma unroll
+      for (int m = 0; m < 4; ++m)
+#pragma unroll
+        for (int n = 0; n < 4; ++n) acc[m][n] = __dp4a(a[m], b[n], acc[m][n]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    const int t = t0 + ty * 4 + m;
+    if (t >= T) continue;
+    const float sx = xs[t];
+#pragma unroll
+    for (int n = 0; n < 4; ++n) {
+      const int o = n0 + tx * 4 + n;
+      if (o >= N) continue;
+      const float y = __fmul_rn(__fmul_rn(__int2float_rn(acc[m][n]), sx), ws[o]);
+      float* dst = Y + (size_t)t * ldy + o;
+      *dst = accumulate ? __fadd_rn(*dst, y) : y;
+    }
+  }
+}
+
+// RoPE from the f32 tables (rope_llama_table, src/forward.c:552-565) on q
+// (heads 0..nh-1 of the qkv row) and k (the next nkv heads) at each
+// position's place in its sequence.
+__global__ void bd_rope(float* __restrict__ qkv, int T, int ld, int n_rot_heads,
+                        const int32_t* __restrict__ pos, const float* __restrict__ cosT,
+                        const float* __restrict__ sinT) {
+  constexpr int half = kHd / 2;
+  const long long n = (long long)T * n_rot_heads * half;
+  for (long long k = (long long)blockIdx.x * blockDim.x + threadIdx.x; k < n;
+       k += (long long)gridDim.x * blockDim.x) {
+    const int i = (int)(k % half);
+    const int hh = (int)((k / half) % n_rot_heads);
+    const int t = (int)(k / ((long long)half * n_rot_heads));
+    float* v = qkv + (size_t)t * ld + hh * kHd;
+    const float c = cosT[(size_t)pos[t] * half + i], s = sinT[(size_t)pos[t] * half + i];
+    const float a = v[2 * i], b = v[2 * i + 1];
+    v[2 * i] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+    v[2 * i + 1] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+  }
+}
+
+// Causal GQA attention in the reference's order (src/forward.c:1186-1229):
+// one warp per (position, head).  Scores q.k / 8 (each lane one key, the
+// 64-term sum in index order), max, e = expf(s - max), the sum of e in key
+// order (lane 0), then out[i] = sum over keys of (e * (1/sum)) * v[i] in key
+// order (lanes over i).  Keys from seq_start + s_start(window) to t.
+__global__ void __launch_bounds__(32 * kAttnWarps)
+    bd_attn(const float* __restrict__ qkv, int T, int ld, int nh, int nkv, int dim,
+            const int32_t* __restrict__ pos, int window, float* __restrict__ out, int max_seq) {
+  extern __shared__ float sc_all[];
+  const int wib = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const long long item = (long long)blockIdx.x * kAttnWarps + wib;
+  if (item >= (long long)T * nh) return;
+  const int t = (int)(item / nh), h = (int)(item % nh);
+  float* sc = sc_all + (size_t)wib * (max_seq + kHd);
+  float* qs = sc + max_seq;
+  const int kvh = h * nkv / nh;
+  const int p = pos[t];
+  int lo = 0;
+  if (window > 0) {
+    lo = p + 1 - window;
+    if (lo < 0) lo = 0;
+    if (lo > p) lo = p;
+  }
+  const int first = t - p + lo;  // global index of the first key
+  const int n_keys = p - lo + 1;
+  const float* q = qkv + (size_t)t * ld + h * kHd;
+  qs[lane] = q[lane];
+  qs[lane + 32] = q[lane + 32];
+  __syncwarp();
+  const float* kbase = qkv + dim + kvh * kHd;
+  const float* vbase = qkv + dim + nkv * kHd + kvh * kHd;
+  float mx = -INFINITY;
+  for (int j = lane; j < n_keys; j += 32) {
+    const float* kr = kbase + (size_t)(first + j) * ld;
+    float d = 0.f;
+#pragma unroll 16
+    for (int i = 0; i < kHd; ++i) d = __fadd_rn(d, __fmul_rn(qs[i], kr[i]));
+    d = __fmul_rn(d, 0.125f);  // 1 / sqrtf(64)
+    sc[j] = d;
+    mx = fmaxf(mx, d);
+  }
+  mx = warp_max(mx);
+  __syncwarp();
+  for (int j = lane; j < n_keys; j += 32) sc[j] = expf(__fsub_rn(sc[j], mx));
+  __syncwarp();
+  float sum = 0.f;
+  if (lane == 0)
+    for (int j = 0; j < n_keys; ++j) sum = __fadd_rn(sum, sc[j]);
+  sum = __shfl_sync(0xffffffffu, sum, 0);
+  const float inv_sum = sum > 0.f ? __fdiv_rn(1.0f, sum) : 0.f;
+  float o0 = 0.f, o1 = 0.f;
+  for (int j = 0; j < n_keys; ++j) {
+    const float wgt = __fmul_rn(sc[j], inv_sum);
+    const float* vr = vbase + (size_t)(first + j) * ld;
+    o0 = __fadd_rn(o0, __fmul_rn(wgt, vr[lane]));
+    o1 = __fadd_rn(o1, __fmul_rn(wgt, vr[lane + 32]));
+  }
+  float* orow = out + (size_t)t * dim + h * kHd;
+  orow[lane] = o0;
+  orow[lane + 32] = o1;
+}
+
+}  // namespace
+
+struct lora_body_handle {
+  lora_body_config cfg{};
+  int d = 0, ffn = 0, kvdim = 0, nqkv = 0, Tcap = 0;
+  cudaStream_t stream = nullptr;
+  // weights (int8 per-row) and scales, per layer
+  struct Layer {
+    int8_t* wqkv = nullptr;  // [q | k | v] rows, each [d]
+    float* sqkv = nullptr;
+    int8_t* wo = nullptr;
+    float* so = nullptr;
+    int8_t* wgu = nullptr;   // [gate | up] rows, each [d]
+    float* sgu = nullptr;
+    int8_t* wd = nullptr;    // [d] rows of [ffn]
+    float* sd = nullptr;
+    float* attn_norm = nullptr;
+    float* ffn_norm = nullptr;
+    int window = 0;
+    bool set = false;
+  };
+  std::vector<Layer> layers;
+  __half* embd = nullptr;
+  float* out_norm = nullptr;
+  bool have_embd = false;
+  float* rope_cos = nullptr;
+  float* rope_sin = nullptr;
+  // activations
+  float* x = nullptr;     // [Tcap][d] residual stream
+  float* xn = nullptr;    // [Tcap][max(d, ffn)] scratch (normalised rows, SwiGLU output)
+  int8_t* xq = nullptr;   // [Tcap][max(d, ffn)]
+  float* xs = nullptr;    // [Tcap]
+  float* qkv = nullptr;   // [Tcap][nqkv]
+  float* att = nullptr;   // [Tcap][d]
+  float* gu = nullptr;    // [Tcap][2 ffn]
+  int32_t* pos = nullptr;
+  int32_t* tok = nullptr;  // staging for host tokens
+  float* hout = nullptr;   // staging for host output
+  int32_t* pos_host = nullptr;  // pinned
+  int* err = nullptr;
+};
+
+namespace {
+
+template <class T>
+int balloc(T** p, size_t count) {
+  if (cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T) + 16) != cudaSuccess) {
+    *p = nullptr;
+    cudaGetLastError();
+    return bfail(LORA_CE_ENOMEM, "cudaMalloc failed");
+  }
+  return 0;
+}
+
+void free_body(lora_body_handle* h) {
+  for (auto& L : h->layers) {
+    void* ps[] = {L.wqkv, L.sqkv, L.wo, L.so, L.wgu, L.sgu, L.wd, L.sd, L.attn_norm, L.ffn_norm};
+    for (void* p : ps)
+      if (p) cudaFree(p);
+  }
+  void* ps[] = {h->embd, h->out_norm, h->rope_cos, h->rope_sin, h->x,  h->xn,  h->xq,
+                h->xs,   h->qkv,      h->att,      h->gu,       h->pos, h->tok, h->hout, h->err};
+  for (void* p : ps)
+    if (p) cudaFree(p);
+  if (h->pos_host) cudaFreeHost(h->pos_host);
+  if (h->stream) cudaStreamDestroy(h->stream);
+}
+
+// Upload f16 rows, quantise them to int8 rows at q (rows x cols) with scales.
+int upload_quant(lora_body_handle* h, const uint16_t* src, int rows, int cols, int8_t* q,
+                 float* scale, __half* tmp) {
+  BD_CUDA(cudaMemcpyAsync(tmp, src, (size_t)rows * cols * 2, cudaMemcpyHostToDevice, h->stream));
+  bd_quant_rows<<<rows, 256, 0, h->stream>>>(tmp, rows, cols, q, scale);
+  BD_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int check_offsets(lora_body_handle* h, const int32_t* offsets, int n_seqs, int* T_out) {
+  if (!offsets || n_seqs < 1) return bfail(LORA_CE_EINVAL, "need at least one sequence");
+  if (offsets[0] != 0) return bfail(LORA_CE_EINVAL, "offsets[0] must be 0");
+  for (int i = 0; i < n_seqs; ++i) {
+    const int len = offsets[i + 1] - offsets[i];
+    if (len < 1 || len > h->cfg.max_seq)
+      return bfail(LORA_CE_EINVAL, "every sequence needs 1..max_seq positions");
+  }
+  const int T = offsets[n_seqs];
+  if (T > h->Tcap) return bfail(LORA_CE_EINVAL, "more positions than max_tokens");
+  *T_out = T;
+  return 0;
+}
+
+// The whole forward on the handle's stream: d_tok [T] -> out [T][d].
+int run_body(lora_body_handle* h, const int32_t* d_tok, const int32_t* offsets, int n_seqs,
+             int T, void* out, int out_dtype) {
+  cudaStream_t st = h->stream;
+  const int d = h->d, ffn = h->ffn, nh = h->cfg.n_heads, nkv = h->cfg.n_kv_heads;
+  // position of every token within its sequence
+  for (int i = 0; i < n_seqs; ++i)
+    for (int t = offsets[i]; t < offsets[i + 1]; ++t) h->pos_host[t] = t - offsets[i];
+  BD_CUDA(cudaMemcpyAsync(h->pos, h->pos_host, (size_t)T * 4, cudaMemcpyHostToDevice, st));
+  const int eb = (int)std::min<long long>(((long long)T * d + 255) / 256, 4096);
+  bd_embed<<<eb, 256, 0, st>>>(d_tok, T, d, h->cfg.vocab, h->embd, h->x, h->err);
+  const int rows_blocks = (T * 32 + 255) / 256;  // one warp per row, 8 per block
+  const dim3 g_qkv((h->nqkv + kGemmTile - 1) / kGemmTile, (T + kGemmTile - 1) / kGemmTile);
+  const dim3 g_d((d + kGemmTile - 1) / kGemmTile, (T + kGemmTile - 1) / kGemmTile);
+  const dim3 g_gu((2 * ffn + kGemmTile - 1) / kGemmTile, (T + kGemmTile - 1) / kGemmTile);
+  const int max_seq = h->cfg.max_seq;
+  const size_t attn_smem = (size_t)kAttnWarps * (max_seq + kHd) * 4;
+  const long long att_items = (long long)T * nh;
+  const int rope_blocks = (int)std::min<long long>(((long long)T * (nh + nkv) * 32 + 255) / 256, 8192);
+  for (int L = 0; L < h->cfg.n_layers; ++L) {
+    const auto& ly = h->layers[L];
+    bd_norm<<<rows_blocks, 256, 0, st>>>(h->x, ly.attn_norm, T, d, h->cfg.rms_eps, h->xn, h->xq,
+                                         h->xs, nullptr, 0);
+    bd_gemm_q8<<<g_qkv, 256, 0, st>>>(h->xq, h->xs, T, d, ly.wqkv, ly.sqkv, h->nqkv, h->qkv,
+                                      h->nqkv, 0);
+    bd_rope<<<rope_blocks, 256, 0, st>>>(h->qkv, T, h->nqkv, nh + nkv, h->pos, h->rope_cos,
+                                         h->rope_sin);
+    bd_attn<<<(unsigned)((att_items + kAttnWarps - 1) / kAttnWarps), 32 * kAttnWarps, attn_smem,
+              st>>>(h->qkv, T, h->nqkv, nh, nkv, d, h->pos, ly.window, h->att, max_seq);
+    bd_quant_act<<<rows_blocks, 256, 0, st>>>(h->att, T, d, h->xq, h->xs);
+    bd_gemm_q8<<<g_d, 256, 0, st>>>(h->xq, h->xs, T, d, ly.wo, ly.so, d, h->x, d, 1);
+    bd_norm<<<rows_blocks, 256, 0, st>>>(h->x, ly.ffn_norm, T, d, h->cfg.rms_eps, h->xn, h->xq,
+                                         h->xs, nullptr, 0);
+    bd_gemm_q8<<<g_gu, 256, 0, st>>>(h->xq, h->xs, T, d, ly.wgu, ly.sgu, 2 * ffn, h->gu,
+                                     2 * ffn, 0);
+    bd_act_quant<<<rows_blocks, 256, 0, st>>>(h->gu, T, ffn, h->xn, h->xq, h->xs);
+    bd_gemm_q8<<<g_d, 256, 0, st>>>(h->xq, h->xs, T, ffn, ly.wd, ly.sd, d, h->x, d, 1);
+  }
+  bd_norm<<<rows_blocks, 256, 0, st>>>(h->x, h->out_norm, T, d, h->cfg.rms_eps, h->xn, nullptr,
+                                       nullptr, out, out_dtype);
+  BD_CUDA(cudaGetLastError());
+  return 0;
+}
+
+int body_check_error(lora_body_handle* h) {
+  int e = 0;
+  BD_CUDA(cudaMemcpyAsync(&e, h->err, 4, cudaMemcpyDeviceToHost, h->stream));
+  BD_CUDA(cudaStreamSynchronize(h->stream));
+  if (e) {
+    BD_CUDA(cudaMemset(h->err, 0, 4));
+    return bfail(LORA_CE_EDEVICE, "token id out of range");
+  }
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* lora_body_last_error(void) { return g_body_error.c_str(); }
+
+int lora_body_create(const lora_body_config* c, lora_body_handle** out) {
+  if (!out) return bfail(LORA_CE_EINVAL, "null output pointer");
+  *out = nullptr;
+  if (!c) return bfail(LORA_CE_EINVAL, "null config");
+  if (c->n_layers < 1 || c->dim < 64 || c->dim % 64 || c->dim > 4096 || c->n_heads < 1 ||
+      c->n_kv_heads < 1 || c->n_heads % c->n_kv_heads || c->dim / c->n_heads != kHd ||
+      c->dim % c->n_heads || c->ffn_hidden < 64 || c->ffn_hidden % 64 || c->vocab < 1 ||
+      c->max_seq < 1 || c->max_seq > kMaxSeqBody || c->max_tokens < 1 ||
+      c->max_tokens > (1 << 22) || !(c->rms_eps > 0.f) || !(c->rope_theta > 0.f))
+    return bfail(LORA_CE_EINVAL, "bad body configuration (head_dim must be 64)");
+  BD_CUDA(cudaSetDevice(c->device));
+  lora_body_handle* h = new (std::nothrow) lora_body_handle();
+  if (!h) return bfail(LORA_CE_ENOMEM, "host allocation failed");
+  h->cfg = *c;
+  h->d = c->dim;
+  h->ffn = c->ffn_hidden;
+  h->kvdim = c->n_kv_heads * kHd;
+  h->nqkv = h->d + 2 * h->kvdim;
+  h->Tcap = c->max_tokens;
+  h->layers.resize(c->n_layers);
+  const size_t T = (size_t)h->Tcap, d = h->d, ffn = h->ffn, wide = std::max(d, ffn);
+  int rc = 0;
+  if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess)
+    rc = bfail(LORA_CE_ECUDA, "cudaStreamCreate failed");
+  for (auto& L : h->layers) {
+    if (!rc) rc = balloc(&L.wqkv, (size_t)h->nqkv * d);
+    if (!rc) rc = balloc(&L.sqkv, (size_t)h->nqkv);
+    if (!rc) rc = balloc(&L.wo, d * d);
+    if (!rc) rc = balloc(&L.so, d);
+    if (!rc) rc = balloc(&L.wgu, 2 * ffn * d);
+    if (!rc) rc = balloc(&L.sgu, 2 * ffn);
+    if (!rc) rc = balloc(&L.wd, d * ffn);
+    if (!rc) rc = balloc(&L.sd, d);
+    if (!rc) rc = balloc(&L.attn_norm, d);
+    if (!rc) rc = balloc(&L.ffn_norm, d);
+  }
+  if (!rc) rc = balloc(&h->embd, (size_t)c->vocab * d);
+  if (!rc) rc = balloc(&h->out_norm, d);
+  if (!rc) rc = balloc(&h->rope_cos, (size_t)c->max_seq * (kHd / 2));
+  if (!rc) rc = balloc(&h->rope_sin, (size_t)c->max_seq * (kHd / 2));
+  if (!rc) rc = balloc(&h->x, T * d);
+  if (!rc) rc = balloc(&h->xn, T * wide);
+  if (!rc) rc = balloc(&h->xq, T * wide);
+  if (!rc) rc = balloc(&h->xs, T);
+  if (!rc) rc = balloc(&h->qkv, T * h->nqkv);
+  if (!rc) rc = balloc(&h->att, T * d);
+  if (!rc) rc = balloc(&h->gu, T * 2 * ffn);
+  if (!rc) rc = balloc(&h->pos, T);
+  if (!rc) rc = balloc(&h->tok, T);
+  if (!rc) rc = balloc(&h->hout, T * d);
+  if (!rc) rc = balloc(&h->err, 1);
+  if (!rc && cudaMallocHost(reinterpret_cast<void**>(&h->pos_host), T * 4) != cudaSuccess) {
+    h->pos_host = nullptr;
+    rc = bfail(LORA_CE_ENOMEM, "cudaMallocHost failed");
+  }
+  if (!rc && cudaMemset(h->err, 0, 4) != cudaSuccess) rc = bfail(LORA_CE_ECUDA, "cudaMemset failed");
+  if (!rc && cudaFuncSetAttribute(bd_attn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)(kAttnWarps * (c->max_seq + kHd) * 4)) != cudaSuccess)
+    rc = bfail(LORA_CE_ECUDA, "attention shared memory");
+  if (!rc) {
+    // RoPE tables exactly as forward_load builds them (src/forward.c:889-899)
+    const int half = kHd / 2;
+    std::vector<float> cs((size_t)c->max_seq * half), sn(cs.size());
+    for (int p = 0; p < c->max_seq; ++p)
+      for (int i = 0; i < half; ++i) {
+        const float freq = 1.0f / powf(c->rope_theta, (2.0f * (float)i) / (float)kHd);
+        const float angle = (float)p * freq;
+        cs[(size_t)p * half + i] = cosf(angle);
+        sn[(size_t)p * half + i] = sinf(angle);
+      }
+    if (cudaMemcpy(h->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(h->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+      rc = bfail(LORA_CE_ECUDA, "RoPE table upload failed");
+  }
+  if (rc) {
+    free_body(h);
+    delete h;
+    return rc;
+  }
+  *out = h;
+  return 0;
+}
+
+int lora_body_destroy(lora_body_handle* h) {
+  if (!h) return 0;
+  cudaSetDevice(h->cfg.device);
+  if (h->stream) cudaStreamSynchronize(h->stream);
+  free_body(h);
+  delete h;
+  return 0;
+}
+
+int lora_body_set_embedding(lora_body_handle* h, const uint16_t* token_embd,
+                            const float* output_norm) {
+  if (!h || !token_embd || !output_norm) return bfail(LORA_CE_EINVAL, "null argument");
+  BD_CUDA(cudaSetDevice(h->cfg.device));
+  BD_CUDA(cudaMemcpyAsync(h->embd, token_embd, (size_t)h->cfg.vocab * h->d * 2,
+                          cudaMemcpyHostToDevice, h->stream));
+  BD_CUDA(cudaMemcpyAsync(h->out_norm, output_norm, (size_t)h->d * 4, cudaMemcpyHostToDevice,
+                          h->stream));
+  BD_CUDA(cudaStreamSynchronize(h->stream));
+  h->have_embd = true;
+  return 0;
+}
+
+int lora_body_set_layer(lora_body_handle* h, int32_t layer, const float* attn_norm,
+                        const uint16_t* wq, const uint16_t* wk, const uint16_t* wv,
+                        const uint16_t* wo, const float* ffn_norm, const uint16_t* w_gate,
+                        const uint16_t* w_up, const uint16_t* w_down) {
+  if (!h || layer < 0 || layer >= h->cfg.n_layers || !attn_norm || !wq || !wk || !wv || !wo ||
+      !ffn_norm || !w_gate || !w_up || !w_down)
+    return bfail(LORA_CE_EINVAL, "bad argument");
+  BD_CUDA(cudaSetDevice(h->cfg.device));
+  auto& L = h->layers[layer];
+  const int d = h->d, ffn = h->ffn, kv = h->kvdim;
+  __half* tmp = nullptr;
+  if (cudaMalloc(&tmp, (size_t)ffn * d * 2) != cudaSuccess) {
+    cudaGetLastError();
+    return bfail(LORA_CE_ENOMEM, "cudaMalloc failed");
+  }
+  int rc = 0;
+  // each upload waits for the previous quantisation (same stream) before
+  // the staging buffer is overwritten
+  if (!rc) rc = upload_quant(h, wq, d, d, L.wqkv, L.sqkv, tmp);
+  if (!rc) rc = upload_quant(h, wk, kv, d, L.wqkv + (size_t)d * d, L.sqkv + d, tmp);
+  if (!rc) rc = upload_quant(h, wv, kv, d, L.wqkv + (size_t)(d + kv) * d, L.sqkv + d + kv, tmp);
+  if (!rc) rc = upload_quant(h, wo, d, d, L.wo, L.so, tmp);
+  if (!rc) rc = upload_quant(h, w_gate, ffn, d, L.wgu, L.sgu, tmp);
+  if (!rc) rc = upload_quant(h, w_up, ffn, d, L.wgu + (size_t)ffn * d, L.sgu + ffn, tmp);
+  if (!rc) rc = upload_quant(h, w_down, d, ffn, L.wd, L.sd, tmp);
+  if (!rc && (cudaMemcpyAsync(L.attn_norm, attn_norm, (size_t)d * 4, cudaMemcpyHostToDevice,
+                              h->stream) != cudaSuccess ||
+              cudaMemcpyAsync(L.ffn_norm, ffn_norm, (size_t)d * 4, cudaMemcpyHostToDevice,
+                              h->stream) != cudaSuccess))
+    rc = bfail(LORA_CE_ECUDA, "norm upload failed");
+  if (cudaStreamSynchronize(h->stream) != cudaSuccess && !rc)
+    rc = bfail(LORA_CE_ECUDA, "layer upload failed");
+  cudaFree(tmp);
+  if (!rc) L.set = true;
+  return rc;
+}
+
+int lora_body_set_window(lora_body_handle* h, int32_t layer, int32_t window) {
+  if (!h || layer < 0 || layer >= h->cfg.n_layers || window < 0)
+    return bfail(LORA_CE_EINVAL, "bad argument");
+  h->layers[layer].window = window;
+  return 0;
+}
+
+static int ready(lora_body_handle* h) {
+  if (!h) return bfail(LORA_CE_EINVAL, "null handle");
+  if (!h->have_embd) return bfail(LORA_CE_ESTATE, "lora_body_set_embedding not called");
+  for (const auto& L : h->layers)
+    if (!L.set) return bfail(LORA_CE_ESTATE, "a layer has no weights (lora_body_set_layer)");
+  return 0;
+}
+
+int lora_body_hidden(lora_body_handle* h, const int32_t* tokens, const int32_t* offsets,
+                     int32_t n_seqs, float* H_out) {
+  int rc = ready(h);
+  if (rc) return rc;
+  if (!tokens || !H_out) return bfail(LORA_CE_EINVAL, "null argument");
+  int T = 0;
+  if ((rc = check_offsets(h, offsets, n_seqs, &T))) return rc;
+  for (int t = 0; t < T; ++t)
+    if (tokens[t] < 0 || tokens[t] >= h->cfg.vocab) return bfail(LORA_CE_EINVAL, "token id out of range");
+  BD_CUDA(cudaSetDevice(h->cfg.device));
+  BD_CUDA(cudaMemcpyAsync(h->tok, tokens, (size_t)T * 4, cudaMemcpyHostToDevice, h->stream));
+  if ((rc = run_body(h, h->tok, offsets, n_seqs, T, h->hout, LORA_CE_F32))) return rc;
+  BD_CUDA(cudaMemcpyAsync(H_out, h->hout, (size_t)T * h->d * 4, cudaMemcpyDeviceToHost, h->stream));
+  return body_check_error(h);
+}
+
+int lora_body_hidden_device(lora_body_handle* h, const int32_t* d_tokens, const int32_t* offsets,
+                            int32_t n_seqs, void* d_H, int32_t h_dtype) {
+  int rc = ready(h);
+  if (rc) return rc;
+  if (!d_tokens || !d_H) return bfail(LORA_CE_EINVAL, "null argument");
+  if (h_dtype < LORA_CE_BF16 || h_dtype > LORA_CE_F32) return bfail(LORA_CE_EINVAL, "bad dtype");
+  if ((reinterpret_cast<uintptr_t>(d_H) & 15) != 0)
+    return bfail(LORA_CE_EINVAL, "d_H must be 16-byte aligned");
+  int T = 0;
+  if ((rc = check_offsets(h, offsets, n_seqs, &T))) return rc;
+  BD_CUDA(cudaSetDevice(h->cfg.device));
+  // the previous call's positions may still be in flight from pos_host
+  BD_CUDA(cudaStreamSynchronize(h->stream));
+  return run_body(h, d_tokens, offsets, n_seqs, T, d_H, h_dtype);
+}
+
+int lora_body_sync(lora_body_handle* h) {
+  if (!h) return bfail(LORA_CE_EINVAL, "null handle");
+  BD_CUDA(cudaSetDevice(h->cfg.device));
+  return body_check_error(h);
+}
+
+void* lora_body_stream(lora_body_handle* h) { return h ? (void*)h->stream : nullptr; }
+
+}  // extern "C"

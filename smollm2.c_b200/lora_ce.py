@@ -51,6 +51,13 @@ EXPORTS = [
     "lora_ce_copy_times", "lora_ce_set_comm_timeout",
 ]
 
+# Symbols declared in include/lora_body.h.
+BODY_EXPORTS = [
+    "lora_body_create", "lora_body_destroy", "lora_body_set_embedding", "lora_body_set_layer",
+    "lora_body_set_window", "lora_body_hidden", "lora_body_hidden_device", "lora_body_sync",
+    "lora_body_stream", "lora_body_last_error",
+]
+
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
               "-Xcompiler", "-fPIC", "-shared"]
 
@@ -58,7 +65,7 @@ NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", 
 def build(verbose: bool = False) -> str:
     """Compile csrc/ into liblora_ce.so (sm_100a) next to this file."""
     srcs = [os.path.join(HERE, "csrc", f) for f in ("lora_ce_api.cu", "lora_ce_noalloc.cu", "lora_ce_merge.cu",
-                                                         "lora_ce_q4k.cu")]
+                                                         "lora_ce_q4k.cu", "lora_body.cu")]
     cmd = ["nvcc", *NVCC_FLAGS, "-I" + os.path.join(REPO, "include"), "-o", LIB_PATH, *srcs,
            "-ldl"]
     if verbose:
@@ -74,6 +81,13 @@ class Config(C.Structure):
                 ("scale", C.c_float), ("lr", C.c_float), ("beta1", C.c_float),
                 ("beta2", C.c_float), ("eps", C.c_float), ("weight_decay", C.c_float),
                 ("clip_norm", C.c_float), ("max_tokens", C.c_int32), ("device", C.c_int32)]
+
+
+class BodyConfig(C.Structure):
+    _fields_ = [("n_layers", C.c_int32), ("dim", C.c_int32), ("n_heads", C.c_int32),
+                ("n_kv_heads", C.c_int32), ("ffn_hidden", C.c_int32), ("vocab", C.c_int32),
+                ("rms_eps", C.c_float), ("rope_theta", C.c_float), ("max_seq", C.c_int32),
+                ("max_tokens", C.c_int32), ("device", C.c_int32)]
 
 
 class LoraCEError(RuntimeError):
@@ -110,6 +124,18 @@ def load_library() -> C.CDLL:
     lib.lora_ce_get_grads.argtypes = [vp, vp, vp, C.POINTER(C.c_float), C.POINTER(C.c_float)]
     lib.lora_ce_get_token_loss.argtypes = [vp, vp, C.c_int32]
     lib.lora_ce_apply_grads.argtypes = [vp, vp, vp, C.c_float]
+    lib.lora_body_create.argtypes = [C.POINTER(BodyConfig), C.POINTER(vp)]
+    lib.lora_body_destroy.argtypes = [vp]
+    lib.lora_body_set_embedding.argtypes = [vp, vp, vp]
+    lib.lora_body_set_layer.argtypes = [vp, C.c_int32] + [vp] * 9
+    lib.lora_body_set_window.argtypes = [vp, C.c_int32, C.c_int32]
+    lib.lora_body_hidden.argtypes = [vp, vp, vp, C.c_int32, vp]
+    lib.lora_body_hidden_device.argtypes = [vp, vp, vp, C.c_int32, vp, C.c_int32]
+    lib.lora_body_sync.argtypes = [vp]
+    lib.lora_body_stream.argtypes = [vp]
+    lib.lora_body_stream.restype = vp
+    lib.lora_body_last_error.argtypes = []
+    lib.lora_body_last_error.restype = C.c_char_p
     lib.lora_ce_set_copy_timing.argtypes = [vp, C.c_int32]
     lib.lora_ce_set_comm_timeout.argtypes = [vp, C.c_int32]
     lib.lora_ce_copy_times.argtypes = [vp, C.POINTER(C.c_float), C.c_int32]
@@ -417,3 +443,70 @@ class LoraCE:
     def load(self, path: str) -> None:
         ad = load_lora0001(path, self.cfg.dim, self.cfg.vocab, self.cfg.rank)
         self.set_adapter(ad["A"], ad["B"], ad["step"])
+
+
+def _bcheck(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = load_library().lora_body_last_error().decode(errors="replace")
+        raise LoraCEError(f"{what} failed: {ERRORS.get(rc, rc)}: {msg}")
+
+
+class LoraBody:
+    """The body forward on the GPU (include/lora_body.h): hidden states of
+    every position of a batch of token sequences."""
+
+    def __init__(self, n_layers, dim=576, n_heads=9, n_kv_heads=3, ffn_hidden=1536,
+                 vocab=49152, rms_eps=1e-5, rope_theta=1e5, max_seq=256, max_tokens=1024,
+                 device=0):
+        self.lib = load_library()
+        self.cfg = BodyConfig(n_layers, dim, n_heads, n_kv_heads, ffn_hidden, vocab, rms_eps,
+                              rope_theta, max_seq, max_tokens, device)
+        self.h = C.c_void_p()
+        _bcheck(self.lib.lora_body_create(C.byref(self.cfg), C.byref(self.h)), "lora_body_create")
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.lora_body_destroy(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_embedding(self, token_embd_f16: np.ndarray, output_norm: np.ndarray) -> None:
+        e = np.ascontiguousarray(token_embd_f16, np.uint16)
+        n = np.ascontiguousarray(output_norm, np.float32)
+        _bcheck(self.lib.lora_body_set_embedding(self.h, _ptr(e), _ptr(n)), "set_embedding")
+
+    def set_layer(self, L: int, t: dict) -> None:
+        """t: attn_norm, wq, wk, wv, wo, ffn_norm, gate, up, down (f16 bits
+        as uint16 with rows = outputs; norms float32)."""
+        a = [np.ascontiguousarray(t[k], np.float32 if k.endswith("norm") else np.uint16)
+             for k in ("attn_norm", "wq", "wk", "wv", "wo", "ffn_norm", "gate", "up", "down")]
+        _bcheck(self.lib.lora_body_set_layer(self.h, L, *[_ptr(x) for x in a]), "set_layer")
+
+    def set_window(self, L: int, window: int) -> None:
+        _bcheck(self.lib.lora_body_set_window(self.h, L, window), "set_window")
+
+    def hidden(self, tokens: np.ndarray, offsets) -> np.ndarray:
+        tok = np.ascontiguousarray(tokens, np.int32)
+        off = np.ascontiguousarray(offsets, np.int32)
+        out = np.empty((int(off[-1]), self.cfg.dim), np.float32)
+        _bcheck(self.lib.lora_body_hidden(self.h, _ptr(tok), _ptr(off), len(off) - 1, _ptr(out)),
+                "lora_body_hidden")
+        return out
+
+    def hidden_device(self, d_tokens: int, offsets, d_H: int, dtype: int) -> None:
+        off = np.ascontiguousarray(offsets, np.int32)
+        _bcheck(self.lib.lora_body_hidden_device(self.h, C.c_void_p(d_tokens), _ptr(off),
+                                                 len(off) - 1, C.c_void_p(d_H), dtype),
+                "lora_body_hidden_device")
+
+    def sync(self) -> None:
+        _bcheck(self.lib.lora_body_sync(self.h), "lora_body_sync")
+
+    @property
+    def stream(self) -> int:
+        return self.lib.lora_body_stream(self.h) or 0

@@ -149,14 +149,18 @@ def params(rank=4, alpha=8, seq_max=256, lr=1e-3, epochs=1, checkpoint_every=0, 
 
 
 def write_smollm_gguf(path: str, seed: int, n_layers: int = 2, dim: int = 576, heads: int = 9,
-                      kv_heads: int = 3, ffn: int = 1536, vocab: int = 49152) -> np.ndarray:
+                      kv_heads: int = 3, ffn: int = 1536, vocab: int = 49152,
+                      norm_spread: float = 0.0, return_tensors: bool = False):
     """A SmolLM2-135M-shaped model file with random weights: the llama
     metadata and tensor names the reference's forward_load reads
     (src/forward.c:671-880), f16 matrices ~ N(0, 0.02) from a seed, f32
     norms of 1.0, RMSNorm eps 1e-5, RoPE theta 1e5, tied embeddings, and a
     token list of `vocab` placeholder strings.  `n_layers` is 30 in the
-    real model; fewer keep the CPU body quick.  Returns token_embd [V][d]
-    as f16 bits."""
+    real model; fewer keep the CPU body quick.  norm_spread > 0 draws the
+    norm weights from 1 + U(-spread, spread) instead.  Returns token_embd
+    [V][d] as f16 bits, or with return_tensors (token_embd, output_norm,
+    [per layer {attn_norm, wq, wk, wv, wo, ffn_norm, gate, up, down}]) with
+    the matrices as f16 bits [outputs][inputs]."""
     rng = np.random.default_rng(seed)
 
     def f16(*shape):
@@ -164,20 +168,32 @@ def write_smollm_gguf(path: str, seed: int, n_layers: int = 2, dim: int = 576, h
 
     kv_dim = dim // heads * kv_heads
     embd = f16(vocab, dim)
-    ones = np.ones(dim, np.float32)
+
+    def norm():
+        if norm_spread <= 0:
+            return np.ones(dim, np.float32)
+        return (1.0 + rng.uniform(-norm_spread, norm_spread, dim)).astype(np.float32)
+
+    out_norm = norm()
     tensors = [("token_embd.weight", [dim, vocab], GGUF_F16, embd.tobytes()),
-               ("output_norm.weight", [dim], GGUF_F32, ones.tobytes())]
+               ("output_norm.weight", [dim], GGUF_F32, out_norm.tobytes())]
+    layers = []
     for L in range(n_layers):
         b = f"blk.{L}."
-        tensors += [(b + "attn_norm.weight", [dim], GGUF_F32, ones.tobytes()),
-                    (b + "attn_q.weight", [dim, dim], GGUF_F16, f16(dim, dim).tobytes()),
-                    (b + "attn_k.weight", [dim, kv_dim], GGUF_F16, f16(kv_dim, dim).tobytes()),
-                    (b + "attn_v.weight", [dim, kv_dim], GGUF_F16, f16(kv_dim, dim).tobytes()),
-                    (b + "attn_output.weight", [dim, dim], GGUF_F16, f16(dim, dim).tobytes()),
-                    (b + "ffn_norm.weight", [dim], GGUF_F32, ones.tobytes()),
-                    (b + "ffn_gate.weight", [dim, ffn], GGUF_F16, f16(ffn, dim).tobytes()),
-                    (b + "ffn_up.weight", [dim, ffn], GGUF_F16, f16(ffn, dim).tobytes()),
-                    (b + "ffn_down.weight", [ffn, dim], GGUF_F16, f16(dim, ffn).tobytes())]
+        ly = dict(attn_norm=norm(), wq=f16(dim, dim), wk=f16(kv_dim, dim), wv=f16(kv_dim, dim),
+                  wo=f16(dim, dim), ffn_norm=norm(), gate=f16(ffn, dim), up=f16(ffn, dim),
+                  down=f16(dim, ffn))
+        layers.append({k: (v.view(np.uint16) if v.dtype == np.float16 else v)
+                       for k, v in ly.items()})
+        tensors += [(b + "attn_norm.weight", [dim], GGUF_F32, ly["attn_norm"].tobytes()),
+                    (b + "attn_q.weight", [dim, dim], GGUF_F16, ly["wq"].tobytes()),
+                    (b + "attn_k.weight", [dim, kv_dim], GGUF_F16, ly["wk"].tobytes()),
+                    (b + "attn_v.weight", [dim, kv_dim], GGUF_F16, ly["wv"].tobytes()),
+                    (b + "attn_output.weight", [dim, dim], GGUF_F16, ly["wo"].tobytes()),
+                    (b + "ffn_norm.weight", [dim], GGUF_F32, ly["ffn_norm"].tobytes()),
+                    (b + "ffn_gate.weight", [dim, ffn], GGUF_F16, ly["gate"].tobytes()),
+                    (b + "ffn_up.weight", [dim, ffn], GGUF_F16, ly["up"].tobytes()),
+                    (b + "ffn_down.weight", [ffn, dim], GGUF_F16, ly["down"].tobytes())]
     kv = [("general.architecture", "str", "llama"),
           ("llama.embedding_length", "u32", dim), ("llama.block_count", "u32", n_layers),
           ("llama.attention.head_count", "u32", heads),
@@ -187,4 +203,6 @@ def write_smollm_gguf(path: str, seed: int, n_layers: int = 2, dim: int = 576, h
           ("llama.rope.freq_base", "f32", 1e5),
           ("tokenizer.ggml.tokens", "str_arr", [f"t{i}" for i in range(vocab)])]
     write_gguf(path, tensors, kv)
+    if return_tensors:
+        return embd.view(np.uint16), out_norm, layers
     return embd.view(np.uint16)

@@ -53,3 +53,23 @@ def test_null_arguments_fail_cleanly():
     assert lib.lora_ce_destroy(None) == 0
     assert lib.lora_ce_nccl_unique_id(None) == -1
     assert lib.lora_ce_last_error()  # message set
+
+
+def test_body_library_exports_every_declared_symbol():
+    src = open(os.path.join(REPO, "include", "lora_body.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    names = sorted(set(re.findall(r"\b(lora_body_\w+)\s*\(", src)))
+    lib = lora_ce.load_library()
+    for n in names:
+        assert hasattr(lib, n), n
+    assert sorted(lora_ce.BODY_EXPORTS) == names
+
+
+def test_body_create_rejects_bad_config():
+    lib = lora_ce.load_library()
+    assert lib.lora_body_create(None, None) == -1
+    for kw in (dict(dim=100), dict(n_heads=8), dict(max_seq=0), dict(n_kv_heads=2)):
+        args = dict(n_layers=2, dim=576, n_heads=9, n_kv_heads=3)
+        args.update(kw)
+        with pytest.raises(lora_ce.LoraCEError, match="EINVAL"):
+            lora_ce.LoraBody(**args)
