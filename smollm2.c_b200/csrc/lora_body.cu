@@ -598,7 +598,7 @@ int lora_body_set_layer(lora_body_handle* h, int32_t layer, const float* attn_no
   auto& L = h->layers[layer];
   const int d = h->d, ffn = h->ffn, kv = h->kvdim;
   __half* tmp = nullptr;
-  if (cudaMalloc(&tmp, (size_t)ffn * d * 2) != cudaSuccess) {
+  if (cudaMalloc(&tmp, (size_t)std::max(ffn, d) * d * 2) != cudaSuccess) {
     cudaGetLastError();
     return bfail(LORA_CE_ENOMEM, "cudaMalloc failed");
   }
