@@ -549,6 +549,156 @@ def run_q4k(args):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------- config 1
+BODY_LAYERS, BODY_SEQ = 30, 256
+
+
+def _write_body_model(path: str):
+    sys.path.insert(0, os.path.join(REPO, "tests"))
+    import studio_fixtures as sf
+    return sf.write_smollm_gguf(path, seed=1, n_layers=BODY_LAYERS, norm_spread=0.2,
+                                return_tensors=True)
+
+
+def run_config1(args):
+    """The CPU-body training workload (30-layer SmolLM2-135M shape, packed
+    sequences of 256, rank 4, alpha 8, lr 1e-3): the whole training step
+    with its body forward.  GPU: lora_body_train_step (body forward of the
+    sample's positions, then the LoRA step), one sample (255 predicted
+    positions) per step as the reference trains, and the packed variant
+    with 4 samples per step.  CPU: the reference's own body forward and
+    train_step's body forward, as processes over the host cores, on a
+    bounded sample of positions."""
+    import tempfile
+    import numpy as np
+    import torch
+    import lora_ce
+    import workload as wl
+
+    args.warmup = max(args.warmup, 3)
+    tmp = tempfile.mkdtemp(prefix="bench_body_")
+    model = os.path.join(tmp, "m30.gguf")
+    embd, out_norm, layers = _write_body_model(model)
+    note("config 1: model written")
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(1)
+    seqs = [wl.zipf_targets(rng, BODY_SEQ, V).astype(np.int32) for _ in range(4)]
+    body = lora_ce.LoraBody(BODY_LAYERS, max_seq=BODY_SEQ, max_tokens=4 * BODY_SEQ)
+    body.set_embedding(embd, out_norm)
+    for L, t in enumerate(layers):
+        body.set_layer(L, t)
+    A = np.asarray(wl.make_step_inputs(1000, 8, V, D, 4)[2])
+    res = {}
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    st = torch.cuda.ExternalStream(body.stream, device=dev)
+    clk_out = None
+    for pack in (1, 4):
+        T = pack * (BODY_SEQ - 1)
+        ce = lora_ce.LoraCE(lora_ce.default_config(D, V, 4, T, scale=2.0, lr=LR))
+        ce.set_weight(embd)
+        ce.set_adapter(A, np.zeros((4, V), np.float32), 0)
+        tok = np.concatenate([s[:-1] for s in seqs[:pack]])
+        tgt = np.concatenate([s[1:] for s in seqs[:pack]])
+        off = np.arange(pack + 1, dtype=np.int32) * (BODY_SEQ - 1)
+        for _ in range(args.warmup):
+            body.train_step(ce, tok, off, tgt)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        clk = ClockSampler(0)
+        with clk:
+            for s_, e_ in evs:
+                with torch.cuda.stream(st):
+                    flush.fill_(1.0)
+                s_.record(st)
+                body.train_step(ce, tok, off, tgt)
+                e_.record(st)
+            torch.cuda.synchronize(dev)
+        ms = [s_.elapsed_time(e_) for s_, e_ in evs]
+        # the body alone (device tokens -> device hidden rows)
+        dT = torch.from_numpy(tok).to(dev)
+        dH = torch.empty((T, D), dtype=torch.float32, device=dev)
+        bev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        for s_, e_ in bev:
+            with torch.cuda.stream(st):
+                flush.fill_(1.0)
+            s_.record(st)
+            body.hidden_device(dT.data_ptr(), off, dH.data_ptr(), lora_ce.F32)
+            e_.record(st)
+        torch.cuda.synchronize(dev)
+        body_ms = sum(s_.elapsed_time(e_) for s_, e_ in bev) / args.steps
+        ce.close()
+        res[pack] = dict(T=T, ms=sum(ms) / len(ms), body_ms=body_ms,
+                         tokens_s=T * len(ms) / (sum(ms) / 1e3))
+        if clk_out is None:
+            clk_out = clk.summary()
+    body.close()
+    note("config 1: GPU legs done")
+    # MACs of the body per position: 30 layers x (q,k,v,o,gate,up,down) int8
+    kv = 192
+    macs = BODY_LAYERS * (D * (D + 2 * kv) + D * D + 3 * D * 1536)
+    cpu = None
+    if not args.no_cpu_baseline:
+        note("config 1: CPU reference")
+        procs = max(1, min(os.cpu_count() or 1, 16))
+        n = 24
+        ctx = mp.get_context("spawn")
+        with ctx.Pool(procs) as pool:
+            out = pool.map(_ref_body_step, [(model, 50 + i, n) for i in range(procs)])
+        wall = max(out)
+        cpu = {"value": procs * n / wall, "unit": UNIT, "cores": procs, "kind": "reference",
+               "sample": f"{procs} processes x {n} positions of a 30-layer sequence: the "
+                         "reference's body forward position by position (its forward_decode, "
+                         "base logits included); the step's lora_accum and Adam, about 1% of "
+                         "it, are not counted, so this rate is an upper bound of the "
+                         "reference's"}
+    peak_tf, _, peak_kind = peaks()
+    one = res[1]
+    line = {
+        "metric": "LoRA training step with the body forward, tokens/s", "value": one["tokens_s"],
+        "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": one["ms"], "higher_is_better": True, "scaling": "replicas only",
+        "vs_baseline": None, "dtype": "int8 body, f16 lm_head",
+        "data": "synthetic (seeded 30-layer SmolLM2-135M-shaped model file, norms 1+U(-0.2,0.2); "
+                "Zipf(1.1) token ids)",
+        "config": {"workload": "CPU-body training workload: 30 layers, d 576, 9/3 heads, FFN "
+                               "1536, V 49152, sequences of 256, rank 4, alpha 8, lr 1e-3; "
+                               "one sample (255 predicted positions) per step as the reference "
+                               "trains", "config": 1,
+                   "l2": "flushed (256 MB write) before every timed step"},
+        "body_ms_per_step": one["body_ms"],
+        "body": {"kernel": "body forward (int8 dp4a GEMMs, attention, norms)",
+                 "int8_tops": 2.0 * macs * one["T"] / (one["body_ms"] * 1e-3) / 1e12,
+                 "macs_per_position": macs},
+        "packed4": {"tokens_per_step": res[4]["T"], "ms_per_step": res[4]["ms"],
+                    "value": res[4]["tokens_s"], "body_ms_per_step": res[4]["body_ms"]},
+        "cpu_baseline": cpu,
+        "e2e": {"value": one["tokens_s"], "unit": UNIT, "h2d_bytes_per_step": 8 * one["T"],
+                "d2h_bytes_per_step": 4,
+                "note": "lora_body_train_step takes host tokens and targets and returns the loss: "
+                        "the device-timed step is already end to end"},
+        "gpu_launches": None, "clocks": clk_out,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _ref_body_step(args):
+    """Seconds of the reference's own body forward (src/forward.c, position
+    by position as train_step runs it) over one sample of n positions of the
+    30-layer model."""
+    import numpy as np
+    import oracle as orc
+    import workload as wl
+    model, seed, n = args
+    rng = np.random.default_rng(seed)
+    tokens = wl.zipf_targets(rng, n, V).astype(np.int32)
+    rb = orc.RefBody(model, n)
+    _, body_s = rb.hidden(tokens, D)
+    rb.close()
+    return body_s
+
+
 # ----------------------------------------------------------------- GPU leg
 def note(msg: str) -> None:
     """Progress on stderr (the JSON line is the only stdout)."""
@@ -751,7 +901,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--op", default="step", choices=["step", "merge", "q4k"])
-    ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
+    ap.add_argument("--config", type=int, default=2, choices=[1] + sorted(CONFIGS))
     ap.add_argument("--tokens", type=int, default=None,
                     help="positions per step (per rank for weak scaling) instead of the "
                          "workload's own")
@@ -761,6 +911,9 @@ def main():
                     help="run only the device steps (the command for an ncu capture)")
     ap.add_argument("--merge-rank", type=int, default=R)
     args = ap.parse_args()
+    if args.config == 1:
+        run_config1(args)
+        return
     apply_config(args.config)
     if args.tokens:
         CONFIG["tokens"] = args.tokens

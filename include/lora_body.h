@@ -104,6 +104,18 @@ int lora_body_hidden_device(lora_body_handle* h, const int32_t* d_tokens,
                             const int32_t* offsets, int32_t n_seqs, void* d_H,
                             int32_t h_dtype);
 
+/* One training step whose hidden states come from this body: the
+ * positions of n_seqs packed samples (tokens and offsets as
+ * lora_body_hidden; the hidden state of position t feeds the prediction of
+ * targets[t]), run through the body into the body's own device buffer, then
+ * lora_ce_step_device on `ce` (same device), waited for; *loss_out gets the
+ * step's mean loss.  This is train_step with its per-position
+ * forward_prefill / forward_decode loop (src/train.c:210-229) replaced by
+ * one batched body forward; host buffers in. */
+int lora_body_train_step(lora_body_handle* h, lora_ce_handle* ce, const int32_t* tokens,
+                         const int32_t* offsets, int32_t n_seqs, const int32_t* targets,
+                         float* loss_out);
+
 /* Wait for the handle's stream; report a device-side error. */
 int lora_body_sync(lora_body_handle* h);
 

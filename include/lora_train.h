@@ -29,6 +29,17 @@ int lora_train_set_lm_head(train_state* t, const uint16_t* w_f16);
  * QLoRA (src/studio.c:187-191). */
 int lora_train_set_lm_head_gguf(train_state* t, const gguf_ctx* g);
 
+/* Run the body forward on the GPU too (include/lora_body.h), from the
+ * model's own tensors: train_step and train_run then compute the hidden
+ * states of all of a step's positions in one batched forward instead of
+ * forward_prefill / forward_decode per position (src/train.c:210-229).  The
+ * int8 rules, the order of the float operations and the KV / RoPE modes are
+ * the reference's defaults (f32 KV cache, f32 RoPE tables); e^x comes from a
+ * double-precision exp, so hidden states can differ from the CPU body's in
+ * the last bits.  Opt-in; returns 0 or -1.  No counterpart in the
+ * reference. */
+int lora_train_set_body_gguf(train_state* t, const gguf_ctx* g);
+
 #ifdef __cplusplus
 }
 #endif

@@ -8,6 +8,9 @@
  *   _ref/train_body_gpu  with smollm2.c_b200/liblora_train.so (the GPU
  *                        trainer; -DWITH_LORA_TRAIN adds the one call that
  *                        hands it token_embd.weight)
+ *   _ref/train_body_gpubody  the same with -DWITH_GPU_BODY: the trainer
+ *                        also runs the body forward on the GPU
+ *                        (lora_train_set_body_gguf)
  * so a test can run both on the same model and data.  Never part of the
  * product.
  *
@@ -59,7 +62,11 @@ int main(int argc, char** argv) {
         fprintf(stderr, "body_drive: train_create failed\n");
     } else {
 #ifdef WITH_LORA_TRAIN
-        if (lora_train_set_lm_head_gguf(t, &g) != 0) {
+        if (lora_train_set_lm_head_gguf(t, &g) != 0
+#ifdef WITH_GPU_BODY
+            || lora_train_set_body_gguf(t, &g) != 0
+#endif
+        ) {
             train_free(t);
             forward_free(f);
             gguf_free(&g);

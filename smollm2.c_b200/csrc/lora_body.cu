@@ -11,11 +11,12 @@
 // contraction, as the reference's -std=c99 build has none): RoPE from f32
 // cos / sin tables computed on the host with the same libm calls, the
 // attention dot products and weighted sums in the reference's order, the
-// residual adds.  Two things differ: the RMSNorm's f64 sum of squares is
-// added in a different order (a difference below f32 resolution in
-// practice), and expf (softmax, sigmoid) is CUDA's, which can differ from
-// glibc's in the last bit; either can move an int8 activation by one step
-// now and then, which the tests bound.
+// residual adds, the RMSNorm's f64 sum of squares in index order.  One
+// thing differs: e^x (softmax, sigmoid) comes from a double-precision exp
+// rounded to f32 (exp_ref), which differs from glibc's expf in the last bit
+// for a small fraction of arguments; such a difference can move an int8
+// activation of the next matmul by one step now and then, which the tests
+// bound.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -52,15 +53,18 @@ constexpr int kAttnWarps = 4;
 
 // ------------------------------------------------------------------ kernels
 
+// e^x rounded to f32 from CUDA's double-precision exp: the correctly rounded
+// result except where the exact value lies within a double-precision error
+// of a float rounding boundary.  The reference calls glibc's expf, which
+// agrees with this on all but 0.008% of the floats in [-100, 80] (a sweep of
+// 1.4e9 of them on the build host); CUDA's own expf has a 2-ulp bound, and
+// every last-bit difference in a softmax weight or a sigmoid can move an
+// int8 activation of the next matmul by one step.
+__device__ __forceinline__ float exp_ref(float x) { return (float)exp((double)x); }
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-
-__device__ __forceinline__ double warp_sum_d(double v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
 
@@ -139,9 +143,12 @@ __global__ void bd_norm(const float* __restrict__ x, const float* __restrict__ w
   const int lane = threadIdx.x & 31;
   if (warp >= T) return;
   const float* xr = x + (size_t)warp * d;
+  // the f64 sum of squares in index order, as the reference adds it (each
+  // square of an f32 is exact in f64, so the order is all that matters)
   double ss = 0.0;
-  for (int i = lane; i < d; i += 32) ss += (double)xr[i] * (double)xr[i];
-  ss = warp_sum_d(ss);
+  if (lane == 0)
+    for (int i = 0; i < d; ++i) ss += (double)xr[i] * (double)xr[i];
+  ss = __shfl_sync(0xffffffffu, ss, 0);
   ss /= d;
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)ss, eps)));
   float* nr = xn + (size_t)warp * d;
@@ -183,7 +190,7 @@ __global__ void bd_act_quant(const float* __restrict__ gu, int T, int ffn, float
   float* ar = a + (size_t)warp * ffn;
   for (int i = lane; i < ffn; i += 32) {
     const float gv = g[i];
-    const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gv)));
+    const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_ref(-gv)));
     ar[i] = __fmul_rn(__fmul_rn(gv, sig), g[ffn + i]);
   }
   __syncwarp();
@@ -311,7 +318,7 @@ __global__ void __launch_bounds__(32 * kAttnWarps)
   }
   mx = warp_max(mx);
   __syncwarp();
-  for (int j = lane; j < n_keys; j += 32) sc[j] = expf(__fsub_rn(sc[j], mx));
+  for (int j = lane; j < n_keys; j += 32) sc[j] = exp_ref(__fsub_rn(sc[j], mx));
   __syncwarp();
   float sum = 0.f;
   if (lane == 0)
@@ -370,6 +377,8 @@ struct lora_body_handle {
   float* hout = nullptr;   // staging for host output
   int32_t* pos_host = nullptr;  // pinned
   int* err = nullptr;
+  int32_t* tgt = nullptr;  // staging for host targets (lora_body_train_step)
+  float* loss = nullptr;   // [loss, spare]
 };
 
 namespace {
@@ -390,8 +399,9 @@ void free_body(lora_body_handle* h) {
     for (void* p : ps)
       if (p) cudaFree(p);
   }
-  void* ps[] = {h->embd, h->out_norm, h->rope_cos, h->rope_sin, h->x,  h->xn,  h->xq,
-                h->xs,   h->qkv,      h->att,      h->gu,       h->pos, h->tok, h->hout, h->err};
+  void* ps[] = {h->embd, h->out_norm, h->rope_cos, h->rope_sin, h->x,   h->xn,  h->xq,
+                h->xs,   h->qkv,      h->att,      h->gu,       h->pos, h->tok, h->hout,
+                h->err,  h->tgt,      h->loss};
   for (void* p : ps)
     if (p) cudaFree(p);
   if (h->pos_host) cudaFreeHost(h->pos_host);
@@ -533,6 +543,8 @@ int lora_body_create(const lora_body_config* c, lora_body_handle** out) {
   if (!rc) rc = balloc(&h->tok, T);
   if (!rc) rc = balloc(&h->hout, T * d);
   if (!rc) rc = balloc(&h->err, 1);
+  if (!rc) rc = balloc(&h->tgt, T);
+  if (!rc) rc = balloc(&h->loss, 2);
   if (!rc && cudaMallocHost(reinterpret_cast<void**>(&h->pos_host), T * 4) != cudaSuccess) {
     h->pos_host = nullptr;
     rc = bfail(LORA_CE_ENOMEM, "cudaMallocHost failed");
@@ -669,6 +681,30 @@ int lora_body_hidden_device(lora_body_handle* h, const int32_t* d_tokens, const 
   // the previous call's positions may still be in flight from pos_host
   BD_CUDA(cudaStreamSynchronize(h->stream));
   return run_body(h, d_tokens, offsets, n_seqs, T, d_H, h_dtype);
+}
+
+int lora_body_train_step(lora_body_handle* h, lora_ce_handle* ce, const int32_t* tokens,
+                         const int32_t* offsets, int32_t n_seqs, const int32_t* targets,
+                         float* loss_out) {
+  int rc = ready(h);
+  if (rc) return rc;
+  if (!ce || !tokens || !targets || !loss_out) return bfail(LORA_CE_EINVAL, "null argument");
+  int T = 0;
+  if ((rc = check_offsets(h, offsets, n_seqs, &T))) return rc;
+  for (int t = 0; t < T; ++t)
+    if (tokens[t] < 0 || tokens[t] >= h->cfg.vocab || targets[t] < 0 ||
+        targets[t] >= h->cfg.vocab)
+      return bfail(LORA_CE_EINVAL, "token or target id out of range");
+  BD_CUDA(cudaSetDevice(h->cfg.device));
+  BD_CUDA(cudaMemcpyAsync(h->tok, tokens, (size_t)T * 4, cudaMemcpyHostToDevice, h->stream));
+  BD_CUDA(cudaMemcpyAsync(h->tgt, targets, (size_t)T * 4, cudaMemcpyHostToDevice, h->stream));
+  if ((rc = run_body(h, h->tok, offsets, n_seqs, T, h->hout, LORA_CE_F32))) return rc;
+  if ((rc = body_check_error(h))) return rc;  // waits: the step's inputs are ready
+  rc = lora_ce_step_device(ce, h->hout, LORA_CE_F32, T, h->tgt, h->loss);
+  if (!rc) rc = lora_ce_sync(ce);
+  if (rc) return bfail(rc, std::string("lora_ce step: ") + lora_ce_last_error());
+  BD_CUDA(cudaMemcpy(loss_out, h->loss, 4, cudaMemcpyDeviceToHost));
+  return 0;
 }
 
 int lora_body_sync(lora_body_handle* h) {

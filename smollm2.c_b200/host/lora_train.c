@@ -36,6 +36,7 @@
 #include "hw_probe.h"
 #include "data.h"
 
+#include "lora_body.h"
 #include "lora_ce.h"
 #include "lora_train.h"
 
@@ -64,6 +65,12 @@ struct train_state {
     float* H;         /* [pack * max_pred][dim] hidden rows of the current step */
     int32_t* targets; /* [pack * max_pred] */
     float* logits;    /* [vocab]: the body forward writes base logits here */
+    /* the GPU body forward (lora_train_set_body_gguf), when set: the step's
+     * input tokens and sample offsets instead of hidden rows */
+    lora_body_handle* body;
+    int32_t* tokens_in;  /* [pack * max_pred] */
+    int32_t offsets[kSampleCap + 1];
+    int n_samples;
 };
 
 static double env_double(const char* name, double def) {
@@ -145,6 +152,8 @@ train_state* train_create(forward_ctx* f, const train_params* p) {
 
 void train_free(train_state* t) {
     if (!t) return;
+    if (t->body) lora_body_destroy(t->body);
+    free(t->tokens_in);
     if (t->gpu) lora_ce_destroy(t->gpu);
     free(t->H);
     free(t->targets);
@@ -186,6 +195,62 @@ int lora_train_set_lm_head_gguf(train_state* t, const gguf_ctx* g) {
     return 0;
 }
 
+int lora_train_set_body_gguf(train_state* t, const gguf_ctx* g) {
+    if (!t || !g || t->body) return -1;
+    lora_body_config c;
+    memset(&c, 0, sizeof(c));
+    c.n_layers = (int)gguf_kv_i64(g, "llama.block_count", -1);
+    c.n_heads = (int)gguf_kv_i64(g, "llama.attention.head_count", -1);
+    c.n_kv_heads = (int)gguf_kv_i64(g, "llama.attention.head_count_kv", -1);
+    c.ffn_hidden = (int)gguf_kv_i64(g, "llama.feed_forward_length", -1);
+    c.rms_eps = gguf_kv_f32(g, "llama.attention.layer_norm_rms_epsilon", 1e-5f);
+    c.rope_theta = gguf_kv_f32(g, "llama.rope.freq_base", 10000.0f);
+    c.dim = t->dim;
+    c.vocab = t->vocab;
+    c.max_seq = t->max_pred;
+    c.max_tokens = t->max_pred * t->pack;
+    c.device = (int32_t)env_double("LORA_CE_DEVICE", 0.0);
+    lora_body_handle* b = NULL;
+    int rc = lora_body_create(&c, &b);
+    const gguf_tensor_info* e = gguf_tensor_get(g, "token_embd.weight");
+    const gguf_tensor_info* on = gguf_tensor_get(g, "output_norm.weight");
+    if (!rc && (!e || e->dtype != GGUF_DT_F16 || !on || on->dtype != GGUF_DT_F32)) rc = -1;
+    if (!rc) rc = lora_body_set_embedding(b, (const uint16_t*)gguf_tensor_data(g, e),
+                                          (const float*)gguf_tensor_data(g, on));
+    static const char* const names[9] = {"attn_norm", "attn_q", "attn_k", "attn_v",
+                                         "attn_output", "ffn_norm", "ffn_gate", "ffn_up",
+                                         "ffn_down"};
+    for (int L = 0; L < c.n_layers && !rc; L++) {
+        const void* d[9];
+        for (int k = 0; k < 9 && !rc; k++) {
+            char name[96];
+            snprintf(name, sizeof(name), "blk.%d.%s.weight", L, names[k]);
+            const gguf_tensor_info* ti = gguf_tensor_get(g, name);
+            const gguf_dtype want = (k == 0 || k == 5) ? GGUF_DT_F32 : GGUF_DT_F16;
+            if (!ti || ti->dtype != want) rc = -1;
+            else d[k] = gguf_tensor_data(g, ti);
+        }
+        if (!rc)
+            rc = lora_body_set_layer(b, L, (const float*)d[0], (const uint16_t*)d[1],
+                                     (const uint16_t*)d[2], (const uint16_t*)d[3],
+                                     (const uint16_t*)d[4], (const float*)d[5],
+                                     (const uint16_t*)d[6], (const uint16_t*)d[7],
+                                     (const uint16_t*)d[8]);
+    }
+    int32_t* tok = rc ? NULL : malloc((size_t)c.max_tokens * sizeof(int32_t));
+    if (rc || !tok) {
+        fprintf(stderr, "lora_train_set_body_gguf: %s\n",
+                rc > 0 || rc == -1 ? "model tensors missing or of an unsupported type"
+                                   : lora_body_last_error());
+        if (b) lora_body_destroy(b);
+        free(tok);
+        return -1;
+    }
+    t->body = b;
+    t->tokens_in = tok;
+    return 0;
+}
+
 /* The predicted positions of one sample (src/train.c:198-229): positions
  * 0 .. use_n-2 with use_n = min(n_tokens, seq_max), position pos predicting
  * tokens[pos+1], hidden rows from one prefill and use_n-2 decodes of the
@@ -200,6 +265,16 @@ static int gather_sample(train_state* t, const int* tokens, int n_tokens, int at
         const int tgt = tokens[pos + 1];
         if (tgt < 0 || tgt >= t->vocab) return -1;
         t->targets[at + pos] = tgt;
+    }
+    if (t->body) {  /* the GPU body runs over the whole step at once */
+        if (at == 0) t->n_samples = 0;
+        for (int pos = 0; pos < n_pred; pos++) {
+            if (tokens[pos] < 0 || tokens[pos] >= t->vocab) return -1;
+            t->tokens_in[at + pos] = tokens[pos];
+        }
+        t->offsets[t->n_samples] = at;
+        t->offsets[++t->n_samples] = at + n_pred;
+        return n_pred;
     }
     forward_reset(t->f);
     if (forward_prefill(t->f, tokens, 1, t->logits) < 0) return -1;
@@ -216,7 +291,19 @@ static int gather_sample(train_state* t, const int* tokens, int n_tokens, int at
 /* One GPU step over the n gathered positions: the mean loss, or -1.0f. */
 static float step_positions(train_state* t, int n, const char* where) {
     float loss = -1.0f;
-    const int rc = lora_ce_step(t->gpu, t->H, LORA_CE_F32, n, t->targets, &loss);
+    int rc;
+    if (t->body) {
+        rc = lora_body_train_step(t->body, t->gpu, t->tokens_in, t->offsets, t->n_samples,
+                                  t->targets, &loss);
+        if (rc != LORA_CE_OK) {
+            fprintf(stderr, "%s: lora_body error %d: %s\n", where, rc, lora_body_last_error());
+            return -1.0f;
+        }
+        t->step++;
+        t->last_loss = loss;
+        return loss;
+    }
+    rc = lora_ce_step(t->gpu, t->H, LORA_CE_F32, n, t->targets, &loss);
     if (rc != LORA_CE_OK) {
         report(where, rc);
         return -1.0f;

@@ -55,7 +55,7 @@ EXPORTS = [
 BODY_EXPORTS = [
     "lora_body_create", "lora_body_destroy", "lora_body_set_embedding", "lora_body_set_layer",
     "lora_body_set_window", "lora_body_hidden", "lora_body_hidden_device", "lora_body_sync",
-    "lora_body_stream", "lora_body_last_error",
+    "lora_body_stream", "lora_body_last_error", "lora_body_train_step",
 ]
 
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
@@ -132,6 +132,7 @@ def load_library() -> C.CDLL:
     lib.lora_body_hidden.argtypes = [vp, vp, vp, C.c_int32, vp]
     lib.lora_body_hidden_device.argtypes = [vp, vp, vp, C.c_int32, vp, C.c_int32]
     lib.lora_body_sync.argtypes = [vp]
+    lib.lora_body_train_step.argtypes = [vp, vp, vp, vp, C.c_int32, vp, C.POINTER(C.c_float)]
     lib.lora_body_stream.argtypes = [vp]
     lib.lora_body_stream.restype = vp
     lib.lora_body_last_error.argtypes = []
@@ -503,6 +504,17 @@ class LoraBody:
         _bcheck(self.lib.lora_body_hidden_device(self.h, C.c_void_p(d_tokens), _ptr(off),
                                                  len(off) - 1, C.c_void_p(d_H), dtype),
                 "lora_body_hidden_device")
+
+    def train_step(self, ce: "LoraCE", tokens, offsets, targets) -> float:
+        """lora_body_train_step: body forward of the packed samples, then one
+        LoRA step on `ce`; the mean loss."""
+        tok = np.ascontiguousarray(tokens, np.int32)
+        off = np.ascontiguousarray(offsets, np.int32)
+        tg = np.ascontiguousarray(targets, np.int32)
+        loss = C.c_float()
+        _bcheck(self.lib.lora_body_train_step(self.h, ce.h, _ptr(tok), _ptr(off), len(off) - 1,
+                                              _ptr(tg), C.byref(loss)), "lora_body_train_step")
+        return loss.value
 
     def sync(self) -> None:
         _bcheck(self.lib.lora_body_sync(self.h), "lora_body_sync")

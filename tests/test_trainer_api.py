@@ -38,7 +38,8 @@ def env():
 def test_exports_match_headers(env):
     with open(os.path.join(REPO, "include", "lora_train.h")) as f:
         extra = re.findall(r"^int\s+(lora_train_\w+)\s*\(", f.read(), re.M)
-    assert extra == ["lora_train_set_lm_head", "lora_train_set_lm_head_gguf"]
+    assert extra == ["lora_train_set_lm_head", "lora_train_set_lm_head_gguf",
+                     "lora_train_set_body_gguf"]
     for name in TRAIN_H_API + extra:
         assert hasattr(env.lib, name), name
 

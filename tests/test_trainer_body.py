@@ -62,3 +62,30 @@ def test_gpu_trainer_matches_reference_trainer_on_the_real_body(tmp_path):
         f = tmp_path / d / "lora_final.bin"
         assert os.path.getsize(f) == 28 + 4 * (576 * 4 + 4 * 49152)
         assert lora_ce.load_lora0001(str(f), 576, 49152, 4)["step"] == 3
+
+
+GPUBODY_BIN = os.path.join(sf.REPO, "oracle", "_ref", "train_body_gpubody")
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not os.path.exists(GPUBODY_BIN), reason="GPU-body driver not built")
+def test_gpu_body_trainer_matches_reference_trainer(tmp_path):
+    """The whole training step on the GPU (lora_train_set_body_gguf: body
+    forward and LoRA step) against the reference's own command with its CPU
+    body and trainer, same model and data: same lines and files, losses
+    within 1e-3 relative (the base-logit difference above; the body's
+    hidden states are bit-exact at two layers)."""
+    model = str(tmp_path / "smollm.gguf")
+    sf.write_smollm_gguf(model, seed=8, n_layers=2, norm_spread=0.2)
+    rng = np.random.default_rng(8)
+    data = str(tmp_path / "data.bin")
+    sf.write_packed(data, [rng.integers(0, 49152, 64), rng.integers(0, 49152, 1),
+                           rng.integers(0, 49152, 50), rng.integers(0, 49152, 64)])
+    ref = _run(REF_BIN, model, data, str(tmp_path / "ref"))
+    gpu = _run(GPUBODY_BIN, model, data, str(tmp_path / "gpu"))
+    assert len(ref) == len(gpu) == 4
+    for a, b in zip(gpu[:3], ref[:3]):
+        ga, gb = STEP_RE.match(a).groups(), STEP_RE.match(b).groups()
+        assert ga[:3] == gb[:3]
+        assert abs(float(ga[3]) - float(gb[3])) <= 1e-3 * float(gb[3]), (a, b)
+    assert sorted(os.listdir(tmp_path / "gpu")) == sorted(os.listdir(tmp_path / "ref"))
