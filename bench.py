@@ -683,6 +683,29 @@ def run_config1(args):
     print(json.dumps(line), flush=True)
 
 
+def body_kernel_run(args):
+    """Only the body forward of the 30-layer model on --tokens positions
+    (one sequence, default 255), --warmup + --steps times: the command for
+    an ncu capture of the body's kernels."""
+    import tempfile
+    import numpy as np
+    import lora_ce
+    import workload as wl
+
+    T = args.tokens or BODY_SEQ - 1
+    tmp = tempfile.mkdtemp(prefix="bench_body_")
+    embd, out_norm, layers = _write_body_model(os.path.join(tmp, "m30.gguf"))
+    body = lora_ce.LoraBody(BODY_LAYERS, max_seq=T, max_tokens=T)
+    body.set_embedding(embd, out_norm)
+    for L, t in enumerate(layers):
+        body.set_layer(L, t)
+    tok = wl.zipf_targets(np.random.default_rng(1), T, V).astype(np.int32)
+    for _ in range(args.warmup + args.steps):
+        body.hidden(tok, [0, T])
+    body.close()
+    print(f"body kernel run ok: {BODY_LAYERS} layers, T {T}", flush=True)
+
+
 def _ref_body_step(args):
     """Seconds of the reference's own body forward (src/forward.c, position
     by position as train_step runs it) over one sample of n positions of the
@@ -912,7 +935,10 @@ def main():
     ap.add_argument("--merge-rank", type=int, default=R)
     args = ap.parse_args()
     if args.config == 1:
-        run_config1(args)
+        if args.kernel_run:
+            body_kernel_run(args)
+        else:
+            run_config1(args)
         return
     apply_config(args.config)
     if args.tokens:
