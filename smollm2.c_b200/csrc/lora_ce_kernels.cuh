@@ -1491,9 +1491,18 @@ static __global__ void lce_adam(AdamArgs a, float* __restrict__ params, float* _
   const float inv = __fdiv_rn(1.0f, n_pred);
   float coef = 1.0f;
   if (a.clip > 0.f) {
+    // every block reduces the norm partials the same way (strided sums, then
+    // a fixed tree), so every block gets the identical coefficient
+    __shared__ double red[256];
     double ss = 0.0;
-    for (int i = 0; i < a.n_norm_parts; ++i) ss += norm_parts[i];
-    const float norm = (float)sqrt(ss);
+    for (int i = threadIdx.x; i < a.n_norm_parts; i += blockDim.x) ss += norm_parts[i];
+    red[threadIdx.x] = ss;
+    __syncthreads();
+    for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+      if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
+      __syncthreads();
+    }
+    const float norm = (float)sqrt(red[0]);
     const float c = __fdiv_rn(a.clip, __fadd_rn(norm, 1e-6f));
     if (c < 1.0f) coef = c;
   }
