@@ -48,7 +48,6 @@ int bfail(int code, const std::string& msg) {
 
 constexpr int kHd = 64;          // head dimension (the reference's attention rows)
 constexpr int kMaxSeqBody = 4096;
-constexpr int kGemmTile = 64;    // tokens x outputs per GEMM block
 constexpr int kAttnWarps = 4;
 
 // ------------------------------------------------------------------ kernels
@@ -133,21 +132,35 @@ __device__ __forceinline__ void quant_row_warp(const float* __restrict__ src, in
 }
 
 // rmsnorm (the x86 branch, src/forward.c:366-371): f64 sum of squares,
-// inv = 1 / sqrtf(ss / n + eps), out = x * inv * w.  One warp per row;
-// the normalised row goes to `xn` (scratch), then either int8 + scale
-// (quantised) or the final hidden state in h_dtype.
-__global__ void bd_norm(const float* __restrict__ x, const float* __restrict__ w, int T, int d,
-                        float eps, float* __restrict__ xn, int8_t* __restrict__ xq,
-                        float* __restrict__ xs, void* __restrict__ out, int out_dtype) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+// inv = 1 / sqrtf(ss / n + eps), out = x * inv * w.  One warp per row: the
+// lanes square the row into shared memory (each square of an f32 is exact
+// in f64), lane 0 adds them in index order as the reference does, then the
+// normalised row goes to `xn` (scratch) and on to int8 + scale (quantised)
+// or to the final hidden state in out_dtype.
+constexpr int kNormWarps = 4;
+__global__ void __launch_bounds__(32 * kNormWarps)
+    bd_norm(const float* __restrict__ x, const float* __restrict__ w, int T, int d, float eps,
+            float* __restrict__ xn, int8_t* __restrict__ xq, float* __restrict__ xs,
+            void* __restrict__ out, int out_dtype) {
+  extern __shared__ double sq_all[];
+  const int wib = threadIdx.x >> 5;
+  const int warp = blockIdx.x * kNormWarps + wib;
   const int lane = threadIdx.x & 31;
   if (warp >= T) return;
+  double* sq = sq_all + (size_t)wib * d;
   const float* xr = x + (size_t)warp * d;
-  // the f64 sum of squares in index order, as the reference adds it (each
-  // square of an f32 is exact in f64, so the order is all that matters)
+  for (int i = lane; i < d; i += 32) sq[i] = (double)xr[i] * (double)xr[i];
+  __syncwarp();
   double ss = 0.0;
-  if (lane == 0)
-    for (int i = 0; i < d; ++i) ss += (double)xr[i] * (double)xr[i];
+  if (lane == 0) {
+    int i = 0;
+    for (; i + 8 <= d; i += 8) {
+      const double a0 = sq[i], a1 = sq[i + 1], a2 = sq[i + 2], a3 = sq[i + 3];
+      const double a4 = sq[i + 4], a5 = sq[i + 5], a6 = sq[i + 6], a7 = sq[i + 7];
+      ss += a0; ss += a1; ss += a2; ss += a3; ss += a4; ss += a5; ss += a6; ss += a7;
+    }
+    for (; i < d; ++i) ss += sq[i];
+  }
   ss = __shfl_sync(0xffffffffu, ss, 0);
   ss /= d;
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn((float)ss, eps)));
@@ -179,61 +192,107 @@ __global__ void bd_quant_act(const float* __restrict__ src, int T, int n, int8_t
   quant_row_warp(src + (size_t)warp * n, n, q + (size_t)warp * n, s + warp, lane);
 }
 
-// SwiGLU then int8: a = g * (1 / (1 + expf(-g))) * u (src/forward.c:1239-1242),
-// quantised over the row.  gu is [T][2*ffn] (gate | up); one warp per row.
-__global__ void bd_act_quant(const float* __restrict__ gu, int T, int ffn, float* __restrict__ a,
-                             int8_t* __restrict__ q, float* __restrict__ s) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (warp >= T) return;
-  const float* g = gu + (size_t)warp * 2 * ffn;
-  float* ar = a + (size_t)warp * ffn;
-  for (int i = lane; i < ffn; i += 32) {
+// SwiGLU then int8: a = g * (1 / (1 + e^-g)) * u (src/forward.c:1239-1242),
+// quantised over the row (per-tensor, as quant_row_warp).  gu is [T][2*ffn]
+// (gate | up); one 256-thread block per row.
+__global__ void __launch_bounds__(256) bd_act_quant(const float* __restrict__ gu, int T, int ffn,
+                                                    float* __restrict__ a, int8_t* __restrict__ q,
+                                                    float* __restrict__ s) {
+  const int row = blockIdx.x;
+  if (row >= T) return;
+  const float* g = gu + (size_t)row * 2 * ffn;
+  float* ar = a + (size_t)row * ffn;
+  float amax = 0.f;
+  for (int i = threadIdx.x; i < ffn; i += blockDim.x) {
     const float gv = g[i];
     const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_ref(-gv)));
-    ar[i] = __fmul_rn(__fmul_rn(gv, sig), g[ffn + i]);
+    const float v = __fmul_rn(__fmul_rn(gv, sig), g[ffn + i]);
+    ar[i] = v;
+    amax = fmaxf(amax, fabsf(v));
   }
-  __syncwarp();
-  quant_row_warp(ar, ffn, q + (size_t)warp * ffn, s + warp, lane);
+  __shared__ float red[32];
+  amax = warp_max(amax);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    v = warp_max(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  amax = red[0];
+  const float inv = amax > 0.f ? __fdiv_rn(127.0f, amax) : 0.f;
+  for (int i = threadIdx.x; i < ffn; i += blockDim.x) {
+    int v = (int)roundf(__fmul_rn(ar[i], inv));
+    v = v > 127 ? 127 : v < -127 ? -127 : v;
+    q[(size_t)row * ffn + i] = (int8_t)v;
+  }
+  if (threadIdx.x == 0) s[row] = amax > 0.f ? __fdiv_rn(amax, 127.0f) : 1.0f;
 }
 
 // Y[t][n] (+)= (float)(sum_k X[t][k] * W[n][k]) * xs[t] * ws[n]: the
 // reference's matmul_q8_dot_perrow (src/forward.c:470-511, int32 sums, two
 // rounded multiplies), with `accumulate` adding it to Y as the residual
-// add does.  64 x 64 tiles, K in 64-byte steps (K % 64 == 0), dp4a.
-__global__ void __launch_bounds__(256) bd_gemm_q8(const int8_t* __restrict__ X,
+// add does.  Tiles of 32 positions x 64 outputs (small position counts still
+// spread over the SMs), 128 threads of 4 x 4 outputs, K in 64-byte steps
+// (K % 64 == 0) with the next step's tile loaded into registers while the
+// current one is multiplied (dp4a; the int32 sums are exact in any order).
+constexpr int kGemmTM = 32, kGemmTN = 64;
+__global__ void __launch_bounds__(128) bd_gemm_q8(const int8_t* __restrict__ X,
                                                   const float* __restrict__ xs, int T, int K,
                                                   const int8_t* __restrict__ W,
                                                   const float* __restrict__ ws, int N,
                                                   float* __restrict__ Y, int ldy, int accumulate) {
-  __shared__ int sX[kGemmTile][17];
-  __shared__ int sW[kGemmTile][17];
-  const int t0 = blockIdx.y * kGemmTile, n0 = blockIdx.x * kGemmTile;
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  __shared__ int sX[kGemmTM][17];
+  __shared__ int sW[kGemmTN][17];
+  const int t0 = blockIdx.y * kGemmTM, n0 = blockIdx.x * kGemmTN;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // 16 x 8 threads
   int acc[4][4];
 #pragma unroll
   for (int m = 0; m < 4; ++m)
 #pragma unroll
     for (int n = 0; n < 4; ++n) acc[m][n] = 0;
+  // this thread's share of a K-step: 4 words of X, 8 of W
+  int rx[4], rw[8];
+  auto load = [&](int k0) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = threadIdx.x + 128 * u, r = i >> 4, c = i & 15;
+      const int tr = t0 + r;
+      rx[u] = tr < T ? __ldg(reinterpret_cast<const int*>(X + (size_t)tr * K + k0 + 4 * c)) : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = threadIdx.x + 128 * u, r = i >> 4, c = i & 15;
+      const int nr = n0 + r;
+      rw[u] = nr < N ? __ldg(reinterpret_cast<const int*>(W + (size_t)nr * K + k0 + 4 * c)) : 0;
+    }
+  };
+  load(0);
   for (int k0 = 0; k0 < K; k0 += 64) {
-    for (int i = threadIdx.x; i < kGemmTile * 16; i += 256) {
-      const int r = i >> 4, c = i & 15;
-      const int tr = t0 + r, nr = n0 + r;
-      sX[r][c] = tr < T ? *reinterpret_cast<const int*>(X + (size_t)tr * K + k0 + 4 * c) : 0;
-      sW[r][c] = nr < N ? *reinterpret_cast<const int*>(W + (size_t)nr * K + k0 + 4 * c) : 0;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = threadIdx.x + 128 * u;
+      sX[i >> 4][i & 15] = rx[u];
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = threadIdx.x + 128 * u;
+      sW[i >> 4][i & 15] = rw[u];
     }
     __syncthreads();
+    if (k0 + 64 < K) load(k0 + 64);
 #pragma unroll
     for (int c = 0; c < 16; ++c) {
-      int a[4], b[4];
+      int av[4], bv[4];
 #pragma unroll
-      for (int m = 0; m < 4; ++m) a[m] = sX[ty * 4 + m][c];
+      for (int m = 0; m < 4; ++m) av[m] = sX[ty * 4 + m][c];
 #pragma unroll
-      for (int n = 0; n < 4; ++n) b[n] = sW[tx * 4 + n][c];
+      for (int n = 0; n < 4; ++n) bv[n] = sW[tx * 4 + n][c];
 #pragma unroll
       for (int m = 0; m < 4; ++m)
 #pragma unroll
-        for (int n = 0; n < 4; ++n) acc[m][n] = __dp4a(a[m], b[n], acc[m][n]);
+        for (int n = 0; n < 4; ++n) acc[m][n] = __dp4a(av[m], bv[n], acc[m][n]);
     }
     __syncthreads();
   }
@@ -276,9 +335,11 @@ __global__ void bd_rope(float* __restrict__ qkv, int T, int ld, int n_rot_heads,
 
 // Causal GQA attention in the reference's order (src/forward.c:1186-1229):
 // one warp per (position, head).  Scores q.k / 8 (each lane one key, the
-// 64-term sum in index order), max, e = expf(s - max), the sum of e in key
+// 64-term sum in index order), max, e = e^(s - max), the sum of e in key
 // order (lane 0), then out[i] = sum over keys of (e * (1/sum)) * v[i] in key
-// order (lanes over i).  Keys from seq_start + s_start(window) to t.
+// order (lanes over i).  Keys from seq_start + s_start(window) to t.  The
+// loads are vectorised and the key loops unrolled so that they are in
+// flight ahead of the ordered additions.
 __global__ void __launch_bounds__(32 * kAttnWarps)
     bd_attn(const float* __restrict__ qkv, int T, int ld, int nh, int nkv, int dim,
             const int32_t* __restrict__ pos, int window, float* __restrict__ out, int max_seq) {
@@ -288,8 +349,7 @@ __global__ void __launch_bounds__(32 * kAttnWarps)
   const long long item = (long long)blockIdx.x * kAttnWarps + wib;
   if (item >= (long long)T * nh) return;
   const int t = (int)(item / nh), h = (int)(item % nh);
-  float* sc = sc_all + (size_t)wib * (max_seq + kHd);
-  float* qs = sc + max_seq;
+  float* sc = sc_all + (size_t)wib * max_seq;
   const int kvh = h * nkv / nh;
   const int p = pos[t];
   int lo = 0;
@@ -300,18 +360,29 @@ __global__ void __launch_bounds__(32 * kAttnWarps)
   }
   const int first = t - p + lo;  // global index of the first key
   const int n_keys = p - lo + 1;
-  const float* q = qkv + (size_t)t * ld + h * kHd;
-  qs[lane] = q[lane];
-  qs[lane + 32] = q[lane + 32];
-  __syncwarp();
+  float qv[kHd];
+  {
+    const float4* q4 = reinterpret_cast<const float4*>(qkv + (size_t)t * ld + h * kHd);
+#pragma unroll
+    for (int i = 0; i < kHd / 4; ++i) {
+      const float4 v = __ldg(q4 + i);
+      qv[4 * i] = v.x; qv[4 * i + 1] = v.y; qv[4 * i + 2] = v.z; qv[4 * i + 3] = v.w;
+    }
+  }
   const float* kbase = qkv + dim + kvh * kHd;
   const float* vbase = qkv + dim + nkv * kHd + kvh * kHd;
   float mx = -INFINITY;
   for (int j = lane; j < n_keys; j += 32) {
-    const float* kr = kbase + (size_t)(first + j) * ld;
+    const float4* k4 = reinterpret_cast<const float4*>(kbase + (size_t)(first + j) * ld);
+    float kv[kHd];
+#pragma unroll
+    for (int i = 0; i < kHd / 4; ++i) {
+      const float4 v = __ldg(k4 + i);
+      kv[4 * i] = v.x; kv[4 * i + 1] = v.y; kv[4 * i + 2] = v.z; kv[4 * i + 3] = v.w;
+    }
     float d = 0.f;
-#pragma unroll 16
-    for (int i = 0; i < kHd; ++i) d = __fadd_rn(d, __fmul_rn(qs[i], kr[i]));
+#pragma unroll
+    for (int i = 0; i < kHd; ++i) d = __fadd_rn(d, __fmul_rn(qv[i], kv[i]));
     d = __fmul_rn(d, 0.125f);  // 1 / sqrtf(64)
     sc[j] = d;
     mx = fmaxf(mx, d);
@@ -321,12 +392,37 @@ __global__ void __launch_bounds__(32 * kAttnWarps)
   for (int j = lane; j < n_keys; j += 32) sc[j] = exp_ref(__fsub_rn(sc[j], mx));
   __syncwarp();
   float sum = 0.f;
-  if (lane == 0)
-    for (int j = 0; j < n_keys; ++j) sum = __fadd_rn(sum, sc[j]);
+  if (lane == 0) {
+    int j = 0;
+    for (; j + 8 <= n_keys; j += 8) {
+      const float e0 = sc[j], e1 = sc[j + 1], e2 = sc[j + 2], e3 = sc[j + 3];
+      const float e4 = sc[j + 4], e5 = sc[j + 5], e6 = sc[j + 6], e7 = sc[j + 7];
+      sum = __fadd_rn(sum, e0); sum = __fadd_rn(sum, e1); sum = __fadd_rn(sum, e2);
+      sum = __fadd_rn(sum, e3); sum = __fadd_rn(sum, e4); sum = __fadd_rn(sum, e5);
+      sum = __fadd_rn(sum, e6); sum = __fadd_rn(sum, e7);
+    }
+    for (; j < n_keys; ++j) sum = __fadd_rn(sum, sc[j]);
+  }
   sum = __shfl_sync(0xffffffffu, sum, 0);
   const float inv_sum = sum > 0.f ? __fdiv_rn(1.0f, sum) : 0.f;
   float o0 = 0.f, o1 = 0.f;
-  for (int j = 0; j < n_keys; ++j) {
+  int j = 0;
+  for (; j + 8 <= n_keys; j += 8) {
+    float va[8], vb[8], wg[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const float* vr = vbase + (size_t)(first + j + u) * ld;
+      va[u] = __ldg(vr + lane);
+      vb[u] = __ldg(vr + lane + 32);
+      wg[u] = __fmul_rn(sc[j + u], inv_sum);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      o0 = __fadd_rn(o0, __fmul_rn(wg[u], va[u]));
+      o1 = __fadd_rn(o1, __fmul_rn(wg[u], vb[u]));
+    }
+  }
+  for (; j < n_keys; ++j) {
     const float wgt = __fmul_rn(sc[j], inv_sum);
     const float* vr = vbase + (size_t)(first + j) * ld;
     o0 = __fadd_rn(o0, __fmul_rn(wgt, vr[lane]));
@@ -443,33 +539,36 @@ int run_body(lora_body_handle* h, const int32_t* d_tok, const int32_t* offsets, 
   const int eb = (int)std::min<long long>(((long long)T * d + 255) / 256, 4096);
   bd_embed<<<eb, 256, 0, st>>>(d_tok, T, d, h->cfg.vocab, h->embd, h->x, h->err);
   const int rows_blocks = (T * 32 + 255) / 256;  // one warp per row, 8 per block
-  const dim3 g_qkv((h->nqkv + kGemmTile - 1) / kGemmTile, (T + kGemmTile - 1) / kGemmTile);
-  const dim3 g_d((d + kGemmTile - 1) / kGemmTile, (T + kGemmTile - 1) / kGemmTile);
-  const dim3 g_gu((2 * ffn + kGemmTile - 1) / kGemmTile, (T + kGemmTile - 1) / kGemmTile);
+  const int norm_blocks = (T + kNormWarps - 1) / kNormWarps;
+  const size_t norm_smem = (size_t)kNormWarps * d * sizeof(double);
+  const int tm = (T + kGemmTM - 1) / kGemmTM;
+  const dim3 g_qkv((h->nqkv + kGemmTN - 1) / kGemmTN, tm);
+  const dim3 g_d((d + kGemmTN - 1) / kGemmTN, tm);
+  const dim3 g_gu((2 * ffn + kGemmTN - 1) / kGemmTN, tm);
   const int max_seq = h->cfg.max_seq;
-  const size_t attn_smem = (size_t)kAttnWarps * (max_seq + kHd) * 4;
+  const size_t attn_smem = (size_t)kAttnWarps * max_seq * 4;
   const long long att_items = (long long)T * nh;
   const int rope_blocks = (int)std::min<long long>(((long long)T * (nh + nkv) * 32 + 255) / 256, 8192);
   for (int L = 0; L < h->cfg.n_layers; ++L) {
     const auto& ly = h->layers[L];
-    bd_norm<<<rows_blocks, 256, 0, st>>>(h->x, ly.attn_norm, T, d, h->cfg.rms_eps, h->xn, h->xq,
+    bd_norm<<<norm_blocks, 32 * kNormWarps, norm_smem, st>>>(h->x, ly.attn_norm, T, d, h->cfg.rms_eps, h->xn, h->xq,
                                          h->xs, nullptr, 0);
-    bd_gemm_q8<<<g_qkv, 256, 0, st>>>(h->xq, h->xs, T, d, ly.wqkv, ly.sqkv, h->nqkv, h->qkv,
+    bd_gemm_q8<<<g_qkv, 128, 0, st>>>(h->xq, h->xs, T, d, ly.wqkv, ly.sqkv, h->nqkv, h->qkv,
                                       h->nqkv, 0);
     bd_rope<<<rope_blocks, 256, 0, st>>>(h->qkv, T, h->nqkv, nh + nkv, h->pos, h->rope_cos,
                                          h->rope_sin);
     bd_attn<<<(unsigned)((att_items + kAttnWarps - 1) / kAttnWarps), 32 * kAttnWarps, attn_smem,
               st>>>(h->qkv, T, h->nqkv, nh, nkv, d, h->pos, ly.window, h->att, max_seq);
     bd_quant_act<<<rows_blocks, 256, 0, st>>>(h->att, T, d, h->xq, h->xs);
-    bd_gemm_q8<<<g_d, 256, 0, st>>>(h->xq, h->xs, T, d, ly.wo, ly.so, d, h->x, d, 1);
-    bd_norm<<<rows_blocks, 256, 0, st>>>(h->x, ly.ffn_norm, T, d, h->cfg.rms_eps, h->xn, h->xq,
+    bd_gemm_q8<<<g_d, 128, 0, st>>>(h->xq, h->xs, T, d, ly.wo, ly.so, d, h->x, d, 1);
+    bd_norm<<<norm_blocks, 32 * kNormWarps, norm_smem, st>>>(h->x, ly.ffn_norm, T, d, h->cfg.rms_eps, h->xn, h->xq,
                                          h->xs, nullptr, 0);
-    bd_gemm_q8<<<g_gu, 256, 0, st>>>(h->xq, h->xs, T, d, ly.wgu, ly.sgu, 2 * ffn, h->gu,
+    bd_gemm_q8<<<g_gu, 128, 0, st>>>(h->xq, h->xs, T, d, ly.wgu, ly.sgu, 2 * ffn, h->gu,
                                      2 * ffn, 0);
-    bd_act_quant<<<rows_blocks, 256, 0, st>>>(h->gu, T, ffn, h->xn, h->xq, h->xs);
-    bd_gemm_q8<<<g_d, 256, 0, st>>>(h->xq, h->xs, T, ffn, ly.wd, ly.sd, d, h->x, d, 1);
+    bd_act_quant<<<T, 256, 0, st>>>(h->gu, T, ffn, h->xn, h->xq, h->xs);
+    bd_gemm_q8<<<g_d, 128, 0, st>>>(h->xq, h->xs, T, ffn, ly.wd, ly.sd, d, h->x, d, 1);
   }
-  bd_norm<<<rows_blocks, 256, 0, st>>>(h->x, h->out_norm, T, d, h->cfg.rms_eps, h->xn, nullptr,
+  bd_norm<<<norm_blocks, 32 * kNormWarps, norm_smem, st>>>(h->x, h->out_norm, T, d, h->cfg.rms_eps, h->xn, nullptr,
                                        nullptr, out, out_dtype);
   BD_CUDA(cudaGetLastError());
   return 0;
@@ -551,8 +650,11 @@ int lora_body_create(const lora_body_config* c, lora_body_handle** out) {
   }
   if (!rc && cudaMemset(h->err, 0, 4) != cudaSuccess) rc = bfail(LORA_CE_ECUDA, "cudaMemset failed");
   if (!rc && cudaFuncSetAttribute(bd_attn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)(kAttnWarps * (c->max_seq + kHd) * 4)) != cudaSuccess)
+                                  (int)(kAttnWarps * c->max_seq * 4)) != cudaSuccess)
     rc = bfail(LORA_CE_ECUDA, "attention shared memory");
+  if (!rc && cudaFuncSetAttribute(bd_norm, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)(kNormWarps * c->dim * sizeof(double))) != cudaSuccess)
+    rc = bfail(LORA_CE_ECUDA, "norm shared memory");
   if (!rc) {
     // RoPE tables exactly as forward_load builds them (src/forward.c:889-899)
     const int half = kHd / 2;
