@@ -134,3 +134,37 @@ def test_body_full_model_one_sequence(tmp_path):
     print("by position (every 16th):", " ".join(f"{e:.1e}" for e in err[::16]))
     assert err.max() <= ROW_RTOL
     assert np.all(err[:8] == 0.0)  # before any e^x difference has had an effect
+
+
+@pytest.mark.gpu
+def test_body_train_step_is_body_then_step(tmp_path):
+    """lora_body_train_step (body into its own buffer, then the LoRA step)
+    gives the loss and adapter of the two calls made separately: the body's
+    hidden rows through lora_ce_step, packed samples included."""
+    model = str(tmp_path / "m.gguf")
+    embd, out_norm, layers = sf.write_smollm_gguf(model, seed=4, n_layers=2, norm_spread=0.2,
+                                                  return_tensors=True)
+    import workload as wl
+    rng = np.random.default_rng(6)
+    seqs = [wl.zipf_targets(rng, n, 49152).astype(np.int32) for n in (40, 2, 64)]
+    tok = np.concatenate([s[:-1] for s in seqs])
+    tgt = np.concatenate([s[1:] for s in seqs])
+    off = np.cumsum([0] + [len(s) - 1 for s in seqs])
+    T = int(off[-1])
+    _, _, A, B = wl.make_step_inputs(6, 8, 49152, 576, 4)
+    b = body_from(embd, out_norm, layers, 64, 128)
+    out = []
+    for fused in (True, False):
+        ce = lora_ce.LoraCE(lora_ce.default_config(576, 49152, 4, T, scale=2.0, lr=1e-3))
+        ce.set_weight(embd)
+        ce.set_adapter(A, B, 0)
+        if fused:
+            loss = b.train_step(ce, tok, off, tgt)
+        else:
+            loss = ce.step(b.hidden(tok, off), tgt)
+        out.append((loss, ce.get_adapter()[1], ce.get_grads()[1]))
+        ce.close()
+    b.close()
+    assert out[0][0] == out[1][0]
+    np.testing.assert_array_equal(out[0][1], out[1][1])
+    np.testing.assert_array_equal(out[0][2], out[1][2])
