@@ -855,7 +855,15 @@ def measure(rig, m, h, tgt, dH, dT, T, world, steps, warmup, clocks=None, breakd
     for _ in range(2):
         m.step(hHn, hTn)
     rig.barrier()
-    e2e_ms = rig.timed(st, lambda: m.step(hHn, hTn), steps)
+    host = []
+
+    def e2e_step():
+        m.step(hHn, hTn)
+        host.append(m.copy_times())  # the graph replay's host enqueue / wait
+
+    e2e_ms = rig.timed(st, e2e_step, steps)
+    out["e2e_host_us"] = {"enqueue_median": round(statistics.median(x["host_us"] for x in host), 1),
+                          "wait_median": round(statistics.median(x["wait_us"] for x in host), 1)}
     out["e2e_ms"] = e2e_ms
     out["e2e_value"] = world * T * steps / (rig.max_over_ranks(sum(e2e_ms)) / 1e3)
     out["h2d_bytes"] = int(hH.numel() * 2 + hT.numel() * 4)
@@ -1061,6 +1069,7 @@ def main():
                     "ms_per_step": {"min": round(min(e2e_ms), 4),
                                     "median": round(statistics.median(e2e_ms), 4),
                                     "max": round(max(e2e_ms), 4)},
+                    "graph_host_us": res.get("e2e_host_us"),
                     "breakdown": res.get("e2e_breakdown")},
             "gpu_launches": res["launches"] * args.steps,
             "clocks": clk,

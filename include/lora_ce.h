@@ -185,7 +185,8 @@ const char* lora_ce_phase_name(int32_t i);
  * result, [2] ms from the step's start on the compute stream to the start
  * of the copies, [3 .. 3+c) ms of each of the c chunk copies of h, [3+c]
  * ms from the step's start to the result read-back.  Returns how many
- * values it wrote (at most cap). */
+ * values it wrote (at most cap).  With timing off it writes only [0] and
+ * [1] of the last lora_ce_step (graph replays included) and returns 2. */
 int lora_ce_set_copy_timing(lora_ce_handle* h, int32_t enable);
 int32_t lora_ce_copy_times(lora_ce_handle* h, float* out, int32_t cap);
 

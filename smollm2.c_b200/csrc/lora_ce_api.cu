@@ -1572,8 +1572,13 @@ int lora_ce_set_copy_timing(lora_ce_handle* h, int32_t enable) {
 }
 
 int32_t lora_ce_copy_times(lora_ce_handle* h, float* out, int32_t cap) {
-  if (!h || !out || !h->ctime || h->ctime_chunks < 1)
-    return fail(LORA_CE_EINVAL, "copy timing not enabled or no host-input step yet");
+  if (!h || !out || cap < 1) return fail(LORA_CE_EINVAL, "bad argument");
+  if (!h->ctime) {  // the host's own times of the last lora_ce_step only
+    out[0] = h->host_us[0];
+    if (cap > 1) out[1] = h->host_us[1];
+    return cap > 1 ? 2 : 1;
+  }
+  if (h->ctime_chunks < 1) return fail(LORA_CE_EINVAL, "no host-input step yet");
   if (cudaSetDevice(h->cfg.device) != cudaSuccess ||
       cudaEventSynchronize(h->tev[kMaxChunks + 2]) != cudaSuccess)
     return fail(LORA_CE_ECUDA, "cudaEventSynchronize failed");

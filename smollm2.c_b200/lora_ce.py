@@ -414,6 +414,8 @@ class LoraCE:
         if n < 0:
             _check(n, "copy_times")
         v = [float(buf[i]) for i in range(n)]
+        if n == 2:  # timing off: the host's times only
+            return {"host_us": v[0], "wait_us": v[1]}
         return {"host_us": v[0], "wait_us": v[1], "copy_wait_ms": v[2], "chunk_ms": v[3:-1],
                 "step_ms": v[-1]}
 
