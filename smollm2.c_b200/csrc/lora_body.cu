@@ -24,6 +24,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -475,6 +476,13 @@ struct lora_body_handle {
   int* err = nullptr;
   int32_t* tgt = nullptr;  // staging for host targets (lora_body_train_step)
   float* loss = nullptr;   // [loss, spare]
+  // the forward as a CUDA graph, for the last (T, tokens, output, dtype)
+  bool use_graph = true;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t gexec = nullptr;
+  int gT = -1, gdtype = 0;
+  const int32_t* gtok = nullptr;
+  void* gout = nullptr;
 };
 
 namespace {
@@ -489,7 +497,10 @@ int balloc(T** p, size_t count) {
   return 0;
 }
 
+void drop_body_graph(lora_body_handle* h);
+
 void free_body(lora_body_handle* h) {
+  drop_body_graph(h);
   for (auto& L : h->layers) {
     void* ps[] = {L.wqkv, L.sqkv, L.wo, L.so, L.wgu, L.sgu, L.wd, L.sd, L.attn_norm, L.ffn_norm};
     for (void* p : ps)
@@ -528,14 +539,10 @@ int check_offsets(lora_body_handle* h, const int32_t* offsets, int n_seqs, int* 
 }
 
 // The whole forward on the handle's stream: d_tok [T] -> out [T][d].
-int run_body(lora_body_handle* h, const int32_t* d_tok, const int32_t* offsets, int n_seqs,
-             int T, void* out, int out_dtype) {
+// The forward's kernels (capturable: no host work, no copies).
+int enqueue_body(lora_body_handle* h, const int32_t* d_tok, int T, void* out, int out_dtype) {
   cudaStream_t st = h->stream;
   const int d = h->d, ffn = h->ffn, nh = h->cfg.n_heads, nkv = h->cfg.n_kv_heads;
-  // position of every token within its sequence
-  for (int i = 0; i < n_seqs; ++i)
-    for (int t = offsets[i]; t < offsets[i + 1]; ++t) h->pos_host[t] = t - offsets[i];
-  BD_CUDA(cudaMemcpyAsync(h->pos, h->pos_host, (size_t)T * 4, cudaMemcpyHostToDevice, st));
   const int eb = (int)std::min<long long>(((long long)T * d + 255) / 256, 4096);
   bd_embed<<<eb, 256, 0, st>>>(d_tok, T, d, h->cfg.vocab, h->embd, h->x, h->err);
   const int rows_blocks = (T * 32 + 255) / 256;  // one warp per row, 8 per block
@@ -571,6 +578,52 @@ int run_body(lora_body_handle* h, const int32_t* d_tok, const int32_t* offsets, 
   bd_norm<<<norm_blocks, 32 * kNormWarps, norm_smem, st>>>(h->x, h->out_norm, T, d, h->cfg.rms_eps, h->xn, nullptr,
                                        nullptr, out, out_dtype);
   BD_CUDA(cudaGetLastError());
+  return 0;
+}
+
+void drop_body_graph(lora_body_handle* h) {
+  if (h->gexec) cudaGraphExecDestroy(h->gexec);
+  if (h->graph) cudaGraphDestroy(h->graph);
+  h->gexec = nullptr;
+  h->graph = nullptr;
+  h->gT = -1;
+}
+
+// Positions of the tokens within their sequences (uploaded every call), then
+// the forward: a CUDA graph of its ~8 launches per layer, captured on first
+// use and replayed while (T, tokens, output, dtype) repeat.
+int run_body(lora_body_handle* h, const int32_t* d_tok, const int32_t* offsets, int n_seqs,
+             int T, void* out, int out_dtype) {
+  cudaStream_t st = h->stream;
+  for (int i = 0; i < n_seqs; ++i)
+    for (int t = offsets[i]; t < offsets[i + 1]; ++t) h->pos_host[t] = t - offsets[i];
+  BD_CUDA(cudaMemcpyAsync(h->pos, h->pos_host, (size_t)T * 4, cudaMemcpyHostToDevice, st));
+  if (!h->use_graph) return enqueue_body(h, d_tok, T, out, out_dtype);
+  if (!(h->gexec && h->gT == T && h->gtok == d_tok && h->gout == out && h->gdtype == out_dtype)) {
+    drop_body_graph(h);
+    cudaGraph_t graph = nullptr;
+    if (cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+      cudaGetLastError();
+      h->use_graph = false;
+      return enqueue_body(h, d_tok, T, out, out_dtype);
+    }
+    const int rc = enqueue_body(h, d_tok, T, out, out_dtype);
+    const cudaError_t ce = cudaStreamEndCapture(st, &graph);
+    cudaGraphExec_t exec = nullptr;
+    if (rc || ce != cudaSuccess || !graph || cudaGraphInstantiate(&exec, graph, 0) != cudaSuccess) {
+      if (graph) cudaGraphDestroy(graph);
+      cudaGetLastError();
+      h->use_graph = false;  // launch directly from now on
+      return rc ? rc : enqueue_body(h, d_tok, T, out, out_dtype);
+    }
+    h->graph = graph;
+    h->gexec = exec;
+    h->gT = T;
+    h->gtok = d_tok;
+    h->gout = out;
+    h->gdtype = out_dtype;
+  }
+  BD_CUDA(cudaGraphLaunch(h->gexec, st));
   return 0;
 }
 
@@ -611,6 +664,10 @@ int lora_body_create(const lora_body_config* c, lora_body_handle** out) {
   h->nqkv = h->d + 2 * h->kvdim;
   h->Tcap = c->max_tokens;
   h->layers.resize(c->n_layers);
+  {
+    const char* e = getenv("LORA_BODY_GRAPHS");  // "0": launch the kernels directly
+    h->use_graph = !(e && e[0] == '0');
+  }
   const size_t T = (size_t)h->Tcap, d = h->d, ffn = h->ffn, wide = std::max(d, ffn);
   int rc = 0;
   if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess)
@@ -741,6 +798,7 @@ int lora_body_set_layer(lora_body_handle* h, int32_t layer, const float* attn_no
 int lora_body_set_window(lora_body_handle* h, int32_t layer, int32_t window) {
   if (!h || layer < 0 || layer >= h->cfg.n_layers || window < 0)
     return bfail(LORA_CE_EINVAL, "bad argument");
+  if (h->layers[layer].window != window) drop_body_graph(h);  // captured with the old one
   h->layers[layer].window = window;
   return 0;
 }
