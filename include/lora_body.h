@@ -97,7 +97,9 @@ int lora_body_hidden(lora_body_handle* h, const int32_t* tokens, const int32_t* 
 /* The same on device memory: d_tokens [T] on the handle's device, offsets
  * on the host, d_H [T][dim] of h_dtype (LORA_CE_F32, LORA_CE_BF16 or
  * LORA_CE_F16; 16-byte aligned).  Enqueued on the handle's stream; returns
- * without waiting.  Token ids are range-checked on the GPU: an id outside
+ * without waiting for this call's work (it does wait for the previous
+ * call's, whose position table it reuses).  Token ids are range-checked on
+ * the GPU: an id outside
  * [0, vocab) is read as 0 and reported by the next lora_body_sync as
  * LORA_CE_EDEVICE. */
 int lora_body_hidden_device(lora_body_handle* h, const int32_t* d_tokens,

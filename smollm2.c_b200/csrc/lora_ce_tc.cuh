@@ -130,6 +130,19 @@ __device__ __forceinline__ void split_f16x2(float2 x, uint32_t& hi, uint32_t& lo
   lo = pack_f16x2(r.x, r.y);
 }
 
+// The streamed tile of linear tile x (in resident row a): each row's tiles
+// are rotated so that the cluster owning the row's first tile takes
+// streamed tile k mod n_b as its k-th tile.  All clusters then sweep the
+// streamed operand (W in pass 1, h in pass 2) in phase, which keeps the
+// window of it that they read at one time small in L2.  A rotation of a
+// whole row is a permutation of its tiles, so every tile is still taken
+// exactly once, and every role of the kernel uses the same mapping.
+__device__ __forceinline__ int tc_tile_b(long long x, int a, int n_b, long long total, int G) {
+  const long long row0 = (long long)a * n_b;
+  const long long start = tile_start(tile_owner(row0, total, G), total, G);  // <= row0
+  return (int)((x - start) % n_b);
+}
+
 // Rank accumulator of this thread's row: Q[j] = acc[j] + acc[R + j] for
 // ranks [j0, j0 + 16) (or all R < 16).  Waits for its own TMEM loads.
 template <int R>
@@ -249,7 +262,7 @@ __global__ void __launch_bounds__(kThreadsT, 1)
       bool ok = true;
       for (long long x = x_begin; x < x_end && ok; ++x) {
         const int a = (int)(x / g.n_b);
-        const int b = (int)(x % g.n_b);
+        const int b = tc_tile_b(x, a, g.n_b, total, G);
         if (a != cur_a) {
           if (a_uses > 0 &&
               !mbar_wait(&bars[kTAEmpty], (a_uses - 1) & 1, g.err, kErrWaitProducer)) {
@@ -491,7 +504,7 @@ __global__ void __launch_bounds__(kThreadsT, 1)
 
     for (long long x = x_begin; x < x_end; ++x, ++li) {
       const int a = (int)(x / g.n_b);
-      const int b = (int)(x % g.n_b);
+      const int b = tc_tile_b(x, a, g.n_b, total, G);
       if (a != cur_a) {
         if (cur_a >= 0) flush_block(cur_a, blk);
         rr = (g.a0 + a) * kResRows + (int)rank * kBM + row;
@@ -701,7 +714,7 @@ __global__ void __launch_bounds__(kThreadsT, 1)
     if (lane == 0) {
       long long li = 0;
       for (long long x = x_begin; x < x_end; ++x, ++li) {
-        const int b = (int)(x % g.n_b);
+        const int b = tc_tile_b(x, (int)(x / g.n_b), g.n_b, total, G);
         const int xb = (int)(li % kXN);
         const long long use = li / kXN;
         if (use >= 1 && !mbar_wait(&bars[kTXEmpty + xb], (uint32_t)((use - 1) & 1), g.err,
