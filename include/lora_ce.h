@@ -50,8 +50,11 @@ extern "C" {
 typedef struct lora_ce_config {
     int32_t dim;        /* d: hidden size, multiple of 64, <= 640 (576) */
     int32_t vocab;      /* V: vocabulary size (49152) */
-    int32_t rank;       /* r: 1..64 (run at 4, 8, 16, 32 or 64 with zero
-                           padding, which leaves every result unchanged) */
+    int32_t rank;       /* r: 1..256, LORA_MAX_RANK (src/train.c:20).  Run
+                           at 4, 8, 16, 32, 64, 128 or 256 with zero
+                           padding, which leaves every result unchanged;
+                           ranks above 64 take a slower path that keeps the
+                           logit rows of a block of positions in HBM */
     float scale;        /* alpha / r (train_create: src/train.c:62-63) */
     float lr;           /* learning rate */
     float beta1;        /* 0.9   (ADAM_B1, src/train.c:23) */

@@ -20,6 +20,7 @@
 #include "lora_ce.h"
 #include "lora_ce_kernels.cuh"
 #include "lora_ce_tc.cuh"
+#include "lora_ce_wide.cuh"
 
 using namespace lce;
 
@@ -282,6 +283,16 @@ struct lora_ce_handle {
   __half* xt = nullptr;
   float* nml = nullptr;
   CUtensorMap mapW_strT{}, mapWa_strT{}, mapXv{};
+  // ranks 65..256 (kernel ranks 128, 256): position blocks of `wide_p`
+  // positions with materialised logit rows (lora_ce_wide.cuh)
+  bool wide = false;
+  int wide_p = 0;
+  float* w_sU = nullptr;     // [Tcap][R] s*U
+  float* w_Z = nullptr;      // [wide_p][Vpad] logits, then p - onehot
+  float* w_Bp = nullptr;     // [R][Vpad] B, plain
+  float* w_dB = nullptr;     // [R][Vpad] dB sums
+  float* w_dUp = nullptr;    // [kWMaxSplit][wide_p][R] split partials of dU
+  float* w_dAp = nullptr;    // [kWMaxSplit][d][R] split partials of dA
   ncclComm_t comm = nullptr;
   int nranks = 1, rank = 0;
   double comm_timeout_ms = 60000.0;  // bound on any wait that involves a collective
@@ -329,13 +340,20 @@ void free_all(lora_ce_handle* h) {
                   h->Gbuf,  h->gmean, h->p_max,    h->p_sum,  h->p_q,   h->z_tgt,
                   h->loss_tok, h->dU, h->gAp,      h->gBp,    h->norm_parts, h->err, h->corr_fx,
                   h->d_loss, h->in_H, h->in_tgt, h->w_aug, h->h_aug, h->Bc, h->tokc,
-                  h->xv, h->xt, h->nml};
+                  h->xv, h->xt, h->nml, h->w_sU, h->w_Z, h->w_Bp, h->w_dB, h->w_dUp,
+                  h->w_dAp};
   for (void* p : ptrs)
     if (p) cudaFree(p);
 }
 
 // The rank the kernels run at: the adapter's rank rounded up.
-int kernel_rank(int r) { return r <= 4 ? 4 : r <= 8 ? 8 : r <= 16 ? 16 : r <= 32 ? 32 : 64; }
+int kernel_rank(int r) {
+  return r <= 4 ? 4 : r <= 8 ? 8 : r <= 16 ? 16 : r <= 32 ? 32 : r <= 64 ? 64 : r <= 128 ? 128 : 256;
+}
+
+// Largest rank of the fused passes; ranks above it take the wide-rank path.
+constexpr int kMaxFusedRank = 64;
+constexpr int kMaxRank = 256;  // LORA_MAX_RANK (src/train.c:20)
 
 // The same decisions at run time, for sizing a handle's buffers.
 int aug_width_of(int R) {
@@ -348,8 +366,9 @@ int check_cfg(const lora_ce_config* c) {
   if (c->dim < 64 || c->dim % 64 != 0 || c->dim > 64 * kMaxKBlocks)
     return fail(LORA_CE_EINVAL, "dim must be a multiple of 64 in [64, 640]");
   if (c->vocab < 1) return fail(LORA_CE_EINVAL, "vocab must be positive");
-  if (c->rank < 1 || c->rank > 64) return fail(LORA_CE_EINVAL, "rank must be in [1, 64]");
-  if (c->dim / 64 + aug_width_of(kernel_rank(c->rank)) / 64 > kMaxKBlocks)
+  if (c->rank < 1 || c->rank > kMaxRank) return fail(LORA_CE_EINVAL, "rank must be in [1, 256]");
+  if (c->rank <= kMaxFusedRank &&
+      c->dim / 64 + aug_width_of(kernel_rank(c->rank)) / 64 > kMaxKBlocks)
     return fail(LORA_CE_EINVAL, "dim too large for this rank (resident K-blocks)");
   if (c->max_tokens < 1 || c->max_tokens > kMaxTokens)
     return fail(LORA_CE_EINVAL, "max_tokens must be in [1, 2^24]");
@@ -834,8 +853,117 @@ int run_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t*
   return 0;
 }
 
+// K splits of a split-K product whose output has `tiles` 128 x 128 tiles:
+// enough blocks for two per SM, each split a multiple of kWK long.
+void wide_splits(long long K, long long tiles, int num_sms, int* splits, int* k_split) {
+  long long s = (2LL * num_sms + tiles - 1) / tiles;
+  s = std::max(1LL, std::min<long long>(s, kWMaxSplit));
+  const long long ks = round_up((K + s - 1) / s, kWK);
+  *k_split = (int)ks;
+  *splits = (int)((K + ks - 1) / ks);
+}
+
+// The step for ranks 65..256 (kernel ranks 128 and 256), lora_ce_wide.cuh:
+// per block of wide_p positions the logit rows are materialised, turned
+// into p - onehot, and multiplied into dB and dU; dA follows over all
+// positions; G is packed in the fused path's layout, and the all-reduce,
+// clip and Adam are the fused path's kernels.
+int run_step_wide(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t* dtg,
+                  float* d_loss_out, int chunks, const cudaEvent_t* chunk_ready) {
+  cudaStream_t st = h->stream;
+  const int d = h->d, V = h->V, R = h->R;
+  const long long Vpad = h->Vpad;
+  const float scale = h->cfg.scale;
+  const int grid_ew = 8 * h->num_sms;  // grid-stride element-wise kernels
+  const unsigned rt = (unsigned)((R + kWTile - 1) / kWTile);
+  int launches = 0;
+  mark(h, kPhPrep);
+  for (int c = 0; chunk_ready && c < chunks; ++c)
+    LCE_CUDA(cudaStreamWaitEvent(st, chunk_ready[c], 0));
+  lw_convert<<<grid_ew, 256, 0, st>>>(dH, dtype, (long long)T * d, h->h16);
+  float* const Bt = h->params + (long long)d * R;
+  lw_b_plain<<<grid_ew, 256, 0, st>>>(Bt, R, V, Vpad, h->w_Bp);
+  LCE_CUDA(cudaMemsetAsync(h->w_dB, 0, (size_t)R * Vpad * 4, st));
+  launches += 2;
+  mark(h, kPhPass1);
+  const unsigned vt = (unsigned)((V + kWTile - 1) / kWTile);
+  for (int p0 = 0; p0 < T; p0 += h->wide_p) {
+    const int Pb = std::min(h->wide_p, T - p0);
+    const unsigned mt = (unsigned)((Pb + kWTile - 1) / kWTile);  // <= 4096: wide_p <= 2^19
+    float* const sU = h->w_sU + (long long)p0 * R;
+    // sU = s * (h16 . A)
+    lw_gemm<<<dim3(rt, mt, 1), kWThreads, 0, st>>>(
+        Pb, R, d, d, WideOp<__half, true>{h->h16 + (long long)p0 * d, d},
+        WideOp<float, false>{h->params, R}, WideStore{sU, R, scale});
+    // Z = h16 . W^T + sU . B
+    lw_gemm<<<dim3(vt, mt, 1), kWThreads, 0, st>>>(
+        Pb, V, d, d, WideOp<__half, true>{h->h16 + (long long)p0 * d, d},
+        WideOp<__half, true>{h->W, d}, WideStore{h->w_Z, Vpad, 1.0f});
+    lw_gemm<<<dim3(vt, mt, 1), kWThreads, 0, st>>>(Pb, V, R, R, WideOp<float, true>{sU, R},
+                                                   WideOp<float, false>{h->w_Bp, Vpad},
+                                                   WideAdd{h->w_Z, Vpad});
+    // loss per position; Z <- p - onehot
+    lw_softmax<<<Pb, kWSoftThreads, 0, st>>>(h->w_Z, Vpad, V, dtg, p0, h->loss_tok, h->err);
+    // dB += sU^T . Z
+    lw_gemm<<<dim3(vt, rt, 1), kWThreads, 0, st>>>(R, V, Pb, Pb, WideOp<float, false>{sU, R},
+                                                   WideOp<float, false>{h->w_Z, Vpad},
+                                                   WideAdd{h->w_dB, Vpad});
+    // dU = s * (Z . B^T), split over the vocabulary
+    int splits = 1, k_split = V;
+    wide_splits(V, (long long)mt * rt, h->num_sms, &splits, &k_split);
+    lw_gemm<<<dim3(rt, mt, (unsigned)splits), kWThreads, 0, st>>>(
+        Pb, R, V, k_split, WideOp<float, true>{h->w_Z, Vpad}, WideOp<float, true>{h->w_Bp, Vpad},
+        WideSplit{h->w_dUp, R, (long long)Pb * R});
+    lw_reduce_du<<<grid_ew, 256, 0, st>>>(Pb, R, splits, h->w_dUp, scale,
+                                          h->dU + (long long)p0 * R);
+    launches += 7;
+  }
+  mark(h, kPhCombine);
+  mark(h, kPhPass2);
+  mark(h, kPhDA);
+  // dA = h16^T . dU over all positions, split over positions
+  int a_splits = 1, a_k = T;
+  const unsigned dt = (unsigned)((d + kWTile - 1) / kWTile);
+  wide_splits(T, (long long)dt * rt, h->num_sms, &a_splits, &a_k);
+  lw_gemm<<<dim3(rt, dt, (unsigned)a_splits), kWThreads, 0, st>>>(
+      d, R, T, a_k, WideOp<__half, false>{h->h16, d}, WideOp<float, false>{h->dU, R},
+      WideSplit{h->w_dAp, R, (long long)d * R});
+  ++launches;
+  const long long nparam = (long long)d * R + Vpad * R;
+  const int32_t next_step = h->step + 1;
+  const AdamArgs aa = adam_args(h, nparam, next_step);
+  mark(h, kPhFinalize);
+  lw_pack<<<(int)std::min<long long>((nparam + 255) / 256, kFinBlocksMax), 256, 0, st>>>(
+      d, R, V, Vpad, T, a_splits, h->w_dAp, h->w_dB, h->loss_tok, h->Gbuf);
+  ++launches;
+  mark(h, kPhAllReduce);
+  if (h->comm) {
+    ncclResult_t r = nccl().AllReduce(h->Gbuf, h->Gbuf, (size_t)(nparam + 2), ncclFloat, ncclSum,
+                                      h->comm, st);
+    if (r == ncclInProgress) r = nccl_settle(h->comm, h->comm_timeout_ms);
+    if (r != ncclSuccess)
+      return fail(LORA_CE_ENCCL, std::string("ncclAllReduce: ") + nccl_str(r));
+  }
+  mark(h, kPhNorm);
+  if (aa.clip > 0.f) {
+    lce_sqnorm<<<256, 256, 0, st>>>(nparam, h->Gbuf, h->norm_parts);
+    ++launches;
+  }
+  mark(h, kPhAdam);
+  lce_adam<<<(int)std::min<long long>((nparam + 255) / 256, 8LL * h->num_sms), 256, 0, st>>>(
+      aa, h->params, h->mom1, h->mom2, h->Gbuf, h->gmean, h->norm_parts, d_loss_out);
+  ++launches;
+  mark(h, kNumPhases);
+  LCE_CUDA(cudaGetLastError());
+  h->step = next_step;
+  h->launches = launches;
+  h->last_T = T;
+  return 0;
+}
+
 int dispatch_step(lora_ce_handle* h, const void* dH, int dtype, int T, const int32_t* dtg,
                   float* d_loss, int chunks = 1, const cudaEvent_t* chunk_ready = nullptr) {
+  if (h->wide) return run_step_wide(h, dH, dtype, T, dtg, d_loss, chunks, chunk_ready);
   switch (h->R) {
     case 4: return run_step<4>(h, dH, dtype, T, dtg, d_loss, chunks, chunk_ready);
     case 8: return run_step<8>(h, dH, dtype, T, dtg, d_loss, chunks, chunk_ready);
@@ -1090,6 +1218,56 @@ int run_or_replay(lora_ce_handle* h, bool host, const void* H, int dtype, int T,
 
 }  // namespace
 
+namespace {
+
+// Buffers and streams of a wide-rank handle (ranks 65..256).  The logit
+// rows of one position block take at most 512 MB.
+int create_wide(lora_ce_handle* h) {
+  h->wide = true;
+  h->tc = false;
+  h->units1 = h->units2 = 1;
+  const int R = h->R, d = h->d;
+  const long long V = h->V, Vpad = h->Vpad, Tcap = h->Tcap;
+  const long long rows = (512LL << 20) / (Vpad * 4) / kWTile * kWTile;
+  h->wide_p = (int)std::max<long long>(kWTile, std::min<long long>(rows, Tcap));
+  const long long P = h->wide_p;
+  const long long nparam = (long long)d * R + Vpad * R;
+  int rc = 0;
+  if (!rc) rc = dalloc(&h->W, (size_t)V * d);
+  if (!rc) rc = dalloc(&h->h16, (size_t)Tcap * d);
+  if (!rc) rc = dalloc(&h->params, (size_t)nparam);
+  if (!rc) rc = dalloc(&h->mom1, (size_t)nparam);
+  if (!rc) rc = dalloc(&h->mom2, (size_t)nparam);
+  if (!rc) rc = dalloc(&h->Gbuf, (size_t)nparam + 2);
+  if (!rc) rc = dalloc(&h->gmean, (size_t)nparam);
+  if (!rc) rc = dalloc(&h->loss_tok, (size_t)Tcap);
+  if (!rc) rc = dalloc(&h->dU, (size_t)Tcap * R);
+  if (!rc) rc = dalloc(&h->norm_parts, kFinBlocksMax);
+  if (!rc) rc = dalloc(&h->err, 1);
+  if (!rc) rc = dalloc(&h->d_loss, 2);
+  if (!rc) rc = dalloc(reinterpret_cast<char**>(&h->in_H), (size_t)Tcap * d * 4);
+  if (!rc) rc = dalloc(&h->in_tgt, (size_t)Tcap);
+  if (!rc) rc = dalloc(&h->w_sU, (size_t)Tcap * R);
+  if (!rc) rc = dalloc(&h->w_Z, (size_t)P * Vpad);
+  if (!rc) rc = dalloc(&h->w_Bp, (size_t)R * Vpad);
+  if (!rc) rc = dalloc(&h->w_dB, (size_t)R * Vpad);
+  if (!rc) rc = dalloc(&h->w_dUp, (size_t)kWMaxSplit * P * R);
+  if (!rc) rc = dalloc(&h->w_dAp, (size_t)kWMaxSplit * d * R);
+  if (!rc && (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess ||
+              cudaStreamCreateWithFlags(&h->cstream, cudaStreamNonBlocking) != cudaSuccess))
+    rc = fail(LORA_CE_ECUDA, "cudaStreamCreate failed");
+  if (!rc && cudaMallocHost(reinterpret_cast<void**>(&h->res_host), 16) != cudaSuccess)
+    rc = fail(LORA_CE_ENOMEM, "cudaMallocHost failed");
+  if (!rc && cudaEventCreateWithFlags(&h->ev_start, cudaEventDisableTiming) != cudaSuccess)
+    rc = fail(LORA_CE_ECUDA, "cudaEventCreate failed");
+  for (int c = 0; c < kMaxChunks && !rc; ++c)
+    if (cudaEventCreateWithFlags(&h->ev_chunk[c], cudaEventDisableTiming) != cudaSuccess)
+      rc = fail(LORA_CE_ECUDA, "cudaEventCreate failed");
+  return rc;
+}
+
+}  // namespace
+
 extern "C" {
 
 void lora_ce_default_config(lora_ce_config* c, int32_t dim, int32_t vocab, int32_t rank,
@@ -1143,6 +1321,17 @@ int lora_ce_create(const lora_ce_config* cfg, lora_ce_handle** out) {
     const char* tc = getenv("LORA_CE_TC");
     const int tc_min = tc && tc[0] == '1' ? 8 : LCE_TC_MIN_RANK;
     h->tc = h->pair == 2 && h->R >= tc_min && !(tc && tc[0] == '0');
+  }
+  if (h->R > kMaxFusedRank) {
+    rc = create_wide(h);
+    if (rc) {
+      free_all(h);
+      free_streams(h);
+      delete h;
+      return rc;
+    }
+    *out = h;
+    return 0;
   }
   const int R = h->R, d = h->d;
   const int res_rows = kBM * h->pair;

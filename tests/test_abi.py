@@ -37,7 +37,7 @@ def test_default_config_is_reference_defaults():
     assert cfg.weight_decay == 0.0 and cfg.clip_norm == 0.0
 
 
-@pytest.mark.parametrize("field,value", [("dim", 100), ("rank", 65), ("rank", 0), ("max_tokens", 0),
+@pytest.mark.parametrize("field,value", [("dim", 100), ("rank", 257), ("rank", 0), ("max_tokens", 0),
                                          ("vocab", 0), ("beta1", 1.0)])
 def test_create_rejects_bad_config(field, value):
     cfg = lora_ce.default_config(576, 49152, 4, 256)

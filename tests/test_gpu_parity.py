@@ -84,6 +84,10 @@ def run_case(oracle, V, d, r, T, seed, dtype="bf16", steps=1, scale=2.0, lr=1e-3
         (3000, 192, 20, 77, "f16"),     # padded to 32
         (2048, 576, 40, 260, "bf16"),   # padded to 64
         (49152, 576, 64, 300, "bf16"),  # rank 64 at full vocabulary (11 resident K-blocks)
+        (49152, 576, 100, 300, "bf16"),  # wide-rank path (kernel rank 128)
+        (3000, 192, 65, 77, "f16"),
+        (4099, 128, 256, 129, "f32"),  # LORA_MAX_RANK, vocabulary and positions off the tiles
+        (49152, 576, 256, 1, "bf16"),
     ],
 )
 def test_step_matches_oracle(oracle, V, d, r, T, dtype):
@@ -113,6 +117,14 @@ def test_step_matches_oracle_both_rank_paths(oracle, monkeypatch, tc, V, d, r, T
 def test_adamw_and_clip_extensions(oracle):
     run_case(oracle, 49152, 576, 4, 300, seed=77, wd=0.01, clip=1.0, steps=2)
     run_case(oracle, 3000, 128, 4, 50, seed=78, wd=0.01, clip=1e-4, steps=1)  # clip active
+
+
+def test_wide_rank_adamw_clip_and_position_blocks(oracle):
+    """Ranks above 64 (the wide-rank path): AdamW with an active clip, and a
+    vocabulary large enough that 3000 positions run as three position
+    blocks (512 MB of logit rows hold 1280 positions at V = 100,000)."""
+    run_case(oracle, 3000, 128, 128, 200, seed=91, wd=0.01, clip=1e-4, steps=2)
+    run_case(oracle, 100000, 64, 72, 3000, seed=92, steps=1)
 
 
 def test_adam_state_carries_over_steps(oracle):
