@@ -118,7 +118,8 @@ def _gpu_rank(rank, world, uid_path, out, r):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("r", [4, 64])  # rank 64: the tensor-core rank-sum passes
+# rank 64: the tensor-core rank-sum passes; rank 100: the wide-rank path (kernel rank 128)
+@pytest.mark.parametrize("r", [4, 64, 100])
 def test_two_gpus_match_oracle(oracle, tmp_path, r):
     import torch
     if torch.cuda.device_count() < 2:

@@ -121,14 +121,15 @@ def _read_adapter(path, d, V, r):
 
 
 @pytest.mark.gpu
-def test_train_step_matches_oracle(env, oracle, tmp_path):
-    d, V, r, n = 576, 49152, 4, 256
+@pytest.mark.parametrize("r", [4, 128])  # 128: the wide-rank path (ranks above 64)
+def test_train_step_matches_oracle(env, oracle, tmp_path, r):
+    d, V, n = 576, 49152, 256
     W = wl.make_weight(31, V, d)
     h, tgt, _, _ = wl.make_step_inputs(31, n - 1, V, d, r)
     H = np.ascontiguousarray(wl.oracle_hidden(h))
     tokens = np.concatenate([[7], tgt]).astype(np.int32)
     f = env.forward(H, V)
-    t = env.lib.train_create(f, sf.params(rank=r, alpha=8, seq_max=n, lr=1e-3, seed=42))
+    t = env.lib.train_create(f, sf.params(rank=r, alpha=2 * r, seq_max=n, lr=1e-3, seed=42))
     assert t
     assert env.lib.train_step(t, tokens.ctypes.data, n) == -1.0  # no lm_head yet
     assert env.lib.lora_train_set_lm_head(t, W.ctypes.data) == 0
