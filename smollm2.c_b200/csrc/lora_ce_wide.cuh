@@ -114,7 +114,8 @@ __device__ __forceinline__ void wide_stash(const float (&reg)[8], int tid,
 // split z covers k in [z*k_split, (z+1)*k_split).  Two shared-memory
 // stages: the next stage is read into registers while the current one is
 // multiplied, and written to the other stage after it (one barrier per
-// stage).
+// stage).  The multiply-adds run two columns per f32x2 instruction, each
+// lane of it an ordinary fp32 fma.
 template <class OA, class OB, class Ep>
 __global__ void __launch_bounds__(kWThreads, 2) lw_gemm(int M, int N, int K, int k_split, OA oa,
                                                      OB ob, Ep ep) {
@@ -125,11 +126,11 @@ __global__ void __launch_bounds__(kWThreads, 2) lw_gemm(int M, int N, int K, int
   const int m0 = blockIdx.y * kWTile, n0 = blockIdx.x * kWTile;
   const int k_lo = blockIdx.z * k_split;
   const int k_hi = min(K, k_lo + k_split);
-  float acc[8][8];
+  float2 acc[8][4];  // [row][column pair]
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    for (int j = 0; j < 4; ++j) acc[i][j] = make_float2(0.f, 0.f);
   if (k_lo < k_hi) {
     float ra[8], rb[8];
     wide_fetch(oa, m0, M, k_lo, k_hi, tid, ra);
@@ -154,9 +155,12 @@ __global__ void __launch_bounds__(kWThreads, 2) lw_gemm(int M, int N, int K, int
         *reinterpret_cast<float4*>(&b[4]) =
             *reinterpret_cast<const float4*>(&sb[buf][k][64 + tx * 4]);
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < 8; ++i) {
+          const float2 ai = make_float2(a[i], a[i]);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+          for (int j = 0; j < 4; ++j)
+            acc[i][j] = __ffma2_rn(ai, make_float2(b[2 * j], b[2 * j + 1]), acc[i][j]);
+        }
       }
       if (more) {
         wide_stash<OA>(ra, tid, sa[buf ^ 1]);
@@ -173,7 +177,7 @@ __global__ void __launch_bounds__(kWThreads, 2) lw_gemm(int M, int N, int K, int
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int n = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + j - 4);
-      if (n < N) ep(m, n, (int)blockIdx.z, acc[i][j]);
+      if (n < N) ep(m, n, (int)blockIdx.z, (j & 1) ? acc[i][j >> 1].y : acc[i][j >> 1].x);
     }
   }
 }
