@@ -49,7 +49,6 @@ int bfail(int code, const std::string& msg) {
 
 constexpr int kHd = 64;          // head dimension (the reference's attention rows)
 constexpr int kMaxSeqBody = 4096;
-constexpr int kAttnWarps = 4;
 
 // ------------------------------------------------------------------ kernels
 
@@ -334,104 +333,173 @@ __global__ void bd_rope(float* __restrict__ qkv, int T, int ld, int n_rot_heads,
   }
 }
 
-// Causal GQA attention in the reference's order (src/forward.c:1186-1229):
-// one warp per (position, head).  Scores q.k / 8 (each lane one key, the
-// 64-term sum in index order), max, e = e^(s - max), the sum of e in key
-// order (lane 0), then out[i] = sum over keys of (e * (1/sum)) * v[i] in key
-// order (lanes over i).  Keys from seq_start + s_start(window) to t.  The
-// loads are vectorised and the key loops unrolled so that they are in
-// flight ahead of the ordered additions.
-__global__ void __launch_bounds__(32 * kAttnWarps)
-    bd_attn(const float* __restrict__ qkv, int T, int ld, int nh, int nkv, int dim,
-            const int32_t* __restrict__ pos, int window, float* __restrict__ out, int max_seq) {
-  extern __shared__ float sc_all[];
+// Causal GQA attention in the reference's order (src/forward.c:1186-1229),
+// one warp per (position, query head) item: scores q.k / 8 (each lane one
+// key, the 64-term sum in index order), max, e = e^(s - max), the sum of e
+// in key order (lane 0), then out[i] = sum over keys of (e * (1/sum)) * v[i]
+// in key order (lanes over i).  Keys from seq_start + s_start(window) to t.
+// One block per (tile of kAttnTile positions, KV head) first copies that
+// head's K and V rows for the tile's key range into shared memory (rows
+// padded to kAttnRowF floats, so the lanes' row-strided float4 reads fall in
+// different banks): every key row is read from global memory once per
+// block instead of once per item.  A block whose key range has more rows
+// than `stage_cap` reads them from global memory.  The loads are vectorised
+// and the key loops unrolled so that they are in flight ahead of the ordered
+// additions.
+constexpr int kAttnTile = 8;
+constexpr int kAttnTWarps = 12;
+constexpr int kAttnRowF = kHd + 4;
+// dynamic shared memory of bd_attn_tile: the warps' score rows, then the
+// staged K and V rows
+inline size_t attn_tile_smem(int max_seq, int stage_cap) {
+  return (size_t)kAttnTWarps * max_seq * 4 + 2 * (size_t)stage_cap * kAttnRowF * 4;
+}
+__global__ void __launch_bounds__(32 * kAttnTWarps)
+    bd_attn_tile(const float* __restrict__ qkv, int T, int ld, int nh, int nkv, int dim,
+                 const int32_t* __restrict__ pos, int window, float* __restrict__ out, int max_seq,
+                 int stage_cap) {
+  extern __shared__ __align__(16) float att_smem[];
+  __shared__ int s_lo;
   const int wib = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const long long item = (long long)blockIdx.x * kAttnWarps + wib;
-  if (item >= (long long)T * nh) return;
-  const int t = (int)(item / nh), h = (int)(item % nh);
+  const int t0 = blockIdx.x * kAttnTile;
+  const int t1 = min(T, t0 + kAttnTile);
+  const int kvh = blockIdx.y;
+  const int gsz = nh / nkv;  // query heads of this KV head: h * nkv / nh == kvh
+  auto first_key = [&](int t) {
+    const int p = pos[t];
+    int lo = 0;
+    if (window > 0) {
+      lo = p + 1 - window;
+      if (lo < 0) lo = 0;
+      if (lo > p) lo = p;
+    }
+    return t - p + lo;
+  };
+  if (threadIdx.x == 0) {
+    int m = t0;
+    for (int t = t0; t < t1; ++t) m = min(m, first_key(t));
+    s_lo = m;
+  }
+  __syncthreads();
+  const int kv_lo = s_lo;
+  const int n_rows = t1 - kv_lo;
+  const bool staged = n_rows <= stage_cap;
+  float* sc_all = att_smem;                        // [kAttnTWarps][max_seq] scores
+  float* sK = att_smem + (size_t)kAttnTWarps * max_seq;
+  float* sV = sK + (size_t)stage_cap * kAttnRowF;
+  const float* gK = qkv + dim + kvh * kHd;
+  const float* gV = qkv + dim + nkv * kHd + kvh * kHd;
+  if (staged) {
+    // 16 float4 per row; each thread moves up to 8 (row, float4) slices of
+    // K and V per round, all loads of a round in flight before its stores
+    constexpr int kQ = kHd / 4, kU = 8;
+    const int n4 = n_rows * kQ;
+    for (int k0 = 0; k0 < n4; k0 += kU * (int)blockDim.x) {
+      float4 kv4[kU], vv4[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int k = k0 + u * (int)blockDim.x + (int)threadIdx.x;
+        if (k < n4) {
+          const size_t go = (size_t)(kv_lo + k / kQ) * ld;
+          kv4[u] = __ldg(reinterpret_cast<const float4*>(gK + go) + k % kQ);
+          vv4[u] = __ldg(reinterpret_cast<const float4*>(gV + go) + k % kQ);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int k = k0 + u * (int)blockDim.x + (int)threadIdx.x;
+        if (k < n4) {
+          const size_t so = (size_t)(k / kQ) * kAttnRowF + 4 * (k % kQ);
+          *reinterpret_cast<float4*>(sK + so) = kv4[u];
+          *reinterpret_cast<float4*>(sV + so) = vv4[u];
+        }
+      }
+    }
+  }
+  __syncthreads();
+  // row r of K / V: base + (r - row0) * stride
+  const float* kb = staged ? sK : gK;
+  const float* vb = staged ? sV : gV;
+  const long long kst = staged ? kAttnRowF : ld;
+  const int row0 = staged ? kv_lo : 0;
   float* sc = sc_all + (size_t)wib * max_seq;
-  const int kvh = h * nkv / nh;
-  const int p = pos[t];
-  int lo = 0;
-  if (window > 0) {
-    lo = p + 1 - window;
-    if (lo < 0) lo = 0;
-    if (lo > p) lo = p;
-  }
-  const int first = t - p + lo;  // global index of the first key
-  const int n_keys = p - lo + 1;
-  float qv[kHd];
-  {
-    const float4* q4 = reinterpret_cast<const float4*>(qkv + (size_t)t * ld + h * kHd);
+  const int n_items = (t1 - t0) * gsz;
+  for (int it = wib; it < n_items; it += kAttnTWarps) {
+    const int t = t0 + it / gsz, h = kvh * gsz + it % gsz;
+    const int first = first_key(t);
+    const int n_keys = t - first + 1;
+    float qv[kHd];
+    {
+      const float4* q4 = reinterpret_cast<const float4*>(qkv + (size_t)t * ld + h * kHd);
 #pragma unroll
-    for (int i = 0; i < kHd / 4; ++i) {
-      const float4 v = __ldg(q4 + i);
-      qv[4 * i] = v.x; qv[4 * i + 1] = v.y; qv[4 * i + 2] = v.z; qv[4 * i + 3] = v.w;
+      for (int i = 0; i < kHd / 4; ++i) {
+        const float4 v = __ldg(q4 + i);
+        qv[4 * i] = v.x; qv[4 * i + 1] = v.y; qv[4 * i + 2] = v.z; qv[4 * i + 3] = v.w;
+      }
     }
-  }
-  const float* kbase = qkv + dim + kvh * kHd;
-  const float* vbase = qkv + dim + nkv * kHd + kvh * kHd;
-  float mx = -INFINITY;
-  for (int j = lane; j < n_keys; j += 32) {
-    const float4* k4 = reinterpret_cast<const float4*>(kbase + (size_t)(first + j) * ld);
-    float kv[kHd];
+    float mx = -INFINITY;
+    for (int j = lane; j < n_keys; j += 32) {
+      const float4* k4 = reinterpret_cast<const float4*>(kb + (long long)(first + j - row0) * kst);
+      float kv[kHd];
 #pragma unroll
-    for (int i = 0; i < kHd / 4; ++i) {
-      const float4 v = __ldg(k4 + i);
-      kv[4 * i] = v.x; kv[4 * i + 1] = v.y; kv[4 * i + 2] = v.z; kv[4 * i + 3] = v.w;
+      for (int i = 0; i < kHd / 4; ++i) {
+        const float4 v = k4[i];
+        kv[4 * i] = v.x; kv[4 * i + 1] = v.y; kv[4 * i + 2] = v.z; kv[4 * i + 3] = v.w;
+      }
+      float dd = 0.f;
+#pragma unroll
+      for (int i = 0; i < kHd; ++i) dd = __fadd_rn(dd, __fmul_rn(qv[i], kv[i]));
+      dd = __fmul_rn(dd, 0.125f);  // 1 / sqrtf(64)
+      sc[j] = dd;
+      mx = fmaxf(mx, dd);
     }
-    float d = 0.f;
-#pragma unroll
-    for (int i = 0; i < kHd; ++i) d = __fadd_rn(d, __fmul_rn(qv[i], kv[i]));
-    d = __fmul_rn(d, 0.125f);  // 1 / sqrtf(64)
-    sc[j] = d;
-    mx = fmaxf(mx, d);
-  }
-  mx = warp_max(mx);
-  __syncwarp();
-  for (int j = lane; j < n_keys; j += 32) sc[j] = exp_ref(__fsub_rn(sc[j], mx));
-  __syncwarp();
-  float sum = 0.f;
-  if (lane == 0) {
+    mx = warp_max(mx);
+    __syncwarp();
+    for (int j = lane; j < n_keys; j += 32) sc[j] = exp_ref(__fsub_rn(sc[j], mx));
+    __syncwarp();
+    float sum = 0.f;
+    if (lane == 0) {
+      int j = 0;
+      for (; j + 8 <= n_keys; j += 8) {
+        const float e0 = sc[j], e1 = sc[j + 1], e2 = sc[j + 2], e3 = sc[j + 3];
+        const float e4 = sc[j + 4], e5 = sc[j + 5], e6 = sc[j + 6], e7 = sc[j + 7];
+        sum = __fadd_rn(sum, e0); sum = __fadd_rn(sum, e1); sum = __fadd_rn(sum, e2);
+        sum = __fadd_rn(sum, e3); sum = __fadd_rn(sum, e4); sum = __fadd_rn(sum, e5);
+        sum = __fadd_rn(sum, e6); sum = __fadd_rn(sum, e7);
+      }
+      for (; j < n_keys; ++j) sum = __fadd_rn(sum, sc[j]);
+    }
+    sum = __shfl_sync(0xffffffffu, sum, 0);
+    const float inv_sum = sum > 0.f ? __fdiv_rn(1.0f, sum) : 0.f;
+    float o0 = 0.f, o1 = 0.f;
     int j = 0;
     for (; j + 8 <= n_keys; j += 8) {
-      const float e0 = sc[j], e1 = sc[j + 1], e2 = sc[j + 2], e3 = sc[j + 3];
-      const float e4 = sc[j + 4], e5 = sc[j + 5], e6 = sc[j + 6], e7 = sc[j + 7];
-      sum = __fadd_rn(sum, e0); sum = __fadd_rn(sum, e1); sum = __fadd_rn(sum, e2);
-      sum = __fadd_rn(sum, e3); sum = __fadd_rn(sum, e4); sum = __fadd_rn(sum, e5);
-      sum = __fadd_rn(sum, e6); sum = __fadd_rn(sum, e7);
-    }
-    for (; j < n_keys; ++j) sum = __fadd_rn(sum, sc[j]);
-  }
-  sum = __shfl_sync(0xffffffffu, sum, 0);
-  const float inv_sum = sum > 0.f ? __fdiv_rn(1.0f, sum) : 0.f;
-  float o0 = 0.f, o1 = 0.f;
-  int j = 0;
-  for (; j + 8 <= n_keys; j += 8) {
-    float va[8], vb[8], wg[8];
+      float va[8], vb2[8], wg[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const float* vr = vbase + (size_t)(first + j + u) * ld;
-      va[u] = __ldg(vr + lane);
-      vb[u] = __ldg(vr + lane + 32);
-      wg[u] = __fmul_rn(sc[j + u], inv_sum);
-    }
+      for (int u = 0; u < 8; ++u) {
+        const float* vr = vb + (long long)(first + j + u - row0) * kst;
+        va[u] = vr[lane];
+        vb2[u] = vr[lane + 32];
+        wg[u] = __fmul_rn(sc[j + u], inv_sum);
+      }
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      o0 = __fadd_rn(o0, __fmul_rn(wg[u], va[u]));
-      o1 = __fadd_rn(o1, __fmul_rn(wg[u], vb[u]));
+      for (int u = 0; u < 8; ++u) {
+        o0 = __fadd_rn(o0, __fmul_rn(wg[u], va[u]));
+        o1 = __fadd_rn(o1, __fmul_rn(wg[u], vb2[u]));
+      }
     }
+    for (; j < n_keys; ++j) {
+      const float wgt = __fmul_rn(sc[j], inv_sum);
+      const float* vr = vb + (long long)(first + j - row0) * kst;
+      o0 = __fadd_rn(o0, __fmul_rn(wgt, vr[lane]));
+      o1 = __fadd_rn(o1, __fmul_rn(wgt, vr[lane + 32]));
+    }
+    float* orow = out + (size_t)t * dim + h * kHd;
+    orow[lane] = o0;
+    orow[lane + 32] = o1;
+    __syncwarp();  // sc is reused by this warp's next item
   }
-  for (; j < n_keys; ++j) {
-    const float wgt = __fmul_rn(sc[j], inv_sum);
-    const float* vr = vbase + (size_t)(first + j) * ld;
-    o0 = __fadd_rn(o0, __fmul_rn(wgt, vr[lane]));
-    o1 = __fadd_rn(o1, __fmul_rn(wgt, vr[lane + 32]));
-  }
-  float* orow = out + (size_t)t * dim + h * kHd;
-  orow[lane] = o0;
-  orow[lane + 32] = o1;
 }
 
 }  // namespace
@@ -439,6 +507,7 @@ __global__ void __launch_bounds__(32 * kAttnWarps)
 struct lora_body_handle {
   lora_body_config cfg{};
   int d = 0, ffn = 0, kvdim = 0, nqkv = 0, Tcap = 0;
+  int attn_cap = 0;  // K / V rows bd_attn_tile stages per block
   cudaStream_t stream = nullptr;
   // weights (int8 per-row) and scales, per layer
   struct Layer {
@@ -553,8 +622,8 @@ int enqueue_body(lora_body_handle* h, const int32_t* d_tok, int T, void* out, in
   const dim3 g_d((d + kGemmTN - 1) / kGemmTN, tm);
   const dim3 g_gu((2 * ffn + kGemmTN - 1) / kGemmTN, tm);
   const int max_seq = h->cfg.max_seq;
-  const size_t attn_smem = (size_t)kAttnWarps * max_seq * 4;
-  const long long att_items = (long long)T * nh;
+  const size_t attn_smem = attn_tile_smem(max_seq, h->attn_cap);
+  const dim3 g_att((unsigned)((T + kAttnTile - 1) / kAttnTile), (unsigned)nkv);
   const int rope_blocks = (int)std::min<long long>(((long long)T * (nh + nkv) * 32 + 255) / 256, 8192);
   for (int L = 0; L < h->cfg.n_layers; ++L) {
     const auto& ly = h->layers[L];
@@ -564,8 +633,8 @@ int enqueue_body(lora_body_handle* h, const int32_t* d_tok, int T, void* out, in
                                       h->nqkv, 0);
     bd_rope<<<rope_blocks, 256, 0, st>>>(h->qkv, T, h->nqkv, nh + nkv, h->pos, h->rope_cos,
                                          h->rope_sin);
-    bd_attn<<<(unsigned)((att_items + kAttnWarps - 1) / kAttnWarps), 32 * kAttnWarps, attn_smem,
-              st>>>(h->qkv, T, h->nqkv, nh, nkv, d, h->pos, ly.window, h->att, max_seq);
+    bd_attn_tile<<<g_att, 32 * kAttnTWarps, attn_smem, st>>>(
+        h->qkv, T, h->nqkv, nh, nkv, d, h->pos, ly.window, h->att, max_seq, h->attn_cap);
     bd_quant_act<<<rows_blocks, 256, 0, st>>>(h->att, T, d, h->xq, h->xs);
     bd_gemm_q8<<<g_d, 128, 0, st>>>(h->xq, h->xs, T, d, ly.wo, ly.so, d, h->x, d, 1);
     bd_norm<<<norm_blocks, 32 * kNormWarps, norm_smem, st>>>(h->x, ly.ffn_norm, T, d, h->cfg.rms_eps, h->xn, h->xq,
@@ -706,9 +775,17 @@ int lora_body_create(const lora_body_config* c, lora_body_handle** out) {
     rc = bfail(LORA_CE_ENOMEM, "cudaMallocHost failed");
   }
   if (!rc && cudaMemset(h->err, 0, 4) != cudaSuccess) rc = bfail(LORA_CE_ECUDA, "cudaMemset failed");
-  if (!rc && cudaFuncSetAttribute(bd_attn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)(kAttnWarps * c->max_seq * 4)) != cudaSuccess)
-    rc = bfail(LORA_CE_ECUDA, "attention shared memory");
+  if (!rc) {
+    // stage a whole tile's key range up to a 200 KB block (the usual case:
+    // max_seq 256 needs 263 rows, 143 KB); longer ranges read global memory
+    const long long want = kAttnTile + (long long)c->max_seq - 1;
+    const long long fit =
+        (200LL * 1024 - (long long)kAttnTWarps * c->max_seq * 4) / (2LL * kAttnRowF * 4);
+    h->attn_cap = (int)std::max<long long>(0, std::min(want, fit));
+    if (cudaFuncSetAttribute(bd_attn_tile, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)attn_tile_smem(c->max_seq, h->attn_cap)) != cudaSuccess)
+      rc = bfail(LORA_CE_ECUDA, "attention shared memory");
+  }
   if (!rc && cudaFuncSetAttribute(bd_norm, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)(kNormWarps * c->dim * sizeof(double))) != cudaSuccess)
     rc = bfail(LORA_CE_ECUDA, "norm shared memory");
