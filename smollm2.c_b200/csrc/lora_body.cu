@@ -233,30 +233,34 @@ __global__ void __launch_bounds__(256) bd_act_quant(const float* __restrict__ gu
 // Y[t][n] (+)= (float)(sum_k X[t][k] * W[n][k]) * xs[t] * ws[n]: the
 // reference's matmul_q8_dot_perrow (src/forward.c:470-511, int32 sums, two
 // rounded multiplies), with `accumulate` adding it to Y as the residual
-// add does.  Tiles of 32 positions x 64 outputs (small position counts still
-// spread over the SMs), 128 threads of 4 x 4 outputs, K in 64-byte steps
-// (K % 64 == 0) with the next step's tile loaded into registers while the
-// current one is multiplied (dp4a; the int32 sums are exact in any order).
-constexpr int kGemmTM = 32, kGemmTN = 64;
+// add does.  Tiles of 8*MR positions x 64 outputs (MR = 4 for the wide
+// gate/up GEMM, 2 for the narrower ones, whose 32-position tiles left SMs
+// idle), 128 threads of MR x 4 outputs, K in 64-byte steps (K % 64 == 0)
+// with the next step's tile loaded into registers while the current one is
+// multiplied (dp4a; the int32 sums are exact in any order, so the tiling
+// does not change any result).
+constexpr int kGemmTN = 64;
+template <int MR>
 __global__ void __launch_bounds__(128) bd_gemm_q8(const int8_t* __restrict__ X,
                                                   const float* __restrict__ xs, int T, int K,
                                                   const int8_t* __restrict__ W,
                                                   const float* __restrict__ ws, int N,
                                                   float* __restrict__ Y, int ldy, int accumulate) {
-  __shared__ int sX[kGemmTM][17];
+  constexpr int TM = 8 * MR;
+  __shared__ int sX[TM][17];
   __shared__ int sW[kGemmTN][17];
-  const int t0 = blockIdx.y * kGemmTM, n0 = blockIdx.x * kGemmTN;
+  const int t0 = blockIdx.y * TM, n0 = blockIdx.x * kGemmTN;
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // 16 x 8 threads
-  int acc[4][4];
+  int acc[MR][4];
 #pragma unroll
-  for (int m = 0; m < 4; ++m)
+  for (int m = 0; m < MR; ++m)
 #pragma unroll
     for (int n = 0; n < 4; ++n) acc[m][n] = 0;
-  // this thread's share of a K-step: 4 words of X, 8 of W
-  int rx[4], rw[8];
+  // this thread's share of a K-step: MR words of X, 8 of W
+  int rx[MR], rw[8];
   auto load = [&](int k0) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < MR; ++u) {
       const int i = threadIdx.x + 128 * u, r = i >> 4, c = i & 15;
       const int tr = t0 + r;
       rx[u] = tr < T ? __ldg(reinterpret_cast<const int*>(X + (size_t)tr * K + k0 + 4 * c)) : 0;
@@ -271,7 +275,7 @@ __global__ void __launch_bounds__(128) bd_gemm_q8(const int8_t* __restrict__ X,
   load(0);
   for (int k0 = 0; k0 < K; k0 += 64) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < MR; ++u) {
       const int i = threadIdx.x + 128 * u;
       sX[i >> 4][i & 15] = rx[u];
     }
@@ -284,21 +288,21 @@ __global__ void __launch_bounds__(128) bd_gemm_q8(const int8_t* __restrict__ X,
     if (k0 + 64 < K) load(k0 + 64);
 #pragma unroll
     for (int c = 0; c < 16; ++c) {
-      int av[4], bv[4];
+      int av[MR], bv[4];
 #pragma unroll
-      for (int m = 0; m < 4; ++m) av[m] = sX[ty * 4 + m][c];
+      for (int m = 0; m < MR; ++m) av[m] = sX[ty * MR + m][c];
 #pragma unroll
       for (int n = 0; n < 4; ++n) bv[n] = sW[tx * 4 + n][c];
 #pragma unroll
-      for (int m = 0; m < 4; ++m)
+      for (int m = 0; m < MR; ++m)
 #pragma unroll
         for (int n = 0; n < 4; ++n) acc[m][n] = __dp4a(av[m], bv[n], acc[m][n]);
     }
     __syncthreads();
   }
 #pragma unroll
-  for (int m = 0; m < 4; ++m) {
-    const int t = t0 + ty * 4 + m;
+  for (int m = 0; m < MR; ++m) {
+    const int t = t0 + ty * MR + m;
     if (t >= T) continue;
     const float sx = xs[t];
 #pragma unroll
@@ -508,6 +512,7 @@ struct lora_body_handle {
   lora_body_config cfg{};
   int d = 0, ffn = 0, kvdim = 0, nqkv = 0, Tcap = 0;
   int attn_cap = 0;  // K / V rows bd_attn_tile stages per block
+  int num_sms = 0;
   cudaStream_t stream = nullptr;
   // weights (int8 per-row) and scales, per layer
   struct Layer {
@@ -617,10 +622,17 @@ int enqueue_body(lora_body_handle* h, const int32_t* d_tok, int T, void* out, in
   const int rows_blocks = (T * 32 + 255) / 256;  // one warp per row, 8 per block
   const int norm_blocks = (T + kNormWarps - 1) / kNormWarps;
   const size_t norm_smem = (size_t)kNormWarps * d * sizeof(double);
-  const int tm = (T + kGemmTM - 1) / kGemmTM;
-  const dim3 g_qkv((h->nqkv + kGemmTN - 1) / kGemmTN, tm);
-  const dim3 g_d((d + kGemmTN - 1) / kGemmTN, tm);
-  const dim3 g_gu((2 * ffn + kGemmTN - 1) / kGemmTN, tm);
+  // int8 GEMM Y (+)= X . W^T over N outputs: tiles of 32 positions, or of
+  // 16 where 32-position tiles would leave SMs without a block
+  auto gemm = [&](const int8_t* W, const float* ws, int K, int N, float* Y, int ldy, int acc) {
+    const int nb = (N + kGemmTN - 1) / kGemmTN;
+    if ((long long)nb * ((T + 31) / 32) < h->num_sms)
+      bd_gemm_q8<2><<<dim3(nb, (T + 15) / 16), 128, 0, st>>>(h->xq, h->xs, T, K, W, ws, N, Y,
+                                                            ldy, acc);
+    else
+      bd_gemm_q8<4><<<dim3(nb, (T + 31) / 32), 128, 0, st>>>(h->xq, h->xs, T, K, W, ws, N, Y,
+                                                            ldy, acc);
+  };
   const int max_seq = h->cfg.max_seq;
   const size_t attn_smem = attn_tile_smem(max_seq, h->attn_cap);
   const dim3 g_att((unsigned)((T + kAttnTile - 1) / kAttnTile), (unsigned)nkv);
@@ -629,20 +641,18 @@ int enqueue_body(lora_body_handle* h, const int32_t* d_tok, int T, void* out, in
     const auto& ly = h->layers[L];
     bd_norm<<<norm_blocks, 32 * kNormWarps, norm_smem, st>>>(h->x, ly.attn_norm, T, d, h->cfg.rms_eps, h->xn, h->xq,
                                          h->xs, nullptr, 0);
-    bd_gemm_q8<<<g_qkv, 128, 0, st>>>(h->xq, h->xs, T, d, ly.wqkv, ly.sqkv, h->nqkv, h->qkv,
-                                      h->nqkv, 0);
+    gemm(ly.wqkv, ly.sqkv, d, h->nqkv, h->qkv, h->nqkv, 0);
     bd_rope<<<rope_blocks, 256, 0, st>>>(h->qkv, T, h->nqkv, nh + nkv, h->pos, h->rope_cos,
                                          h->rope_sin);
     bd_attn_tile<<<g_att, 32 * kAttnTWarps, attn_smem, st>>>(
         h->qkv, T, h->nqkv, nh, nkv, d, h->pos, ly.window, h->att, max_seq, h->attn_cap);
     bd_quant_act<<<rows_blocks, 256, 0, st>>>(h->att, T, d, h->xq, h->xs);
-    bd_gemm_q8<<<g_d, 128, 0, st>>>(h->xq, h->xs, T, d, ly.wo, ly.so, d, h->x, d, 1);
+    gemm(ly.wo, ly.so, d, d, h->x, d, 1);
     bd_norm<<<norm_blocks, 32 * kNormWarps, norm_smem, st>>>(h->x, ly.ffn_norm, T, d, h->cfg.rms_eps, h->xn, h->xq,
                                          h->xs, nullptr, 0);
-    bd_gemm_q8<<<g_gu, 128, 0, st>>>(h->xq, h->xs, T, d, ly.wgu, ly.sgu, 2 * ffn, h->gu,
-                                     2 * ffn, 0);
+    gemm(ly.wgu, ly.sgu, d, 2 * ffn, h->gu, 2 * ffn, 0);
     bd_act_quant<<<T, 256, 0, st>>>(h->gu, T, ffn, h->xn, h->xq, h->xs);
-    bd_gemm_q8<<<g_d, 128, 0, st>>>(h->xq, h->xs, T, ffn, ly.wd, ly.sd, d, h->x, d, 1);
+    gemm(ly.wd, ly.sd, ffn, d, h->x, d, 1);
   }
   bd_norm<<<norm_blocks, 32 * kNormWarps, norm_smem, st>>>(h->x, h->out_norm, T, d, h->cfg.rms_eps, h->xn, nullptr,
                                        nullptr, out, out_dtype);
@@ -733,6 +743,11 @@ int lora_body_create(const lora_body_config* c, lora_body_handle** out) {
   h->nqkv = h->d + 2 * h->kvdim;
   h->Tcap = c->max_tokens;
   h->layers.resize(c->n_layers);
+  if (cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, c->device) !=
+      cudaSuccess) {
+    delete h;
+    return bfail(LORA_CE_ECUDA, "cudaDeviceGetAttribute failed");
+  }
   {
     const char* e = getenv("LORA_BODY_GRAPHS");  // "0": launch the kernels directly
     h->use_graph = !(e && e[0] == '0');
