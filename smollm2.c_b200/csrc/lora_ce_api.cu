@@ -1232,6 +1232,17 @@ int create_wide(lora_ce_handle* h) {
   h->wide_p = (int)std::max<long long>(kWTile, std::min<long long>(rows, Tcap));
   const long long P = h->wide_p;
   const long long nparam = (long long)d * R + Vpad * R;
+  // dU split partials: the most (K splits x block positions) any block can
+  // use, over block sizes 1..P (the splits depend on its 128-row tiles)
+  long long dup = 0;
+  {
+    const long long rt = (R + kWTile - 1) / kWTile;
+    for (long long mt = 1; (mt - 1) * kWTile < P; ++mt) {
+      int splits = 1, k_split = 0;
+      wide_splits(V, mt * rt, h->num_sms, &splits, &k_split);
+      dup = std::max(dup, (long long)splits * std::min(P, mt * kWTile));
+    }
+  }
   int rc = 0;
   if (!rc) rc = dalloc(&h->W, (size_t)V * d);
   if (!rc) rc = dalloc(&h->h16, (size_t)Tcap * d);
@@ -1251,7 +1262,7 @@ int create_wide(lora_ce_handle* h) {
   if (!rc) rc = dalloc(&h->w_Z, (size_t)P * Vpad);
   if (!rc) rc = dalloc(&h->w_Bp, (size_t)R * Vpad);
   if (!rc) rc = dalloc(&h->w_dB, (size_t)R * Vpad);
-  if (!rc) rc = dalloc(&h->w_dUp, (size_t)kWMaxSplit * P * R);
+  if (!rc) rc = dalloc(&h->w_dUp, (size_t)dup * R);
   if (!rc) rc = dalloc(&h->w_dAp, (size_t)kWMaxSplit * d * R);
   if (!rc && (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess ||
               cudaStreamCreateWithFlags(&h->cstream, cudaStreamNonBlocking) != cudaSuccess))
