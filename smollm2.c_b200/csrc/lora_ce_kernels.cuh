@@ -1320,25 +1320,35 @@ __global__ void __launch_bounds__(32 * da_rows(R)) lce_dA_partial(int T, int d,
     sdU[k] = dU[(long long)(t0 + k / R) * rank_total + rank_off + k % R];
   __syncthreads();
   const int i = blockIdx.y * 64 + 2 * threadIdx.x;
-  float a0[R], a1[R];
+  // a0 / a1: columns i / i+1, ranks in pairs (j, j+1) per f32x2 fma, whose
+  // lanes are the same fmas in the same position order as scalar ones
+  static_assert(R % 4 == 0, "ranks in float4 groups");
+  float2 a0[R / 2], a1[R / 2];
 #pragma unroll
-  for (int j = 0; j < R; ++j) a0[j] = a1[j] = 0.f;
+  for (int j = 0; j < R / 2; ++j) a0[j] = a1[j] = make_float2(0.f, 0.f);
   if (i < d) {
     const __half* hp = h16 + (long long)t0 * d + i;
 #pragma unroll 4
     for (int tt = threadIdx.y; tt < nt; tt += Y) {
       const float2 hv = __half22float2(*reinterpret_cast<const __half2*>(hp + (long long)tt * d));
+      const float2 hx = make_float2(hv.x, hv.x), hy = make_float2(hv.y, hv.y);
 #pragma unroll
-      for (int j = 0; j < R; ++j) {
-        a0[j] = fmaf(hv.x, sdU[tt * R + j], a0[j]);
-        a1[j] = fmaf(hv.y, sdU[tt * R + j], a1[j]);
+      for (int j = 0; j < R; j += 4) {
+        const float4 u = *reinterpret_cast<const float4*>(&sdU[tt * R + j]);
+        const float2 u01 = make_float2(u.x, u.y), u23 = make_float2(u.z, u.w);
+        a0[j / 2] = __ffma2_rn(hx, u01, a0[j / 2]);
+        a0[j / 2 + 1] = __ffma2_rn(hx, u23, a0[j / 2 + 1]);
+        a1[j / 2] = __ffma2_rn(hy, u01, a1[j / 2]);
+        a1[j / 2 + 1] = __ffma2_rn(hy, u23, a1[j / 2 + 1]);
       }
     }
   }
 #pragma unroll
-  for (int j = 0; j < R; ++j) {
-    sred[threadIdx.y][(2 * threadIdx.x) * R + j] = a0[j];
-    sred[threadIdx.y][(2 * threadIdx.x + 1) * R + j] = a1[j];
+  for (int j = 0; j < R / 2; ++j) {
+    sred[threadIdx.y][(2 * threadIdx.x) * R + 2 * j] = a0[j].x;
+    sred[threadIdx.y][(2 * threadIdx.x) * R + 2 * j + 1] = a0[j].y;
+    sred[threadIdx.y][(2 * threadIdx.x + 1) * R + 2 * j] = a1[j].x;
+    sred[threadIdx.y][(2 * threadIdx.x + 1) * R + 2 * j + 1] = a1[j].y;
   }
   __syncthreads();
   for (int k = tid; k < 64 * R; k += NT) {
