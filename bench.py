@@ -24,7 +24,8 @@ scaling), with its per-rank all-reduce and pass times.
 Other modes: --config 3/4/5 (the rank-16, Q4_K and rank-64 workloads as the
 main line), --tokens T (positions per rank), --op merge / q4k (the merge and
 dequantisation kernels), --kernel-run (only the device steps, the command
-to capture under ncu), --impl reference (the reference's CPU path).
+to capture under ncu; --rank R runs them at another adapter rank, e.g. 128
+for the wide-rank path), --impl reference (the reference's CPU path).
 """
 from __future__ import annotations
 
@@ -926,12 +927,14 @@ def kernel_run(args):
     import lora_ce
 
     torch.cuda.set_device(0)
+    if args.rank:
+        CONFIGS[args.config] = dict(CONFIGS[args.config], rank=args.rank, alpha=2 * args.rank)
     m, h, tgt, dH, dT, T = make_handle(args.config, 1, 0, 0, args.tokens)
     for _ in range(args.warmup + args.steps):
         m.step_device(dH.data_ptr(), lora_ce.BF16, T, dT.data_ptr(), 0)
     m.sync()
     m.close()
-    print(f"kernel run ok: config {args.config}, rank {CONFIG['rank']}, T {T}, "
+    print(f"kernel run ok: config {args.config}, rank {CONFIGS[args.config]['rank']}, T {T}, "
           f"{args.warmup + args.steps} steps", flush=True)
 
 
@@ -955,6 +958,9 @@ def main():
                     help="leave out the rank-16 strong-scaling object of the default line")
     ap.add_argument("--kernel-run", action="store_true",
                     help="run only the device steps (the command for an ncu capture)")
+    ap.add_argument("--rank", type=int, default=None,
+                    help="with --kernel-run: this adapter rank (alpha 2 x rank) instead of the "
+                         "workload's, e.g. 128 for the wide-rank path")
     ap.add_argument("--merge-rank", type=int, default=R)
     args = ap.parse_args()
     if args.config == 1:
